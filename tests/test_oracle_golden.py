@@ -1,0 +1,156 @@
+"""Pins the CPU oracle against golden vectors and known answers (CPU only).
+
+* ggml Q8_0 / Q4_0 block quantisers vs gguf-py 0.19.0 fixtures (bit-exact).
+* The reference's W4A16 probe: regenerated inputs match the reference
+  generator's files by SHA-256, and the oracle reproduces its f16 golden
+  output bit for bit.
+* The reference A8W8 chain known answer (custom_a8w8_chain_probe.cpp:189):
+  xq[0] == 127 and |out[0] - sum_k W[k, 0]| <= 8, for both probe shapes.
+* FLASH_ATTN_EXT oracle modes agree; kv_lengths derivation follows
+  llama-graph.cpp set_input_kv_lengths_impl (patch P:2900-2916).
+"""
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+import probe_data as PD
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.mark.parametrize("name", ["q8_0", "q4_0"])
+def test_block_quantiser_matches_gguf(name):
+    f = np.load(os.path.join(GOLD, f"gguf_{name}.npz"))
+    x, blocks, deq = f["x"], f["blocks"], f["dequant"]
+    mine = O.quantize_q8_0(x) if name == "q8_0" else O.quantize_q4_0(x)
+    assert mine.dtype == np.uint8
+    np.testing.assert_array_equal(mine.reshape(-1), blocks)
+    back = O.dequantize_q8_0(blocks) if name == "q8_0" else O.dequantize_q4_0(blocks)
+    np.testing.assert_array_equal(back.reshape(-1), deq)
+
+
+def test_f16_conversion_exhaustive():
+    lib = O.lib()
+    h = np.arange(65536, dtype=np.uint16)
+    f = h.view(np.float16).astype(np.float32)
+    finite = np.isfinite(f)
+    # f16 -> f32 -> f16 round trip and f32 -> f16 against numpy for every finite half
+    for i in np.nonzero(finite)[0][::37]:
+        assert lib.ref_f32_to_f16(float(f[i])) == h[i] or (f[i] == 0.0)
+    rng = np.random.default_rng(1)
+    vals = np.concatenate([rng.standard_normal(20000).astype(np.float32) * s for s in (1e-7, 1e-3, 1.0, 3e4)])
+    vals = np.concatenate([vals, np.array([65504.0, 65519.0, 65520.0, 2.0 ** -25, 2.0 ** -24, 6.1e-5], np.float32)])
+    mine = np.array([lib.ref_f32_to_f16(float(v)) for v in vals], dtype=np.uint16)
+    np.testing.assert_array_equal(mine, vals.astype(np.float16).view(np.uint16))
+
+
+def test_w4a16_probe_golden_bit_exact():
+    f = np.load(os.path.join(GOLD, "w4a16_probe_golden.npz"))
+    x, q, scales = PD.w4a16_probe_inputs()
+    packed, sl = PD.w4a16_probe_pack(q, scales)
+    xrep = np.repeat(x[:, None], PD.W4_TILE, axis=1)
+    assert hashlib.sha256(packed.tobytes()).hexdigest() == str(f["sha_weight"])
+    assert hashlib.sha256(sl.tobytes()).hexdigest() == str(f["sha_scales"])
+    assert hashlib.sha256(np.ascontiguousarray(xrep).tobytes()).hexdigest() == str(f["sha_x"])
+    y = O.w4a16_probe(x, packed, sl, PD.W4_K, PD.W4_N, PD.W4_TILE)
+    np.testing.assert_array_equal(y.view(np.uint16), f["golden"].view(np.uint16))
+
+
+def test_w4a16_probe_as_q4_0_within_reference_tolerance():
+    """The probe's weights re-expressed as Q4_0 blocks, through the oracle's
+    true-W4A16 mode, meet the reference verifier's rtol = atol = 2e-2
+    (verify_result.py:15)."""
+    f = np.load(os.path.join(GOLD, "w4a16_probe_golden.npz"))
+    x, q, scales = PD.w4a16_probe_inputs()
+    blocks = PD.w4a16_as_q4_0_blocks(q, scales)
+    y = O.mul_mat_q4_0(blocks, x.astype(np.float32), mode=1)
+    g = f["golden"].astype(np.float32)
+    assert np.allclose(y, g, rtol=2e-2, atol=2e-2)
+    cos = float(np.dot(y, g) / (np.linalg.norm(y) * np.linalg.norm(g)))
+    assert cos > 0.9999
+
+
+@pytest.mark.parametrize("k,n", [(1536, 8960), (8960, 1536)])
+def test_a8w8_chain_known_answer(k, n):
+    x, w, w_nz, expected_first = PD.a8w8_chain_inputs(k, n)
+    xq, xs = O.a8w8_quantize_token(x)
+    assert int(xq[0]) == 127
+    acc = O.a8w8_matmul_i32(xq, w_nz, k, n)
+    np.testing.assert_array_equal(acc, 127 * w.astype(np.int64).sum(axis=0))
+    out = O.a8w8_dequant(acc, xs, np.ones(n, np.float16))
+    assert abs(float(out[0]) - expected_first) <= 8.0
+
+
+def test_a8w8_transform_roundtrip():
+    rng = np.random.default_rng(3)
+    n, k = 64, 96
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float16)
+    q_nz, s = O.a8w8_transform_weight(w)
+    kk = np.arange(k)[None, :]
+    nn = np.arange(n)[:, None]
+    q = q_nz[O.a8w8_nz_index(kk, nn, k)]
+    back = q.astype(np.float32) * s.astype(np.float32)[:, None]
+    err = np.abs(back - w.astype(np.float32)).max(axis=1)
+    # half a quantisation step, plus 127 x the f16 rounding of the stored scale
+    assert np.all(err <= s.astype(np.float32) * (0.5 + 127 * 2.0 ** -11) + 1e-7)
+
+
+def test_kv_lengths_from_mask():
+    m = np.zeros((3, 10), np.float16)
+    m[0, 7:] = -np.inf
+    m[1, :] = -np.inf
+    np.testing.assert_array_equal(O.kv_lengths_from_mask(m), [7, 1, 10])
+
+
+def test_flash_attn_modes_agree():
+    rng = np.random.default_rng(11)
+    hq, hkv, d, n_kv = 12, 2, 128, 700
+    q = rng.standard_normal((hq, d)).astype(np.float32)
+    k = rng.standard_normal((n_kv, hkv, d)).astype(np.float16)
+    v = rng.standard_normal((n_kv, hkv, d)).astype(np.float16)
+    mask = np.zeros(n_kv, np.float16)
+    mask[650:] = -np.inf
+    o0 = O.flash_attn_decode(q, k, v, mask, mode=0)
+    # numpy truth
+    g = hq // hkv
+    qh = q.astype(np.float16).astype(np.float64)
+    ref = np.empty_like(o0)
+    for h in range(hq):
+        s = (k[:650, h // g].astype(np.float64) @ qh[h]) / np.sqrt(d)
+        p = np.exp(s - s.max())
+        ref[h] = (p @ v[:650, h // g].astype(np.float64)) / p.sum()
+    np.testing.assert_allclose(o0, ref, rtol=0, atol=1e-6)
+    o1 = O.flash_attn_decode(q, k, v, mask, mode=1)
+    o2 = O.flash_attn_decode(q, k, v, mask, mode=2)
+    scale = np.abs(o0).max()
+    # ggml-cpu keeps the F16-V accumulator in f16: ~6e-3 of max|out| from the
+    # fp64 truth at 650 positions, so the 1e-3 parity bar is taken against the
+    # fp32-accumulating oracle (mode 0), not against this mode.
+    assert np.abs(o1 - o0).max() / scale < 2e-2
+    assert np.abs(o2 - o0).max() / scale < 2e-3
+    # kv_len truncation equals masking the tail
+    o3 = O.flash_attn_decode(q, k, v, None, kv_len=650, mode=0)
+    np.testing.assert_allclose(o3, o0, rtol=0, atol=1e-6)
+
+
+def test_mul_mat_oracles_vs_numpy():
+    rng = np.random.default_rng(5)
+    n, k = 96, 512
+    x = rng.standard_normal(k).astype(np.float32)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    wh = w.astype(np.float16)
+    y = O.mul_mat_f16(wh, x)
+    ref = wh.astype(np.float64) @ x.astype(np.float16).astype(np.float64)
+    np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-6)
+    for fmt in ("q4_0", "q8_0"):
+        b = O.quantize_q4_0(w) if fmt == "q4_0" else O.quantize_q8_0(w)
+        wd = O.dequantize_q4_0(b) if fmt == "q4_0" else O.dequantize_q8_0(b)
+        xd = O.dequantize_q8_0(O.quantize_q8_0(x))
+        y = O.mul_mat_q4_0(b, x, mode=0) if fmt == "q4_0" else O.mul_mat_q8_0(b, x)
+        ref = wd.astype(np.float64) @ xd.astype(np.float64)
+        np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-6)
+        dots = O.block_dots(fmt, b, x)
+        assert dots.shape == (n, k // 32)
