@@ -1,0 +1,131 @@
+/*
+ * b200_decode.h -- C ABI of the B200 (sm_100a) single-token decode hot path.
+ *
+ * Plain C: device pointers, element counts, byte strides, a CUDA stream, and
+ * an int status (0 = ok, negative = B200_E*).  No ggml or torch types.  Every
+ * kernel entry point is asynchronous on the given stream; "device pointer"
+ * means memory of the device that is current on the calling thread.
+ *
+ * Each entry point names the reference interface it replaces.  References
+ * use the path inside the reference project; "patch:N" is line N of
+ * patches/ascend310b4-llama-cpp.patch, a diff against llama.cpp 37b3a9e0.
+ */
+#ifndef B200_DECODE_H
+#define B200_DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; NULL means the legacy default stream. */
+typedef struct CUstream_st *b200_stream_t;
+
+/* Status codes. */
+#define B200_OK 0
+#define B200_EINVAL (-1)       /* bad pointer, shape or stride */
+#define B200_ECUDA (-2)        /* a CUDA runtime call failed */
+#define B200_EUNSUPPORTED (-3) /* valid ggml op variant that this backend does not implement */
+#define B200_ENOMEM (-4)
+#define B200_ENCCL (-5)
+#define B200_ESTATE (-6)       /* call out of order (not initialised, wrong phase) */
+
+/* Bits of the device status word (b200_device_status). */
+#define B200_DEVSTATUS_TIMEOUT 1u /* a bounded device-side wait expired */
+#define B200_DEVSTATUS_BOUNDS 2u  /* a device-side range check failed; the access was skipped */
+
+/* Weight type ids: the values of ggml's enum ggml_type. */
+#define B200_TYPE_F32 0
+#define B200_TYPE_F16 1
+#define B200_TYPE_Q4_0 2
+#define B200_TYPE_Q8_0 8
+
+/* Q4_0 GEMV arithmetic. */
+#define B200_Q4_MODE_GGML 0  /* ggml-cpu semantics: x -> Q8_0 blocks, integer block dots */
+#define B200_Q4_MODE_W4A16 1 /* x -> f16, fp32 multiply-accumulate of dequantised weights */
+
+const char *b200_version(void);
+const char *b200_strerror(int code);
+
+/* Reads (and optionally clears) the status word of the current device.
+ * Synchronises the device. */
+int b200_device_status(unsigned int *status, int reset);
+
+/* ------------------------------------------------------------------------
+ * Weight pre-layout.  Replaces the FRACTAL_NZ dual layout of the reference
+ * (ggml_cann_310b_nz_offset/size patch:1551-1562, set_tensor NZ branch
+ * patch:1768-1806, get_alloc_size patch:1810-1846, aclnnTransMatmulWeight).
+ *
+ * The packed layout is a sequence of tiles of R rows x the full K.  A tile is
+ * contiguous and a multiple of 16 bytes so the GEMV streams it with one bulk
+ * copy.  Inside a tile:
+ *   F16 : w[R][K] halves (identical to ggml rows; only the last tile is padded)
+ *   Q4_0: qs[R][K/32][16 bytes] then d[R][K/32] f16
+ *   Q8_0: qs[R][K/32][bytes 0..15], qs[R][K/32][bytes 16..31], d[R][K/32] f16
+ * Rows past n in the last tile are zero.
+ * ---------------------------------------------------------------------- */
+int64_t b200_packed_rows_per_tile(int type, int64_t n, int64_t k);
+size_t b200_packed_size(int type, int64_t n, int64_t k); /* 0 when unsupported */
+/* src: ggml rows (n rows of k elements, row stride = ggml_row_size) on the device. */
+int b200_repack(int type, const void *src, void *dst, int64_t n, int64_t k, b200_stream_t stream);
+/* Packs 2*n_each rows: packed row 2i is src_even row i, 2i+1 is src_odd row i
+ * (gate/up pairs for the fused SwiGLU GEMV). */
+int b200_repack_interleave2(int type, const void *src_even, const void *src_odd, void *dst, int64_t n_each,
+                            int64_t k, b200_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * MUL_MAT at M = 1 (ggml mul_mat(W[K,N], x[K,1]) -> y f32 [N]).
+ * Replaces ggml_cann_mat_mul_fp (patch:1188-1355): the F16 NZ decode branch
+ * (cast, aclnnMatmul, cast: patch:1286-1313) and the A8W8 chain (cast,
+ * W8a8QuantizeCustom, MatmulW8a8I32Custom, W8a8DequantCustom, cast:
+ * patch:1223-1282) -- here one kernel launch each.
+ * w_packed is b200_repack output; x f32 [k]; y f32 [n]. */
+int b200_gemv_f16(const void *w_packed, const float *x, float *y, int64_t n, int64_t k, b200_stream_t stream);
+int b200_gemv_q4_0(const void *w_packed, const float *x, float *y, int64_t n, int64_t k, int mode,
+                   b200_stream_t stream);
+int b200_gemv_q8_0_q8_0(const void *w_packed, const float *x, float *y, int64_t n, int64_t k,
+                        b200_stream_t stream);
+
+/* Exactness exports.  b200_quantize_q8_0 runs the activation quantiser that
+ * the Q4_0/Q8_0 GEMVs fuse (replaces W8a8QuantizeCustom,
+ * w8a8_quantize_custom_vector.cpp:97-106, with ggml's per-32 Q8_0 rule) and
+ * writes ggml block_q8_0 bytes (k/32 * 34).  b200_gemv_block_dots runs the
+ * GEMV kernel itself in its export mode: it writes the int32 dot of every
+ * (row, 32-block) to dots[n][k/32] and, when xq_blocks != NULL, the Q8_0
+ * blocks its prologue quantised x into (k/32 * 34 bytes). */
+int b200_quantize_q8_0(const float *x, void *blocks, int64_t k, b200_stream_t stream);
+int b200_gemv_block_dots(int type, const void *w_packed, const float *x, int32_t *dots, void *xq_blocks, int64_t n,
+                         int64_t k, b200_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * FLASH_ATTN_EXT, one query token (GQA, online softmax, split-KV).
+ * Replaces ggml_cann_flash_attn_ext's custom branch (patch:1370-1432) and
+ * aclnnAttentionStepCustom (attention_step_custom.cpp:599-622).
+ *   q    f32 [n_head][head_dim] (ggml q [D,1,Hq,1], contiguous)
+ *   k, v f16; element (t, h, d) at byte t*nb1 + h*nb2 + 2*d (ggml view
+ *        [D, n_kv, Hkv] with nb1 = Hkv*D*2 for the llama cache)
+ *   mask f16 [n_kv] additive (may be NULL); kv_len int32 [1] (may be NULL):
+ *        only the first kv_len[0] positions are read when 0 < kv_len[0] < n_kv
+ *        (attention_step_custom.cpp:110-113; src[5] of patch:2009-2023)
+ *   out  f32 [n_head][head_dim]
+ * s = scale * (f16(q) . k) + mask; positions whose mask is -inf are skipped.
+ * The workspace (b200_fa_workspace_size bytes) must be zero-filled before its
+ * first use; every call leaves its counters zero again.  Calls that share a
+ * workspace must not overlap on the GPU. */
+size_t b200_fa_workspace_size(int head_dim, int n_head, int n_head_kv, int n_kv);
+int b200_fa_decode(const float *q, const void *k, const void *v, const void *mask, const int32_t *kv_len,
+                   float *out, int head_dim, int n_head, int n_head_kv, int n_kv, int64_t k_nb1, int64_t k_nb2,
+                   int64_t v_nb1, int64_t v_nb2, float scale, void *workspace, size_t workspace_size,
+                   b200_stream_t stream);
+
+/* Host helper mirroring llama-graph.cpp set_input_kv_lengths_impl
+ * (patch:2900-2916): out[r] = 1 + index of the last finite entry of mask row
+ * r (at least 1).  mask f16 host array [n_rows][n_kv]. */
+int b200_kv_lengths_from_mask_f16(const uint16_t *mask, int64_t n_kv, int64_t n_rows, int32_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200_DECODE_H */

@@ -1,0 +1,105 @@
+/*
+ * b200_model.h -- C ABI of the native whole-model batch-1 decode driver
+ * (Llama architecture, Q4_0 weights, fp16 KV cache, tensor parallel over the
+ * GPUs of one node with NCCL).
+ *
+ * This is the B200 counterpart of running llama.cpp's decode graph with the
+ * reference add-on's CANN backend: one token per call through
+ * ggml_backend_sched -> graph_compute (patch:1884-1923) with the MUL_MAT,
+ * FLASH_ATTN_EXT and neighbour ops of every layer.  Here the whole step is a
+ * single captured CUDA graph of fused kernels: per layer RMSNorm+Q8_0+QKV
+ * GEMV+RoPE+KV write, split-KV attention, O GEMV+residual, RMSNorm+gate/up
+ * GEMV+SwiGLU, down GEMV+residual; then the lm_head GEMV with argmax.
+ * Tensor parallelism shards Q/K/V/gate/up by output rows (whole KV heads),
+ * O/down by input columns, and the lm_head by vocabulary rows; NCCL
+ * all-reduces follow O and down, and an all-reduce(max) picks the argmax.
+ */
+#ifndef B200_MODEL_H
+#define B200_MODEL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "b200_decode.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct b200_model b200_model;
+
+typedef struct {
+    int n_layer;
+    int d_model;
+    int n_head;
+    int n_head_kv;
+    int head_dim;
+    int d_ff;
+    int vocab;
+    int kv_size; /* KV cache rows (maximum context) */
+    float rope_theta;
+    float rms_eps;
+} b200_llama_config;
+
+/* Weight ids for b200_model_export_weight. */
+#define B200_W_TOK_EMBD 0
+#define B200_W_Q 1
+#define B200_W_K 2
+#define B200_W_V 3
+#define B200_W_O 4
+#define B200_W_GATE 5
+#define B200_W_UP 6
+#define B200_W_DOWN 7
+#define B200_W_LM_HEAD 8
+
+/* 128-byte NCCL unique id, made on one rank and shared with the others. */
+int b200_nccl_unique_id(void *out128);
+
+/* Creates the model on `device` (made current).  tp_world == 1 needs no id. */
+int b200_model_create(const b200_llama_config *cfg, int device, int tp_rank, int tp_world, const void *nccl_id128,
+                      b200_model **out);
+void b200_model_destroy(b200_model *m);
+
+/* Random-init weights: every Q4_0 matrix from N(0, sigma^2) samples quantised
+ * with ggml's Q4_0 rule, norms = 1.  A rank generates exactly the rows or
+ * columns of its shard of the unsharded tensors. */
+int b200_model_init_synthetic(b200_model *m, uint64_t seed, float sigma);
+/* KV cache rows [0, n_pos) of every layer ~ N(0, 1) in f16. */
+int b200_model_fill_kv_synthetic(b200_model *m, uint64_t seed, int n_pos);
+
+/* This rank's shard of a weight in ggml layout (Q4_0 blocks), regenerated on
+ * the device and copied to host memory of `bytes` (query with host == NULL). */
+int b200_model_export_weight(b200_model *m, int layer, int which, void *host, size_t *bytes);
+
+/* This rank's KV cache rows [0, n_pos) of one layer (which: 0 = K, 1 = V) as
+ * f16 [n_pos][n_head_kv_local * head_dim], copied to host memory. */
+int b200_model_export_kv(b200_model *m, int layer, int which, int n_pos, void *host);
+
+/* Captures one decode step into a CUDA graph (call once, after init). */
+int b200_model_capture(b200_model *m);
+
+/* Sets the device step state (async on the model stream): the next step
+ * decodes `token` at `pos`; when advance != 0 each step feeds its argmax back
+ * as the next token and increments pos. */
+int b200_model_set_state(b200_model *m, int token, int pos, int advance);
+/* One captured step, asynchronous on the model stream. */
+int b200_model_launch(b200_model *m);
+/* End to end: host token in, host next token out (and the local logits shard
+ * when logits_host != NULL).  Copies in and out are inside the call. */
+int b200_model_decode(b200_model *m, int token, int pos, int *next_token, float *logits_host);
+/* Copies the logits of the last step: this rank's rows [offset, offset+count). */
+int b200_model_logits(b200_model *m, float *host, int64_t *offset, int64_t *count);
+b200_stream_t b200_model_stream(b200_model *m);
+/* Algorithmic HBM bytes one decode step reads on this rank at context ctx. */
+int b200_model_step_bytes(b200_model *m, int ctx, uint64_t *bytes);
+/* Runs `iters` eager (not captured) steps with CUDA events around every
+ * kernel and returns the mean duration in microseconds per kernel class:
+ * [0] embed, [1] QKV GEMV, [2] attention, [3] O GEMV, [4] gate/up GEMV,
+ * [5] down GEMV, [6] lm_head GEMV, [7] all-reduces (0 at tp_world 1).
+ * Leaves the step state where the last step put it. */
+int b200_model_profile(b200_model *m, int iters, float *us_per_class8);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200_MODEL_H */

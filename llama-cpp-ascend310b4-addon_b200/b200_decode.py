@@ -1,0 +1,264 @@
+"""Python host-side binding of libb200_decode.so (ctypes over the C ABI).
+
+The functions mirror the ggml ops this backend serves, with ggml's argument
+meaning: ``mul_mat(w, x)`` is ggml_mul_mat(src0=W[K, N], src1=x[K, 1]) -> f32
+[N], and ``flash_attn_ext(q, k, v, mask, scale, ...)`` is
+ggml_flash_attn_ext for one query token with the reference add-on's optional
+``kv_lengths`` source (ggml_flash_attn_ext_add_kv_lengths, patch:2009-2023).
+Contract violations raise ``B200Error`` (the reference aborts through
+GGML_ASSERT); unsupported variants raise ``B200Unsupported`` so a caller can
+route them elsewhere, as ggml's scheduler does when supports_op is false.
+
+Tensors are torch CUDA tensors; torch is used only to hold device memory and
+to name the current stream.  There is no CPU fallback: when the shared
+library is missing this module raises on import of the library.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libb200_decode.so")
+
+TYPE_F32 = 0
+TYPE_F16 = 1
+TYPE_Q4_0 = 2
+TYPE_Q8_0 = 8
+Q4_MODE_GGML = 0
+Q4_MODE_W4A16 = 1
+
+BLOCK_BYTES = {TYPE_Q4_0: 18, TYPE_Q8_0: 34}
+
+OK = 0
+EINVAL = -1
+ECUDA = -2
+EUNSUPPORTED = -3
+
+_lib = None
+
+
+class B200Error(RuntimeError):
+    def __init__(self, code: int, what: str):
+        self.code = code
+        super().__init__(f"{what}: {lib().b200_strerror(code).decode()} ({code})")
+
+
+class B200Unsupported(B200Error):
+    pass
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing; build it with `python {os.path.join(HERE, 'build.py')}` "
+                "(there is no fallback path)"
+            )
+        _lib = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
+        _declare(_lib)
+    return _lib
+
+
+P = C.c_void_p
+I64 = C.c_int64
+
+
+def _declare(L):
+    sig = {
+        "b200_version": (C.c_char_p, []),
+        "b200_strerror": (C.c_char_p, [C.c_int]),
+        "b200_device_status": (C.c_int, [C.POINTER(C.c_uint), C.c_int]),
+        "b200_packed_rows_per_tile": (I64, [C.c_int, I64, I64]),
+        "b200_packed_size": (C.c_size_t, [C.c_int, I64, I64]),
+        "b200_repack": (C.c_int, [C.c_int, P, P, I64, I64, P]),
+        "b200_repack_interleave2": (C.c_int, [C.c_int, P, P, P, I64, I64, P]),
+        "b200_gemv_f16": (C.c_int, [P, P, P, I64, I64, P]),
+        "b200_gemv_q4_0": (C.c_int, [P, P, P, I64, I64, C.c_int, P]),
+        "b200_gemv_q8_0_q8_0": (C.c_int, [P, P, P, I64, I64, P]),
+        "b200_quantize_q8_0": (C.c_int, [P, P, I64, P]),
+        "b200_gemv_block_dots": (C.c_int, [C.c_int, P, P, P, P, I64, I64, P]),
+        "b200_fa_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
+        "b200_fa_decode": (
+            C.c_int,
+            [P, P, P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, I64, I64, I64, I64, C.c_float, P, C.c_size_t, P],
+        ),
+        "b200_kv_lengths_from_mask_f16": (C.c_int, [P, I64, I64, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def _check(rc: int, what: str):
+    if rc == EUNSUPPORTED:
+        raise B200Unsupported(rc, what)
+    if rc != OK:
+        raise B200Error(rc, what)
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _stream(device=None):
+    torch = _torch()
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def device_status(reset: bool = True) -> int:
+    v = C.c_uint(0)
+    _check(lib().b200_device_status(C.byref(v), 1 if reset else 0), "b200_device_status")
+    return int(v.value)
+
+
+# ----------------------------------------------------------- packed weights
+
+def packed_size(wtype: int, n: int, k: int) -> int:
+    return int(lib().b200_packed_size(wtype, n, k))
+
+
+def rows_per_tile(wtype: int, n: int, k: int) -> int:
+    return int(lib().b200_packed_rows_per_tile(wtype, n, k))
+
+
+class PackedWeight:
+    """A weight in the tile-interleaved layout on the device."""
+
+    def __init__(self, wtype: int, n: int, k: int, data):
+        self.wtype, self.n, self.k, self.data = wtype, n, k, data
+
+
+def repack(wtype: int, src, n: int, k: int) -> PackedWeight:
+    """src: device tensor holding ggml rows (F16 [n, k] or Q4_0/Q8_0 block bytes)."""
+    torch = _torch()
+    size = packed_size(wtype, n, k)
+    if size == 0:
+        raise B200Unsupported(EUNSUPPORTED, f"repack type={wtype} n={n} k={k}")
+    dst = torch.empty(size, dtype=torch.uint8, device=src.device)
+    _check(lib().b200_repack(wtype, _ptr(src), _ptr(dst), n, k, _stream(src.device)), "b200_repack")
+    return PackedWeight(wtype, n, k, dst)
+
+
+def repack_interleave2(wtype: int, src_even, src_odd, n_each: int, k: int) -> PackedWeight:
+    torch = _torch()
+    size = packed_size(wtype, 2 * n_each, k)
+    dst = torch.empty(size, dtype=torch.uint8, device=src_even.device)
+    _check(
+        lib().b200_repack_interleave2(wtype, _ptr(src_even), _ptr(src_odd), _ptr(dst), n_each, k,
+                                      _stream(src_even.device)),
+        "b200_repack_interleave2",
+    )
+    return PackedWeight(wtype, 2 * n_each, k, dst)
+
+
+# ------------------------------------------------------------------ mul_mat
+
+def mul_mat(w: PackedWeight, x, y=None, q4_mode: int = Q4_MODE_GGML):
+    """ggml_mul_mat(W, x) at M = 1: x f32 [K] -> y f32 [N]."""
+    torch = _torch()
+    assert x.dtype == torch.float32 and x.is_contiguous() and x.numel() == w.k
+    if y is None:
+        y = torch.empty(w.n, dtype=torch.float32, device=x.device)
+    s = _stream(x.device)
+    if w.wtype == TYPE_F16:
+        rc = lib().b200_gemv_f16(_ptr(w.data), _ptr(x), _ptr(y), w.n, w.k, s)
+    elif w.wtype == TYPE_Q4_0:
+        rc = lib().b200_gemv_q4_0(_ptr(w.data), _ptr(x), _ptr(y), w.n, w.k, q4_mode, s)
+    elif w.wtype == TYPE_Q8_0:
+        rc = lib().b200_gemv_q8_0_q8_0(_ptr(w.data), _ptr(x), _ptr(y), w.n, w.k, s)
+    else:
+        raise B200Unsupported(EUNSUPPORTED, f"mul_mat weight type {w.wtype}")
+    _check(rc, "mul_mat")
+    return y
+
+
+def quantize_q8_0(x):
+    torch = _torch()
+    k = x.numel()
+    out = torch.empty(k // 32 * 34, dtype=torch.uint8, device=x.device)
+    _check(lib().b200_quantize_q8_0(_ptr(x), _ptr(out), k, _stream(x.device)), "quantize_q8_0")
+    return out
+
+
+def block_dots(w: PackedWeight, x, with_activation: bool = False):
+    """Runs the GEMV kernel in its export mode: int32 dots [N, K/32] and,
+    optionally, the Q8_0 blocks its prologue produced from x."""
+    torch = _torch()
+    dots = torch.empty((w.n, w.k // 32), dtype=torch.int32, device=x.device)
+    xq = torch.empty(w.k // 32 * 34, dtype=torch.uint8, device=x.device) if with_activation else None
+    _check(lib().b200_gemv_block_dots(w.wtype, _ptr(w.data), _ptr(x), _ptr(dots), _ptr(xq), w.n, w.k,
+                                      _stream(x.device)), "block_dots")
+    return (dots, xq) if with_activation else dots
+
+
+# ------------------------------------------------------------ attention
+
+_ws_cache: dict = {}
+
+
+def fa_workspace(head_dim: int, n_head: int, n_head_kv: int, n_kv: int, device):
+    torch = _torch()
+    size = int(lib().b200_fa_workspace_size(head_dim, n_head, n_head_kv, n_kv))
+    if size == 0:
+        raise B200Error(EINVAL, "fa_workspace_size")
+    key = (str(device), size)
+    ws = _ws_cache.get(key)
+    if ws is None:
+        ws = torch.zeros(size, dtype=torch.uint8, device=device)
+        _ws_cache[key] = ws
+    return ws
+
+
+def flash_attn_ext(q, k, v, mask=None, scale: float = 1.0, max_bias: float = 0.0, logit_softcap: float = 0.0,
+                   kv_lengths=None, out=None, workspace=None):
+    """ggml_flash_attn_ext for one query token.
+
+    q f32 [Hq, D]; k, v f16 tensors viewed as [n_kv, Hkv, D] (any strides with
+    a contiguous last dim); mask f16 [n_kv] or None; kv_lengths int32 [>=1]
+    device tensor or None.  Returns f32 [Hq, D]."""
+    torch = _torch()
+    if max_bias != 0.0 or logit_softcap != 0.0:
+        raise B200Unsupported(EUNSUPPORTED, "flash_attn_ext with ALiBi or softcap")
+    hq, d = q.shape
+    n_kv, hkv, d2 = k.shape
+    if d2 != d or tuple(v.shape) != tuple(k.shape):
+        raise B200Error(EINVAL, "flash_attn_ext shapes")
+    if k.stride(2) != 1 or v.stride(2) != 1:
+        raise B200Error(EINVAL, "flash_attn_ext needs contiguous head dim")
+    q = q.contiguous()
+    if out is None:
+        out = torch.empty((hq, d), dtype=torch.float32, device=q.device)
+    if workspace is None:
+        workspace = fa_workspace(d, hq, hkv, n_kv, q.device)
+    es = k.element_size()
+    rc = lib().b200_fa_decode(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(mask), _ptr(kv_lengths), _ptr(out), d, hq, hkv, n_kv,
+        k.stride(0) * es, k.stride(1) * es, v.stride(0) * es, v.stride(1) * es, float(scale),
+        _ptr(workspace), workspace.numel(), _stream(q.device),
+    )
+    _check(rc, "flash_attn_ext")
+    return out
+
+
+def kv_lengths_from_mask(mask_f16: np.ndarray) -> np.ndarray:
+    m = np.ascontiguousarray(mask_f16, dtype=np.float16)
+    if m.ndim == 1:
+        m = m[None]
+    out = np.empty(m.shape[0], dtype=np.int32)
+    _check(
+        lib().b200_kv_lengths_from_mask_f16(m.ctypes.data_as(C.c_void_p), m.shape[1], m.shape[0],
+                                            out.ctypes.data_as(C.c_void_p)),
+        "kv_lengths_from_mask",
+    )
+    return out

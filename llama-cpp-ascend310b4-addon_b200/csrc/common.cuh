@@ -1,0 +1,123 @@
+// common.cuh -- shared device helpers for the sm_100a decode kernels.
+//
+// Bulk-async copies (cp.async.bulk, no multicast) into shared memory signalled
+// through mbarriers, bounded waits that report a status word instead of
+// hanging, f16 helpers and warp reductions.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/b200_decode.h"
+
+namespace b200 {
+
+// Device status word: kernels OR a B200_DEVSTATUS_* bit in when a bounded wait
+// expires or a runtime bound check fails.  Read with b200_device_status().
+__device__ unsigned int g_status;
+
+constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the mbarrier phase with the given parity.  Gives up after
+// kWaitTimeoutNs, records B200_DEVSTATUS_TIMEOUT and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0 && globaltimer() - t0 > kWaitTimeoutNs) {
+            atomicOr(&g_status, (unsigned int)B200_DEVSTATUS_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+// Global -> shared bulk copy; completion is counted on `bar` (transaction
+// bytes).  dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void record_status(unsigned int bit) { atomicOr(&g_status, bit); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Sum over aligned groups of `width` lanes (width a power of two <= 32).
+__device__ __forceinline__ float group_sum(float v, int width) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        if (o < width) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+// f32 -> f16 (round to nearest even) -> f32: ggml-cpu converts src1 to F16
+// before an F16 dot and q to F16 before the attention dot.
+__device__ __forceinline__ float round_f16(float f) { return __half2float(__float2half_rn(f)); }
+
+// Round half away from zero (C roundf semantics), written out: t = trunc(x)
+// and x - t is exact in fp32 for |x| < 2^23, so the tie test is exact.
+__device__ __forceinline__ int round_half_away(float x) {
+    const float t = truncf(x);
+    const float f = __fsub_rn(x, t);
+    int r = (int)t;
+    if (f >= 0.5f) r += 1;
+    if (f <= -0.5f) r -= 1;
+    return r;
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+}  // namespace b200

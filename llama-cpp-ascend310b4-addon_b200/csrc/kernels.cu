@@ -1,0 +1,439 @@
+// kernels.cu -- device code translation unit and the kernel half of the C ABI.
+//
+// All device code is compiled in this one unit (the .cuh files are included
+// here) so the device status word and helpers need no relocatable device
+// code.  Host-side code elsewhere (graph runner, backend, decode driver)
+// reaches the kernels through include/b200_decode.h and internal.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "fa.cuh"
+#include "gemv.cuh"
+#include "internal.h"
+#include "model_ops.cuh"
+
+using namespace b200;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr size_t kSmemBudget = 200 * 1024;
+
+int g_sms[kMaxDevices];
+std::mutex g_attr_mu;
+bool g_attr_done[kMaxDevices][16][2];
+
+int current_device() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return d;
+}
+
+int sm_count(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return 148;
+    if (g_sms[dev] == 0) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        g_sms[dev] = v > 0 ? v : 148;
+    }
+    return g_sms[dev];
+}
+
+int cuda_status(cudaError_t e) {
+    if (e != cudaSuccess) {
+        fprintf(stderr, "b200_decode: CUDA error %s (%s)\n", cudaGetErrorName(e), cudaGetErrorString(e));
+        return B200_ECUDA;
+    }
+    return B200_OK;
+}
+
+#define CR_(x)                        \
+    do {                              \
+        const int r_ = (x);           \
+        if (r_ != B200_OK) return r_; \
+    } while (0)
+
+// Opts a GEMV instantiation into large dynamic shared memory, once per device.
+// Done before any stream capture (b200i_prepare_device) so that capturing a
+// decode step never calls it.
+template <int FMT, int NU, bool DEBUG>
+int set_gemv_attr(int dev) {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    const int slot = FMT * 4 + (NU == 1 ? 0 : NU == 2 ? 1 : NU == 4 ? 2 : 3);
+    if (dev < 0 || dev >= kMaxDevices || g_attr_done[dev][slot][DEBUG ? 1 : 0]) return B200_OK;
+    cudaError_t e =
+        cudaFuncSetAttribute(gemv_kernel<FMT, NU, DEBUG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return cuda_status(e);
+    g_attr_done[dev][slot][DEBUG ? 1 : 0] = true;
+    return B200_OK;
+}
+
+template <int FMT, bool DEBUG>
+int set_gemv_attrs_fmt(int dev) {
+    CR_((set_gemv_attr<FMT, 1, DEBUG>(dev)));
+    CR_((set_gemv_attr<FMT, 2, DEBUG>(dev)));
+    if constexpr (MaxNU<FMT>::value >= 4) {
+        CR_((set_gemv_attr<FMT, 4, DEBUG>(dev)));
+        CR_((set_gemv_attr<FMT, 8, DEBUG>(dev)));
+    }
+    return B200_OK;
+}
+
+template <int FMT, int NU, bool DEBUG>
+int launch_gemv_nu(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
+    const int dev = current_device();
+    const int grid = (int)std::min<int64_t>(p.ntiles, sm_count(dev));
+    const int64_t per_cta = (p.ntiles + grid - 1) / grid;
+    const size_t fixed = (size_t)(2 * kMaxR * kMaxSlots + 32) * sizeof(float) + 16 * sizeof(uint64_t);
+    int64_t S = (int64_t)((kSmemBudget - fixed) / (size_t)p.tile_bytes);
+    S = std::max<int64_t>(1, std::min<int64_t>(S, per_cta));
+    const size_t smem = (size_t)S * p.tile_bytes + (size_t)S * sizeof(uint64_t) +
+                        (size_t)(2 * kMaxR * kMaxSlots + 32) * sizeof(float);
+    CR_((set_gemv_attr<FMT, NU, DEBUG>(dev)));
+    a.tile_bytes = p.tile_bytes;
+    a.ntiles = p.ntiles;
+    a.R = p.R;
+    a.U = p.U;
+    a.n = p.n;
+    a.k = p.k;
+    a.stages = (int)S;
+    gemv_kernel<FMT, NU, DEBUG><<<grid, kGemvThreads, smem, st>>>(a);
+    return cuda_status(cudaGetLastError());
+}
+
+// Picks the row-group split and the smallest register footprint that covers
+// this thread's share of the activation.
+template <int FMT, bool DEBUG>
+int launch_gemv_t(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
+    a.RG = choose_row_groups(p, MaxNU<FMT>::value);
+    if (a.RG == 0) return B200_EUNSUPPORTED;
+    const int tpr = kGemvThreads / a.RG;
+    const int nu = (p.U + tpr - 1) / tpr;
+    if (nu <= 1) return launch_gemv_nu<FMT, 1, DEBUG>(a, p, st);
+    if (nu <= 2) return launch_gemv_nu<FMT, 2, DEBUG>(a, p, st);
+    if constexpr (MaxNU<FMT>::value >= 4) {
+        if (nu <= 4) return launch_gemv_nu<FMT, 4, DEBUG>(a, p, st);
+        return launch_gemv_nu<FMT, 8, DEBUG>(a, p, st);
+    }
+    return B200_EUNSUPPORTED;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+__global__ void repack_kernel(int type, const uint8_t* src0, const uint8_t* src1, int interleave, uint8_t* dst,
+                              int64_t n, int64_t k, int R, int U, int64_t tile_bytes, int64_t total) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= total) return;
+    const int64_t tile = idx / ((int64_t)R * U);
+    const int64_t rem = idx - tile * (int64_t)R * U;
+    const int r = (int)(rem / U);
+    const int u = (int)(rem - (int64_t)r * U);
+    const int64_t p = tile * R + r;
+    if (p >= n) return;  // destination pre-zeroed
+    const uint8_t* src = src0;
+    int64_t sr = p;
+    if (interleave) {
+        src = (p & 1) ? src1 : src0;
+        sr = p >> 1;
+    }
+    uint8_t* t = dst + tile * tile_bytes;
+    if (type == B200_TYPE_F16) {
+        const uint8_t* s = src + sr * (2 * k) + (int64_t)u * 16;
+        uint8_t* d = t + ((int64_t)r * k + (int64_t)u * 8) * 2;
+        for (int i = 0; i < 16; ++i) d[i] = s[i];
+    } else if (type == B200_TYPE_Q4_0) {
+        const uint8_t* s = src + (sr * U + u) * 18;
+        uint8_t* q = t + ((int64_t)r * U + u) * 16;
+        uint8_t* dd = t + (int64_t)R * U * 16 + ((int64_t)r * U + u) * 2;
+        dd[0] = s[0];
+        dd[1] = s[1];
+        for (int i = 0; i < 16; ++i) q[i] = s[2 + i];
+    } else {
+        const uint8_t* s = src + (sr * U + u) * 34;
+        uint8_t* lo = t + ((int64_t)r * U + u) * 16;
+        uint8_t* hi = t + (int64_t)R * U * 16 + ((int64_t)r * U + u) * 16;
+        uint8_t* dd = t + (int64_t)R * U * 32 + ((int64_t)r * U + u) * 2;
+        dd[0] = s[0];
+        dd[1] = s[1];
+        for (int i = 0; i < 16; ++i) {
+            lo[i] = s[2 + i];
+            hi[i] = s[18 + i];
+        }
+    }
+}
+
+__global__ void quantize_q8_0_kernel(const float* x, uint8_t* out, int64_t nb) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nb) return;
+    const float4* src = reinterpret_cast<const float4*>(x + b * 32);
+    int q[8];
+    float d;
+    uint16_t dh;
+    int qs;
+    quantize_block32([&](int e) { return src[e]; }, q, d, dh, qs);
+    store_block_q8_0(out + b * 34, dh, q);
+}
+
+int gemv_common(int fmt, const void* w, const float* x, float* y, int64_t n, int64_t k, int32_t* dots,
+                cudaStream_t st) {
+    const int type = fmt == FMT_F16 ? B200_TYPE_F16 : (fmt == FMT_Q8 ? B200_TYPE_Q8_0 : B200_TYPE_Q4_0);
+    GemvPlan p;
+    if (!make_plan(type, n, k, &p)) return B200_EUNSUPPORTED;
+    if (!w || !x || !y || !aligned16(w) || !aligned16(x)) return B200_EINVAL;
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.w = static_cast<const uint8_t*>(w);
+    a.x = x;
+    a.pro = PRO_PLAIN;
+    a.epi = EPI_STORE;
+    a.y = y;
+    a.dots = dots;
+    a.n = n;
+    a.k = k;
+    return b200i_gemv(fmt, a, dots != nullptr, st);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ internal
+
+int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st) {
+    const int type = fmt == FMT_F16 ? B200_TYPE_F16 : (fmt == FMT_Q8 ? B200_TYPE_Q8_0 : B200_TYPE_Q4_0);
+    GemvPlan p;
+    if (!make_plan(type, a.n, a.k, &p)) return B200_EUNSUPPORTED;
+    if (debug) {
+        if (fmt == FMT_Q4) return launch_gemv_t<FMT_Q4, true>(a, p, st);
+        if (fmt == FMT_Q8) return launch_gemv_t<FMT_Q8, true>(a, p, st);
+        return B200_EINVAL;
+    }
+    switch (fmt) {
+        case FMT_F16: return launch_gemv_t<FMT_F16, false>(a, p, st);
+        case FMT_Q4: return launch_gemv_t<FMT_Q4, false>(a, p, st);
+        case FMT_Q4W: return launch_gemv_t<FMT_Q4W, false>(a, p, st);
+        case FMT_Q8: return launch_gemv_t<FMT_Q8, false>(a, p, st);
+        default: return B200_EINVAL;
+    }
+}
+
+int b200i_fa(const FaArgs& in, int D, cudaStream_t st) {
+    FaArgs a = in;
+    dim3 grid(a.n_splits, a.Hkv, a.gchunks);
+    switch (D) {
+        case 64: fa_decode_kernel<64><<<grid, kFaThreads, 0, st>>>(a); break;
+        case 128: fa_decode_kernel<128><<<grid, kFaThreads, 0, st>>>(a); break;
+        case 256: fa_decode_kernel<256><<<grid, kFaThreads, 0, st>>>(a); break;
+        default: return B200_EUNSUPPORTED;
+    }
+    return cuda_status(cudaGetLastError());
+}
+
+int b200i_sm_count() { return sm_count(current_device()); }
+
+int b200i_prepare_device() {
+    const int dev = current_device();
+    sm_count(dev);
+    CR_((set_gemv_attrs_fmt<FMT_F16, false>(dev)));
+    CR_((set_gemv_attrs_fmt<FMT_Q4, false>(dev)));
+    CR_((set_gemv_attrs_fmt<FMT_Q4W, false>(dev)));
+    CR_((set_gemv_attrs_fmt<FMT_Q8, false>(dev)));
+    CR_((set_gemv_attrs_fmt<FMT_Q4, true>(dev)));
+    CR_((set_gemv_attrs_fmt<FMT_Q8, true>(dev)));
+    return B200_OK;
+}
+
+static unsigned grid_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
+
+int b200i_synth_q4_0(uint64_t seed, float sigma, int64_t row0, int64_t nrows, int64_t col0, int64_t ncols,
+                     int64_t kglob, void* out, cudaStream_t st) {
+    if (ncols % 32 || nrows <= 0) return B200_EINVAL;
+    synth_q4_0_kernel<<<grid_for(nrows * (ncols / 32), 128), 128, 0, st>>>(seed, sigma, row0, nrows, col0, ncols,
+                                                                          kglob, static_cast<uint8_t*>(out));
+    return cuda_status(cudaGetLastError());
+}
+
+int b200i_synth_rows_f16(uint64_t seed, uint64_t base, int64_t nrows, int64_t rl, int64_t rg, int64_t col0,
+                         void* out, cudaStream_t st) {
+    if (nrows <= 0 || rl <= 0) return B200_OK;
+    synth_rows_f16_kernel<<<grid_for(nrows * rl, 256), 256, 0, st>>>(seed, base, nrows, rl, rg, col0,
+                                                                     static_cast<uint16_t*>(out));
+    return cuda_status(cudaGetLastError());
+}
+
+int b200i_fill_f32(float* p, int64_t n, float v, cudaStream_t st) {
+    fill_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, v);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200i_embed(const void* table, int64_t d_model, int64_t vocab, StepState* state, float* x, cudaStream_t st) {
+    embed_kernel<<<grid_for(d_model, 256) < 64 ? grid_for(d_model, 256) : 64, 256, 0, st>>>(
+        static_cast<const uint8_t*>(table), d_model, vocab, state, x);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200i_finish(StepState* state, cudaStream_t st) {
+    finish_step_kernel<<<1, 1, 0, st>>>(state);
+    return cuda_status(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------- C ABI
+
+extern "C" {
+
+const char* b200_version(void) { return "b200_decode 0.1 (sm_100a)"; }
+
+const char* b200_strerror(int code) {
+    switch (code) {
+        case B200_OK: return "ok";
+        case B200_EINVAL: return "invalid argument";
+        case B200_ECUDA: return "CUDA runtime error";
+        case B200_EUNSUPPORTED: return "unsupported op variant";
+        case B200_ENOMEM: return "out of memory";
+        case B200_ENCCL: return "NCCL error";
+        case B200_ESTATE: return "invalid state";
+        default: return "unknown status";
+    }
+}
+
+int b200_device_status(unsigned int* status, int reset) {
+    if (!status) return B200_EINVAL;
+    int rc = cuda_status(cudaDeviceSynchronize());
+    if (rc) return rc;
+    rc = cuda_status(cudaMemcpyFromSymbol(status, g_status, sizeof(unsigned int)));
+    if (rc) return rc;
+    if (reset) {
+        const unsigned int z = 0;
+        rc = cuda_status(cudaMemcpyToSymbol(g_status, &z, sizeof(unsigned int)));
+    }
+    return rc;
+}
+
+int64_t b200_packed_rows_per_tile(int type, int64_t n, int64_t k) {
+    GemvPlan p;
+    return make_plan(type, n, k, &p) ? p.R : 0;
+}
+
+size_t b200_packed_size(int type, int64_t n, int64_t k) {
+    GemvPlan p;
+    return make_plan(type, n, k, &p) ? (size_t)(p.ntiles * p.tile_bytes) : 0;
+}
+
+static int repack_impl(int type, const void* s0, const void* s1, int interleave, void* dst, int64_t n,
+                       int64_t k, cudaStream_t st) {
+    GemvPlan p;
+    if (!make_plan(type, n, k, &p)) return B200_EUNSUPPORTED;
+    if (!s0 || !dst || (interleave && !s1)) return B200_EINVAL;
+    int rc = cuda_status(cudaMemsetAsync(dst, 0, (size_t)(p.ntiles * p.tile_bytes), st));
+    if (rc) return rc;
+    const int64_t total = p.ntiles * p.R * p.U;
+    const int threads = 256;
+    const int64_t blocks = (total + threads - 1) / threads;
+    repack_kernel<<<(unsigned)blocks, threads, 0, st>>>(type, static_cast<const uint8_t*>(s0),
+                                                        static_cast<const uint8_t*>(s1), interleave,
+                                                        static_cast<uint8_t*>(dst), n, k, p.R, p.U,
+                                                        p.tile_bytes, total);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_repack(int type, const void* src, void* dst, int64_t n, int64_t k, b200_stream_t stream) {
+    return repack_impl(type, src, nullptr, 0, dst, n, k, (cudaStream_t)stream);
+}
+
+int b200_repack_interleave2(int type, const void* src_even, const void* src_odd, void* dst, int64_t n_each,
+                            int64_t k, b200_stream_t stream) {
+    return repack_impl(type, src_even, src_odd, 1, dst, 2 * n_each, k, (cudaStream_t)stream);
+}
+
+int b200_gemv_f16(const void* w, const float* x, float* y, int64_t n, int64_t k, b200_stream_t stream) {
+    return gemv_common(FMT_F16, w, x, y, n, k, nullptr, (cudaStream_t)stream);
+}
+
+int b200_gemv_q4_0(const void* w, const float* x, float* y, int64_t n, int64_t k, int mode,
+                   b200_stream_t stream) {
+    if (mode != B200_Q4_MODE_GGML && mode != B200_Q4_MODE_W4A16) return B200_EINVAL;
+    return gemv_common(mode == B200_Q4_MODE_GGML ? FMT_Q4 : FMT_Q4W, w, x, y, n, k, nullptr,
+                       (cudaStream_t)stream);
+}
+
+int b200_gemv_q8_0_q8_0(const void* w, const float* x, float* y, int64_t n, int64_t k, b200_stream_t stream) {
+    return gemv_common(FMT_Q8, w, x, y, n, k, nullptr, (cudaStream_t)stream);
+}
+
+int b200_quantize_q8_0(const float* x, void* blocks, int64_t k, b200_stream_t stream) {
+    if (!x || !blocks || k <= 0 || k % 32 || !aligned16(x)) return B200_EINVAL;
+    const int64_t nb = k / 32;
+    quantize_q8_0_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, (cudaStream_t)stream>>>(
+        x, static_cast<uint8_t*>(blocks), nb);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_gemv_block_dots(int type, const void* w, const float* x, int32_t* dots, void* xq_blocks, int64_t n,
+                         int64_t k, b200_stream_t stream) {
+    if (!dots) return B200_EINVAL;
+    if (type != B200_TYPE_Q4_0 && type != B200_TYPE_Q8_0) return B200_EUNSUPPORTED;
+    GemvPlan p;
+    if (!make_plan(type, n, k, &p)) return B200_EUNSUPPORTED;
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.w = static_cast<const uint8_t*>(w);
+    a.x = x;
+    a.pro = PRO_PLAIN;
+    a.epi = -1;  // no epilogue: only the block dots are exported
+    a.y = nullptr;
+    a.dots = dots;
+    a.xq_out = static_cast<uint8_t*>(xq_blocks);
+    a.n = n;
+    a.k = k;
+    if (!w || !x || !aligned16(w) || !aligned16(x)) return B200_EINVAL;
+    return b200i_gemv(type == B200_TYPE_Q4_0 ? FMT_Q4 : FMT_Q8, a, true, (cudaStream_t)stream);
+}
+
+size_t b200_fa_workspace_size(int head_dim, int n_head, int n_head_kv, int n_kv) {
+    if (head_dim <= 0 || n_head <= 0 || n_head_kv <= 0 || n_kv <= 0 || n_head % n_head_kv) return 0;
+    return fa_layout(head_dim, n_head, n_head_kv, n_kv).total;
+}
+
+int b200_fa_decode(const float* q, const void* k, const void* v, const void* mask, const int32_t* kv_len,
+                   float* out, int head_dim, int n_head, int n_head_kv, int n_kv, int64_t k_nb1, int64_t k_nb2,
+                   int64_t v_nb1, int64_t v_nb2, float scale, void* workspace, size_t workspace_size,
+                   b200_stream_t stream) {
+    if (!q || !k || !v || !out || !workspace) return B200_EINVAL;
+    if (n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv || n_kv <= 0) return B200_EINVAL;
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256) return B200_EUNSUPPORTED;
+    if (!aligned16(k) || !aligned16(v) || (k_nb1 & 15) || (k_nb2 & 15) || (v_nb1 & 15) || (v_nb2 & 15))
+        return B200_EINVAL;
+    const FaLayout L = fa_layout(head_dim, n_head, n_head_kv, n_kv);
+    if (workspace_size < L.total) return B200_EINVAL;
+    FaArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = q;
+    a.k = static_cast<const uint8_t*>(k);
+    a.v = static_cast<const uint8_t*>(v);
+    a.mask = static_cast<const uint16_t*>(mask);
+    a.kv_len = kv_len;
+    a.out = out;
+    a.Hq = n_head;
+    a.Hkv = n_head_kv;
+    a.G = n_head / n_head_kv;
+    a.gchunks = L.gchunks;
+    a.n_kv = n_kv;
+    a.n_splits = L.n_splits;
+    a.chunks_per_split = L.chunks_per_split;
+    a.k_nb1 = k_nb1;
+    a.k_nb2 = k_nb2;
+    a.v_nb1 = v_nb1;
+    a.v_nb2 = v_nb2;
+    a.scale = scale;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    a.part_o = reinterpret_cast<float*>(ws + L.off_o);
+    a.part_ml = reinterpret_cast<float*>(ws + L.off_ml);
+    a.tickets = reinterpret_cast<unsigned int*>(ws + L.off_tickets);
+    return b200i_fa(a, head_dim, (cudaStream_t)stream);
+}
+
+}  // extern "C"

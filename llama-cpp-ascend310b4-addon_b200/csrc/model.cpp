@@ -1,0 +1,616 @@
+// model.cpp -- native batch-1 decode driver (see include/b200_model.h).
+//
+// Device memory per rank: packed Q4_0 weights of its shard, f32 norms, the
+// f16 KV cache of its KV heads ([kv_size][n_head_kv_local * head_dim] per
+// layer, the ggml cache layout), a few activation vectors and the step state.
+// One decode step = embed, n_layer x (QKV, attention, O [+all-reduce],
+// gate/up, down [+all-reduce]), lm_head [+all-reduce max], finish; captured
+// once into a CUDA graph and replayed.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../../include/b200_model.h"
+#include "internal.h"
+
+using namespace b200;
+
+#define CK(x)                                                                                         \
+    do {                                                                                              \
+        cudaError_t e_ = (x);                                                                         \
+        if (e_ != cudaSuccess) {                                                                      \
+            fprintf(stderr, "b200_model: %s (%s:%d)\n", cudaGetErrorString(e_), __FILE__, __LINE__); \
+            return B200_ECUDA;                                                                        \
+        }                                                                                             \
+    } while (0)
+#define CR(x)                           \
+    do {                                \
+        const int r_ = (x);             \
+        if (r_ != B200_OK) return r_;   \
+    } while (0)
+#define NK(x)                                                                                  \
+    do {                                                                                       \
+        ncclResult_t n_ = (x);                                                                 \
+        if (n_ != ncclSuccess) {                                                               \
+            fprintf(stderr, "b200_model: NCCL %s (%s:%d)\n", ncclGetErrorString(n_), __FILE__, \
+                    __LINE__);                                                                 \
+            return B200_ENCCL;                                                                 \
+        }                                                                                      \
+    } while (0)
+
+namespace {
+
+struct Layer {
+    uint8_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+    uint16_t *kc = nullptr, *vc = nullptr;
+};
+
+constexpr int64_t kQ4Block = 18;
+
+int64_t q4_bytes(int64_t rows, int64_t cols) { return rows * (cols / 32) * kQ4Block; }
+
+// Seed of one weight tensor's counter stream: distinct per (tensor, layer).
+uint64_t tensor_seed(uint64_t seed, int layer, int which) {
+    return seed * 0x9E3779B97F4A7C15ull + (uint64_t)(layer + 2) * 0x100ull + (uint64_t)which;
+}
+
+// Profiling: event pairs around every launch, accumulated per kernel class.
+struct Prof {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> cls;
+    size_t used = 0;
+    int begin(cudaStream_t s, int c) {
+        if (used + 2 > ev.size()) {
+            for (int i = 0; i < 64; ++i) {
+                cudaEvent_t e;
+                CK(cudaEventCreate(&e));
+                ev.push_back(e);
+            }
+        }
+        CK(cudaEventRecord(ev[used], s));
+        cls.push_back(c);
+        return B200_OK;
+    }
+    int end(cudaStream_t s) {
+        CK(cudaEventRecord(ev[used + 1], s));
+        used += 2;
+        return B200_OK;
+    }
+    ~Prof() {
+        for (auto e : ev) cudaEventDestroy(e);
+    }
+};
+
+}  // namespace
+
+struct b200_model {
+    b200_llama_config c{};
+    int device = 0, rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
+    int hq = 0, hkv = 0, ff = 0, voc = 0;
+    int64_t qkv_rows = 0;
+    std::vector<Layer> L;
+    uint8_t* tok_embd = nullptr;
+    float* out_norm = nullptr;
+    uint8_t* lm_head = nullptr;
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *part = nullptr, *logits = nullptr;
+    StepState* st = nullptr;
+    StepState* h_st = nullptr;
+    int* h_next = nullptr;
+    void* fa_ws = nullptr;
+    size_t fa_ws_bytes = 0;
+    uint8_t* staging = nullptr;
+    size_t staging_bytes = 0;
+    cudaStream_t stream = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    std::vector<void*> allocs;
+    uint64_t seed = 0;
+    float sigma = 0.f;
+    FaLayout fa{};
+};
+
+namespace {
+
+int dalloc(b200_model* m, void** p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "b200_model: cudaMalloc(%zu) failed: %s\n", bytes, cudaGetErrorString(e));
+        return B200_ENOMEM;
+    }
+    m->allocs.push_back(*p);
+    return B200_OK;
+}
+
+template <class T>
+int dalloc_t(b200_model* m, T** p, size_t bytes) {
+    void* v = nullptr;
+    CR(dalloc(m, &v, bytes));
+    *p = static_cast<T*>(v);
+    return B200_OK;
+}
+
+// Regenerates one weight shard of this rank in ggml layout at `dst`;
+// returns its row count and column count through rows/cols.
+int gen_weight(b200_model* m, int layer, int which, uint8_t* dst, int64_t* rows, int64_t* cols) {
+    const b200_llama_config& c = m->c;
+    const int D = c.head_dim;
+    const uint64_t s = tensor_seed(m->seed, layer, which);
+    int64_t r0 = 0, nr = 0, c0 = 0, nc = 0, kg = 0;
+    switch (which) {
+        case B200_W_TOK_EMBD: r0 = 0; nr = c.vocab; c0 = 0; nc = c.d_model; kg = c.d_model; break;
+        case B200_W_Q: r0 = (int64_t)m->rank * m->hq * D; nr = (int64_t)m->hq * D; nc = kg = c.d_model; break;
+        case B200_W_K:
+        case B200_W_V: r0 = (int64_t)m->rank * m->hkv * D; nr = (int64_t)m->hkv * D; nc = kg = c.d_model; break;
+        case B200_W_O:
+            nr = c.d_model; c0 = (int64_t)m->rank * m->hq * D; nc = (int64_t)m->hq * D; kg = (int64_t)c.n_head * D;
+            break;
+        case B200_W_GATE:
+        case B200_W_UP: r0 = (int64_t)m->rank * m->ff; nr = m->ff; nc = kg = c.d_model; break;
+        case B200_W_DOWN: nr = c.d_model; c0 = (int64_t)m->rank * m->ff; nc = m->ff; kg = c.d_ff; break;
+        case B200_W_LM_HEAD: r0 = (int64_t)m->rank * m->voc; nr = m->voc; nc = kg = c.d_model; break;
+        default: return B200_EINVAL;
+    }
+    *rows = nr;
+    *cols = nc;
+    return b200i_synth_q4_0(s, m->sigma, r0, nr, c0, nc, kg, dst, m->stream);
+}
+
+int allreduce_sum(b200_model* m, const float* src, float* dst, size_t n, cudaStream_t s) {
+    NK(ncclAllReduce(src, dst, n, ncclFloat32, ncclSum, m->comm, s));
+    return B200_OK;
+}
+
+int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof) {
+    const b200_llama_config& c = m->c;
+    const int D = c.head_dim;
+    const float theta_scale = powf(c.rope_theta, -2.0f / (float)D);
+    auto B = [&](int cls) { return prof ? prof->begin(s, cls) : B200_OK; };
+    auto E = [&]() { return prof ? prof->end(s) : B200_OK; };
+
+    CR(B(0));
+    CR(b200i_embed(m->tok_embd, c.d_model, c.vocab, m->st, m->x, s));
+    CR(E());
+    for (int l = 0; l < c.n_layer; ++l) {
+        const Layer& Ly = m->L[l];
+        GemvArgs a;
+        std::memset(&a, 0, sizeof(a));
+        a.w = Ly.wqkv;
+        a.n = m->qkv_rows;
+        a.k = c.d_model;
+        a.x = m->x;
+        a.norm_w = Ly.attn_norm;
+        a.eps = c.rms_eps;
+        a.pro = PRO_RMSNORM;
+        a.epi = EPI_QKV;
+        a.y = m->q;
+        a.nq = m->hq * D;
+        a.nkv = m->hkv * D;
+        a.head_dim = D;
+        a.pos = &m->st->pos;
+        a.theta_scale = theta_scale;
+        a.kc = Ly.kc;
+        a.vc = Ly.vc;
+        CR(B(1));
+        CR(b200i_gemv(FMT_Q4, a, false, s));
+        CR(E());
+
+        FaArgs f;
+        std::memset(&f, 0, sizeof(f));
+        f.q = m->q;
+        f.k = reinterpret_cast<const uint8_t*>(Ly.kc);
+        f.v = reinterpret_cast<const uint8_t*>(Ly.vc);
+        f.mask = nullptr;
+        f.kv_len = &m->st->ctx;
+        f.out = m->att;
+        f.Hq = m->hq;
+        f.Hkv = m->hkv;
+        f.G = m->hq / m->hkv;
+        f.gchunks = m->fa.gchunks;
+        f.n_kv = c.kv_size;
+        f.n_splits = m->fa.n_splits;
+        f.chunks_per_split = m->fa.chunks_per_split;
+        f.k_nb1 = f.v_nb1 = (int64_t)m->hkv * D * 2;
+        f.k_nb2 = f.v_nb2 = (int64_t)D * 2;
+        f.scale = 1.0f / sqrtf((float)D);
+        uint8_t* ws = static_cast<uint8_t*>(m->fa_ws);
+        f.part_o = reinterpret_cast<float*>(ws + m->fa.off_o);
+        f.part_ml = reinterpret_cast<float*>(ws + m->fa.off_ml);
+        f.tickets = reinterpret_cast<unsigned int*>(ws + m->fa.off_tickets);
+        CR(B(2));
+        CR(b200i_fa(f, D, s));
+        CR(E());
+
+        std::memset(&a, 0, sizeof(a));
+        a.w = Ly.wo;
+        a.n = c.d_model;
+        a.k = (int64_t)m->hq * D;
+        a.x = m->att;
+        a.pro = PRO_PLAIN;
+        a.res = m->x;
+        if (m->world == 1) {
+            a.epi = EPI_ADD;
+            a.y = m->x;
+        } else {
+            a.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
+            a.y = m->part;
+        }
+        CR(B(3));
+        CR(b200i_gemv(FMT_Q4, a, false, s));
+        CR(E());
+        if (m->world > 1) {
+            CR(B(7));
+            CR(allreduce_sum(m, m->part, m->x, c.d_model, s));
+            CR(E());
+        }
+
+        std::memset(&a, 0, sizeof(a));
+        a.w = Ly.wgu;
+        a.n = 2 * (int64_t)m->ff;
+        a.k = c.d_model;
+        a.x = m->x;
+        a.norm_w = Ly.ffn_norm;
+        a.eps = c.rms_eps;
+        a.pro = PRO_RMSNORM;
+        a.epi = EPI_SWIGLU;
+        a.y = m->h;
+        CR(B(4));
+        CR(b200i_gemv(FMT_Q4, a, false, s));
+        CR(E());
+
+        std::memset(&a, 0, sizeof(a));
+        a.w = Ly.wdown;
+        a.n = c.d_model;
+        a.k = m->ff;
+        a.x = m->h;
+        a.pro = PRO_PLAIN;
+        a.res = m->x;
+        if (m->world == 1) {
+            a.epi = EPI_ADD;
+            a.y = m->x;
+        } else {
+            a.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
+            a.y = m->part;
+        }
+        CR(B(5));
+        CR(b200i_gemv(FMT_Q4, a, false, s));
+        CR(E());
+        if (m->world > 1) {
+            CR(B(7));
+            CR(allreduce_sum(m, m->part, m->x, c.d_model, s));
+            CR(E());
+        }
+    }
+    GemvArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.w = m->lm_head;
+    a.n = m->voc;
+    a.k = c.d_model;
+    a.x = m->x;
+    a.norm_w = m->out_norm;
+    a.eps = c.rms_eps;
+    a.pro = PRO_RMSNORM;
+    a.epi = EPI_ARGMAX;
+    a.y = m->logits;
+    a.amax = &m->st->amax;
+    a.row_offset = (int64_t)m->rank * m->voc;
+    CR(B(6));
+    CR(b200i_gemv(FMT_Q4, a, false, s));
+    CR(E());
+    if (m->world > 1) {
+        CR(B(7));
+        NK(ncclAllReduce(&m->st->amax, &m->st->amax, 1, ncclUint64, ncclMax, m->comm, s));
+        CR(E());
+    }
+    CR(b200i_finish(m->st, s));
+    return B200_OK;
+}
+
+int validate(const b200_llama_config& c, int world) {
+    if (c.n_layer <= 0 || c.d_model <= 0 || c.n_head <= 0 || c.n_head_kv <= 0 || c.head_dim <= 0 || c.d_ff <= 0 ||
+        c.vocab <= 0 || c.kv_size <= 0 || world <= 0)
+        return B200_EINVAL;
+    if (c.n_head % c.n_head_kv || c.n_head_kv % world || c.d_ff % (32 * world) || c.vocab % world)
+        return B200_EINVAL;
+    if (c.d_model % 256 || c.head_dim % 2 || ((c.n_head / world) * c.head_dim) % 32) return B200_EINVAL;
+    if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return B200_EUNSUPPORTED;
+    return B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_nccl_unique_id(void* out128) {
+    if (!out128) return B200_EINVAL;
+    ncclUniqueId id;
+    NK(ncclGetUniqueId(&id));
+    static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
+    std::memcpy(out128, &id, sizeof(id));
+    return B200_OK;
+}
+
+int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int tp_world, const void* nccl_id128,
+                      b200_model** out) {
+    if (!cfg || !out) return B200_EINVAL;
+    *out = nullptr;
+    CR(validate(*cfg, tp_world));
+    if (tp_rank < 0 || tp_rank >= tp_world || (tp_world > 1 && !nccl_id128)) return B200_EINVAL;
+    CK(cudaSetDevice(device));
+    b200_model* m = new b200_model();
+    m->c = *cfg;
+    m->device = device;
+    m->rank = tp_rank;
+    m->world = tp_world;
+    const b200_llama_config& c = m->c;
+    const int D = c.head_dim;
+    m->hq = c.n_head / tp_world;
+    m->hkv = c.n_head_kv / tp_world;
+    m->ff = c.d_ff / tp_world;
+    m->voc = c.vocab / tp_world;
+    m->qkv_rows = (int64_t)(m->hq + 2 * m->hkv) * D;
+    int rc = B200_OK;
+    auto fail = [&](int r) {
+        b200_model_destroy(m);
+        return r;
+    };
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(B200_ECUDA);
+    if (tp_world > 1) {
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id128, sizeof(id));
+        if (ncclCommInitRank(&m->comm, tp_world, id, tp_rank) != ncclSuccess) return fail(B200_ENCCL);
+    }
+    const size_t p_qkv = b200_packed_size(B200_TYPE_Q4_0, m->qkv_rows, c.d_model);
+    const size_t p_o = b200_packed_size(B200_TYPE_Q4_0, c.d_model, (int64_t)m->hq * D);
+    const size_t p_gu = b200_packed_size(B200_TYPE_Q4_0, 2 * (int64_t)m->ff, c.d_model);
+    const size_t p_down = b200_packed_size(B200_TYPE_Q4_0, c.d_model, m->ff);
+    const size_t p_head = b200_packed_size(B200_TYPE_Q4_0, m->voc, c.d_model);
+    if (!p_qkv || !p_o || !p_gu || !p_down || !p_head) return fail(B200_EUNSUPPORTED);
+    // pair epilogues (RoPE pairs, gate/up pairs) need two rows per tile
+    if (b200_packed_rows_per_tile(B200_TYPE_Q4_0, m->qkv_rows, c.d_model) < 2 ||
+        b200_packed_rows_per_tile(B200_TYPE_Q4_0, 2 * (int64_t)m->ff, c.d_model) < 2)
+        return fail(B200_EUNSUPPORTED);
+    const size_t kv_bytes = (size_t)c.kv_size * m->hkv * D * 2;
+    m->L.resize(c.n_layer);
+    for (auto& Ly : m->L) {
+        if ((rc = dalloc_t(m, &Ly.wqkv, p_qkv)) || (rc = dalloc_t(m, &Ly.wo, p_o)) ||
+            (rc = dalloc_t(m, &Ly.wgu, p_gu)) || (rc = dalloc_t(m, &Ly.wdown, p_down)) ||
+            (rc = dalloc_t(m, &Ly.attn_norm, c.d_model * 4)) || (rc = dalloc_t(m, &Ly.ffn_norm, c.d_model * 4)) ||
+            (rc = dalloc_t(m, &Ly.kc, kv_bytes)) || (rc = dalloc_t(m, &Ly.vc, kv_bytes)))
+            return fail(rc);
+    }
+    m->staging_bytes = (size_t)std::max<int64_t>(
+        std::max<int64_t>(q4_bytes(m->qkv_rows, c.d_model), q4_bytes(c.d_model, (int64_t)m->hq * D)),
+        std::max<int64_t>(std::max<int64_t>(2 * q4_bytes(m->ff, c.d_model), q4_bytes(c.d_model, m->ff)),
+                          q4_bytes(m->voc, c.d_model)));
+    m->fa = fa_layout(D, m->hq, m->hkv, c.kv_size);
+    m->fa_ws_bytes = m->fa.total;
+    if ((rc = dalloc_t(m, &m->tok_embd, q4_bytes(c.vocab, c.d_model))) || (rc = dalloc_t(m, &m->lm_head, p_head)) ||
+        (rc = dalloc_t(m, &m->out_norm, c.d_model * 4)) || (rc = dalloc_t(m, &m->x, c.d_model * 4)) ||
+        (rc = dalloc_t(m, &m->q, (size_t)m->hq * D * 4)) || (rc = dalloc_t(m, &m->att, (size_t)m->hq * D * 4)) ||
+        (rc = dalloc_t(m, &m->h, (size_t)m->ff * 4)) || (rc = dalloc_t(m, &m->part, c.d_model * 4)) ||
+        (rc = dalloc_t(m, &m->logits, (size_t)m->voc * 4)) || (rc = dalloc_t(m, &m->st, sizeof(StepState))) ||
+        (rc = dalloc(m, &m->fa_ws, m->fa_ws_bytes)) || (rc = dalloc_t(m, &m->staging, m->staging_bytes)))
+        return fail(rc);
+    if (cudaMemset(m->fa_ws, 0, m->fa_ws_bytes) != cudaSuccess) return fail(B200_ECUDA);
+    if (cudaMallocHost(reinterpret_cast<void**>(&m->h_st), sizeof(StepState)) != cudaSuccess) return fail(B200_ENOMEM);
+    if (cudaMallocHost(reinterpret_cast<void**>(&m->h_next), sizeof(int)) != cudaSuccess) return fail(B200_ENOMEM);
+    std::memset(m->h_st, 0, sizeof(StepState));
+    m->h_st->ctx = 1;
+    if (cudaMemcpy(m->st, m->h_st, sizeof(StepState), cudaMemcpyHostToDevice) != cudaSuccess) return fail(B200_ECUDA);
+    *out = m;
+    return B200_OK;
+}
+
+void b200_model_destroy(b200_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    // Graphs that hold NCCL work are released before the communicator.
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    if (m->comm) ncclCommDestroy(m->comm);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->h_st) cudaFreeHost(m->h_st);
+    if (m->h_next) cudaFreeHost(m->h_next);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int b200_model_init_synthetic(b200_model* m, uint64_t seed, float sigma) {
+    if (!m) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    m->seed = seed;
+    m->sigma = sigma;
+    const b200_llama_config& c = m->c;
+    const cudaStream_t s = m->stream;
+    int64_t r, k;
+    CR(gen_weight(m, -1, B200_W_TOK_EMBD, m->tok_embd, &r, &k));
+    CR(gen_weight(m, -1, B200_W_LM_HEAD, m->staging, &r, &k));
+    CR(b200_repack(B200_TYPE_Q4_0, m->staging, m->lm_head, r, k, (b200_stream_t)s));
+    CR(b200i_fill_f32(m->out_norm, c.d_model, 1.0f, s));
+    for (int l = 0; l < c.n_layer; ++l) {
+        Layer& Ly = m->L[l];
+        int64_t rq, rk, rv;
+        CR(gen_weight(m, l, B200_W_Q, m->staging, &rq, &k));
+        CR(gen_weight(m, l, B200_W_K, m->staging + q4_bytes(rq, k), &rk, &k));
+        CR(gen_weight(m, l, B200_W_V, m->staging + q4_bytes(rq + rk, k), &rv, &k));
+        CR(b200_repack(B200_TYPE_Q4_0, m->staging, Ly.wqkv, rq + rk + rv, k, (b200_stream_t)s));
+        CR(gen_weight(m, l, B200_W_O, m->staging, &r, &k));
+        CR(b200_repack(B200_TYPE_Q4_0, m->staging, Ly.wo, r, k, (b200_stream_t)s));
+        int64_t rg, ru;
+        CR(gen_weight(m, l, B200_W_GATE, m->staging, &rg, &k));
+        CR(gen_weight(m, l, B200_W_UP, m->staging + q4_bytes(rg, k), &ru, &k));
+        CR(b200_repack_interleave2(B200_TYPE_Q4_0, m->staging, m->staging + q4_bytes(rg, k), Ly.wgu, rg, k,
+                                   (b200_stream_t)s));
+        CR(gen_weight(m, l, B200_W_DOWN, m->staging, &r, &k));
+        CR(b200_repack(B200_TYPE_Q4_0, m->staging, Ly.wdown, r, k, (b200_stream_t)s));
+        CR(b200i_fill_f32(Ly.attn_norm, c.d_model, 1.0f, s));
+        CR(b200i_fill_f32(Ly.ffn_norm, c.d_model, 1.0f, s));
+    }
+    CK(cudaStreamSynchronize(s));
+    return B200_OK;
+}
+
+int b200_model_fill_kv_synthetic(b200_model* m, uint64_t seed, int n_pos) {
+    if (!m || n_pos < 0 || n_pos > m->c.kv_size) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    const b200_llama_config& c = m->c;
+    const int64_t rl = (int64_t)m->hkv * c.head_dim, rg = (int64_t)c.n_head_kv * c.head_dim;
+    const int64_t col0 = (int64_t)m->rank * rl;
+    for (int l = 0; l < c.n_layer; ++l) {
+        for (int w = 0; w < 2; ++w) {
+            const uint64_t base = ((uint64_t)(2 * l + w)) << 40;
+            CR(b200i_synth_rows_f16(seed, base, n_pos, rl, rg, col0, w ? (void*)m->L[l].vc : (void*)m->L[l].kc,
+                                    m->stream));
+        }
+    }
+    CK(cudaStreamSynchronize(m->stream));
+    return B200_OK;
+}
+
+int b200_model_export_weight(b200_model* m, int layer, int which, void* host, size_t* bytes) {
+    if (!m || !bytes) return B200_EINVAL;
+    if (which != B200_W_TOK_EMBD && which != B200_W_LM_HEAD && (layer < 0 || layer >= m->c.n_layer))
+        return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    int64_t r, k;
+    CR(gen_weight(m, (which == B200_W_TOK_EMBD || which == B200_W_LM_HEAD) ? -1 : layer, which, m->staging, &r, &k));
+    const size_t need = (size_t)q4_bytes(r, k);
+    if (!host) {
+        *bytes = need;
+        CK(cudaStreamSynchronize(m->stream));
+        return B200_OK;
+    }
+    if (*bytes < need) return B200_EINVAL;
+    CK(cudaMemcpyAsync(host, m->staging, need, cudaMemcpyDeviceToHost, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    *bytes = need;
+    return B200_OK;
+}
+
+int b200_model_export_kv(b200_model* m, int layer, int which, int n_pos, void* host) {
+    if (!m || !host || layer < 0 || layer >= m->c.n_layer || which < 0 || which > 1 || n_pos < 0 ||
+        n_pos > m->c.kv_size)
+        return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    const size_t bytes = (size_t)n_pos * m->hkv * m->c.head_dim * 2;
+    CK(cudaMemcpyAsync(host, which ? (void*)m->L[layer].vc : (void*)m->L[layer].kc, bytes, cudaMemcpyDeviceToHost,
+                       m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    return B200_OK;
+}
+
+int b200_model_capture(b200_model* m) {
+    if (!m) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    if (m->exec) return B200_OK;
+    CR(b200i_prepare_device());
+    CK(cudaStreamSynchronize(m->stream));
+    CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_step(m, m->stream, nullptr);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc != B200_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    CK(e);
+    m->graph = g;
+    CK(cudaGraphInstantiate(&m->exec, m->graph, 0));
+    return B200_OK;
+}
+
+int b200_model_set_state(b200_model* m, int token, int pos, int advance) {
+    if (!m || pos < 0 || pos >= m->c.kv_size || token < 0 || token >= m->c.vocab) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    CK(cudaStreamSynchronize(m->stream));
+    m->h_st->token = token;
+    m->h_st->pos = pos;
+    m->h_st->ctx = pos + 1;
+    m->h_st->advance = advance ? 1 : 0;
+    CK(cudaMemcpyAsync(m->st, m->h_st, 4 * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    return B200_OK;
+}
+
+int b200_model_launch(b200_model* m) {
+    if (!m) return B200_EINVAL;
+    if (!m->exec) CR(b200_model_capture(m));
+    CK(cudaGraphLaunch(m->exec, m->stream));
+    return B200_OK;
+}
+
+int b200_model_decode(b200_model* m, int token, int pos, int* next_token, float* logits_host) {
+    if (!m || pos < 0 || pos >= m->c.kv_size || token < 0 || token >= m->c.vocab) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    if (!m->exec) CR(b200_model_capture(m));
+    m->h_st->token = token;
+    m->h_st->pos = pos;
+    m->h_st->ctx = pos + 1;
+    m->h_st->advance = 0;
+    CK(cudaMemcpyAsync(m->st, m->h_st, 4 * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    CK(cudaGraphLaunch(m->exec, m->stream));
+    CK(cudaMemcpyAsync(m->h_next, &m->st->next, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    if (logits_host)
+        CK(cudaMemcpyAsync(logits_host, m->logits, (size_t)m->voc * 4, cudaMemcpyDeviceToHost, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    if (next_token) *next_token = *m->h_next;
+    return B200_OK;
+}
+
+int b200_model_logits(b200_model* m, float* host, int64_t* offset, int64_t* count) {
+    if (!m) return B200_EINVAL;
+    if (offset) *offset = (int64_t)m->rank * m->voc;
+    if (count) *count = m->voc;
+    if (!host) return B200_OK;
+    CK(cudaSetDevice(m->device));
+    CK(cudaMemcpyAsync(host, m->logits, (size_t)m->voc * 4, cudaMemcpyDeviceToHost, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    return B200_OK;
+}
+
+b200_stream_t b200_model_stream(b200_model* m) { return m ? (b200_stream_t)m->stream : nullptr; }
+
+int b200_model_step_bytes(b200_model* m, int ctx, uint64_t* bytes) {
+    if (!m || !bytes) return B200_EINVAL;
+    const b200_llama_config& c = m->c;
+    const int64_t D = c.head_dim;
+    uint64_t b = 0;
+    const uint64_t per_layer = (uint64_t)q4_bytes(m->qkv_rows, c.d_model) + q4_bytes(c.d_model, m->hq * D) +
+                               2 * (uint64_t)q4_bytes(m->ff, c.d_model) + q4_bytes(c.d_model, m->ff) +
+                               2ull * c.d_model * 4 + 2ull * (uint64_t)ctx * m->hkv * D * 2;
+    b += per_layer * c.n_layer;
+    b += (uint64_t)q4_bytes(m->voc, c.d_model) + (uint64_t)c.d_model * 4 + (uint64_t)(c.d_model / 32) * 18;
+    *bytes = b;
+    return B200_OK;
+}
+
+int b200_model_profile(b200_model* m, int iters, float* us) {
+    if (!m || !us || iters <= 0) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    CR(b200i_prepare_device());
+    double acc[8] = {0};
+    int cnt[8] = {0};
+    for (int it = 0; it < iters; ++it) {
+        Prof p;
+        CR(enqueue_step(m, m->stream, &p));
+        CK(cudaStreamSynchronize(m->stream));
+        for (size_t i = 0; i < p.cls.size(); ++i) {
+            float ms = 0.f;
+            CK(cudaEventElapsedTime(&ms, p.ev[2 * i], p.ev[2 * i + 1]));
+            acc[p.cls[i]] += ms * 1000.0;
+            cnt[p.cls[i]] += 1;
+        }
+    }
+    for (int i = 0; i < 8; ++i) us[i] = cnt[i] ? (float)(acc[i] / cnt[i]) : 0.f;
+    return B200_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,116 @@
+// model_ops.cuh -- small kernels around the decode step: synthetic weight and
+// KV generation, embedding lookup (GET_ROWS of a Q4_0 table), the step's
+// device state (token, position, argmax) and fills.
+#pragma once
+
+#include "args.h"
+#include "common.cuh"
+
+namespace b200 {
+
+__host__ __device__ inline uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Box-Muller on two 24-bit uniforms drawn from splitmix64(seed, index); the
+// same counter stream as the CPU oracle's ref_synth_normal (values agree up
+// to libm rounding of logf/cosf).
+__device__ __forceinline__ float synth_normal(uint64_t seed_mixed, uint64_t index) {
+    const uint64_t h = splitmix64(seed_mixed ^ (index * 0xD1B54A32D192ED03ull));
+    const float u1 = ((float)(uint32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)(uint32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    const float r = sqrtf(-2.0f * logf(u1));
+    return r * cosf(6.283185307179586f * u2);
+}
+
+// ggml Q4_0 blocks of N(0, sigma^2) samples: local rows [0, nrows) are global
+// rows row0 + r; local columns [0, ncols) are global columns col0 + c of a
+// matrix with kglob columns.  One thread per block, ggml block layout out.
+__global__ void synth_q4_0_kernel(uint64_t seed, float sigma, int64_t row0, int64_t nrows, int64_t col0,
+                                  int64_t ncols, int64_t kglob, uint8_t* out) {
+    const int64_t nb = ncols / 32;
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nrows * nb) return;
+    const int64_t r = b / nb, cb = b - r * nb;
+    const uint64_t sm = splitmix64(seed);
+    const uint64_t base = (uint64_t)(row0 + r) * (uint64_t)kglob + (uint64_t)(col0 + cb * 32);
+    float v[32];
+    float amax = 0.f, mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        v[j] = sigma * synth_normal(sm, base + j);
+        if (amax < fabsf(v[j])) {
+            amax = fabsf(v[j]);
+            mx = v[j];
+        }
+    }
+    // quantize_row_q4_0_ref: d = max / -8, q = min(15, (int8)(x*id + 8.5f))
+    const float d = __fdiv_rn(mx, -8.0f);
+    const float id = d != 0.f ? __frcp_rn(d) : 0.f;
+    uint8_t* blk = out + b * 18;
+    const uint16_t dh = f2h(d);
+    blk[0] = (uint8_t)(dh & 0xff);
+    blk[1] = (uint8_t)(dh >> 8);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        int q0 = (int)(int8_t)__fadd_rn(__fmul_rn(v[j], id), 8.5f);
+        int q1 = (int)(int8_t)__fadd_rn(__fmul_rn(v[16 + j], id), 8.5f);
+        q0 = min(q0, 15);
+        q1 = min(q1, 15);
+        blk[2 + j] = (uint8_t)(q0 | (q1 << 4));
+    }
+}
+
+// f16 N(0,1) rows: local element (r, c) of rows of `rl` elements takes the
+// stream index base + r * rg + col0 + c (rg = global row length), so a
+// tensor-parallel shard holds exactly the values of the unsharded tensor.
+__global__ void synth_rows_f16_kernel(uint64_t seed, uint64_t base, int64_t nrows, int64_t rl, int64_t rg,
+                                      int64_t col0, uint16_t* out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nrows * rl) return;
+    const int64_t r = i / rl, c = i - r * rl;
+    out[i] = f2h(synth_normal(splitmix64(seed), base + (uint64_t)(r * rg + col0 + c)));
+}
+
+__global__ void fill_f32_kernel(float* p, int64_t n, float v) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
+// GET_ROWS of a Q4_0 table (ggml dequantize_row_q4_0: d * (q - 8)), plus the
+// step bookkeeping that must precede the layers.
+__global__ void embed_kernel(const uint8_t* table, int64_t d_model, int64_t vocab, StepState* st, float* x) {
+    int tok = st->token;
+    if (tok < 0 || tok >= vocab) {  // bad token id: record it and read row 0 instead
+        if (blockIdx.x == 0 && threadIdx.x == 0) record_status(B200_DEVSTATUS_BOUNDS);
+        tok = 0;
+    }
+    const int64_t nb = d_model / 32;
+    const uint8_t* row = table + (int64_t)tok * nb * 18;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < d_model; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / 32, j = i % 32;
+        const uint8_t* blk = row + b * 18;
+        const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+        const int q = j < 16 ? (blk[2 + j] & 0x0f) : (blk[2 + j - 16] >> 4);
+        x[i] = (float)(q - 8) * d;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        st->ctx = st->pos + 1;
+        st->amax = 0ull;
+    }
+}
+
+__global__ void finish_step_kernel(StepState* st) {
+    const unsigned long long a = st->amax;
+    const int idx = (int)(0xffffffffu - (unsigned int)(a & 0xffffffffull));
+    st->next = idx;
+    if (st->advance) {
+        st->token = idx;
+        st->pos = st->pos + 1;
+    }
+}
+
+}  // namespace b200

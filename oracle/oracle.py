@@ -312,8 +312,8 @@ class OracleLlama:
         self.v_cache = v_cache
         m = RefLlama()
         m.cfg = RefLlamaCfg(
-            cfg["n_layer"], cfg["d_model"], cfg["n_head"], cfg["n_kv_head"], cfg["head_dim"], cfg["d_ff"],
-            cfg["vocab"], cfg["kv_size"], cfg["rope_theta"], cfg["eps"],
+            cfg["n_layer"], cfg["d_model"], cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"], cfg["d_ff"],
+            cfg["vocab"], cfg["kv_size"], cfg["rope_theta"], cfg["rms_eps"],
         )
         m.tok_embd = _p(weights["tok_embd"]).value
         for key in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown", "attn_norm", "ffn_norm"):

@@ -1,0 +1,89 @@
+"""CPU-side checks of the C ABI library: it loads, exports every entry point
+that include/*.h declares, validates arguments before touching a device, and
+its host helpers match the oracle."""
+import glob
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"\b(b200_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol():
+    import b200_decode as B
+
+    L = B.lib()
+    names = declared_symbols()
+    assert len(names) >= 15
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_version_and_errors():
+    import b200_decode as B
+
+    assert b"sm_100a" in B.lib().b200_version()
+    assert B.lib().b200_strerror(-1) == b"invalid argument"
+
+
+@pytest.mark.parametrize("wtype,n,k", [(1, 8960, 1536), (2, 1536, 8960), (8, 151936, 1536), (2, 10240, 8192),
+                                       (2, 57344, 8192), (2, 8192, 28672), (1, 5, 8), (8, 3, 32)])
+def test_packed_size_layout(wtype, n, k):
+    import b200_decode as B
+
+    r = B.rows_per_tile(wtype, n, k)
+    assert r >= 1 and (r & (r - 1)) == 0
+    rowbytes = {1: 2 * k, 2: k // 2 + k // 16, 8: k + k // 16}[wtype]
+    tile = (r * rowbytes + 15) // 16 * 16
+    assert B.packed_size(wtype, n, k) == tile * ((n + r - 1) // r)
+    assert tile <= 65536
+
+
+def test_unsupported_shapes_report_zero():
+    import b200_decode as B
+
+    assert B.packed_size(2, 16, 48) == 0      # K not a multiple of 32
+    assert B.packed_size(1, 16, 12) == 0      # F16 K not a multiple of 8
+    assert B.packed_size(3, 16, 64) == 0      # type not served
+
+
+def test_argument_validation_without_device():
+    import ctypes as C
+
+    import b200_decode as B
+
+    L = B.lib()
+    assert L.b200_gemv_f16(None, None, None, 8, 8, None) == B.EINVAL
+    assert L.b200_fa_decode(None, None, None, None, None, None, 128, 12, 2, 16, 0, 0, 0, 0, 1.0, None, 0,
+                            None) == B.EINVAL
+    assert L.b200_fa_workspace_size(128, 12, 5, 16) == 0
+    assert L.b200_repack(2, None, None, 4, 64, None) == B.EINVAL
+    assert L.b200_quantize_q8_0(None, None, 32, None) == B.EINVAL
+    v = C.c_uint(0)
+    assert L.b200_device_status(None, 0) == B.EINVAL
+
+
+def test_kv_lengths_host_helper_matches_oracle():
+    import b200_decode as B
+
+    r = np.random.default_rng(0)
+    m = np.zeros((6, 300), np.float16)
+    for i, cut in enumerate([300, 1, 0, 150, 299, 7]):
+        m[i, cut:] = -np.inf
+    m[3, 20] = -np.inf  # interior -inf does not shorten the row
+    np.testing.assert_array_equal(B.kv_lengths_from_mask(m), O.kv_lengths_from_mask(m))
+    np.testing.assert_array_equal(B.kv_lengths_from_mask(m), [300, 1, 1, 150, 299, 7])
