@@ -90,6 +90,13 @@ int b200_model_decode(b200_model *m, int token, int pos, int *next_token, float 
 /* Copies the logits of the last step: this rank's rows [offset, offset+count). */
 int b200_model_logits(b200_model *m, float *host, int64_t *offset, int64_t *count);
 b200_stream_t b200_model_stream(b200_model *m);
+/* Layer dump (the decode-path analogue of the reference's LLAMA_LAYER_DUMP
+ * eval callback, patch:825-892): one eager step at (token, pos) that copies
+ * the residual stream after the embedding and after every layer into
+ * x_host [(n_layer + 1) * d_model], and, when q_host / att_host are not NULL,
+ * the roped q and the attention output of every layer
+ * ([n_layer][n_head_local * head_dim] each).  Logits land as after a decode. */
+int b200_model_debug_step(b200_model *m, int token, int pos, float *x_host, float *q_host, float *att_host);
 /* Algorithmic HBM bytes one decode step reads on this rank at context ctx. */
 int b200_model_step_bytes(b200_model *m, int ctx, uint64_t *bytes);
 /* Runs `iters` eager (not captured) steps with CUDA events around every

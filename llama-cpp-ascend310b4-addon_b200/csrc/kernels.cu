@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -43,6 +44,16 @@ int sm_count(int dev) {
         g_sms[dev] = v > 0 ? v : 148;
     }
     return g_sms[dev];
+}
+
+// B200_GEMV_STAGES caps the bulk-copy pipeline depth (tuning sweeps); unset
+// or 0 means as many stages as the shared-memory budget holds.
+int stage_cap() {
+    static const int cap = [] {
+        const char* s = getenv("B200_GEMV_STAGES");
+        return s ? atoi(s) : 0;
+    }();
+    return cap;
 }
 
 int cuda_status(cudaError_t e) {
@@ -92,6 +103,8 @@ int launch_gemv_nu(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
     const int64_t per_cta = (p.ntiles + grid - 1) / grid;
     const size_t fixed = (size_t)(2 * kMaxR * kMaxSlots + 32) * sizeof(float) + 16 * sizeof(uint64_t);
     int64_t S = (int64_t)((kSmemBudget - fixed) / (size_t)p.tile_bytes);
+    const int cap = stage_cap();
+    if (cap > 0) S = std::min<int64_t>(S, cap);
     S = std::max<int64_t>(1, std::min<int64_t>(S, per_cta));
     const size_t smem = (size_t)S * p.tile_bytes + (size_t)S * sizeof(uint64_t) +
                         (size_t)(2 * kMaxR * kMaxSlots + 32) * sizeof(float);

@@ -168,7 +168,13 @@ int allreduce_sum(b200_model* m, const float* src, float* dst, size_t n, cudaStr
     return B200_OK;
 }
 
-int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof) {
+struct Dump {
+    float* x = nullptr;    // device [(n_layer + 1) * d]
+    float* q = nullptr;    // device [n_layer * hq * D]
+    float* att = nullptr;  // device [n_layer * hq * D]
+};
+
+int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = nullptr) {
     const b200_llama_config& c = m->c;
     const int D = c.head_dim;
     const float theta_scale = powf(c.rope_theta, -2.0f / (float)D);
@@ -178,6 +184,8 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof) {
     CR(B(0));
     CR(b200i_embed(m->tok_embd, c.d_model, c.vocab, m->st, m->x, s));
     CR(E());
+    const size_t qbytes = (size_t)m->hq * D * sizeof(float);
+    if (dump) CK(cudaMemcpyAsync(dump->x, m->x, c.d_model * sizeof(float), cudaMemcpyDeviceToDevice, s));
     for (int l = 0; l < c.n_layer; ++l) {
         const Layer& Ly = m->L[l];
         GemvArgs a;
@@ -224,9 +232,12 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof) {
         f.part_o = reinterpret_cast<float*>(ws + m->fa.off_o);
         f.part_ml = reinterpret_cast<float*>(ws + m->fa.off_ml);
         f.tickets = reinterpret_cast<unsigned int*>(ws + m->fa.off_tickets);
+        if (dump) CK(cudaMemcpyAsync(dump->q + (size_t)l * m->hq * D, m->q, qbytes, cudaMemcpyDeviceToDevice, s));
         CR(B(2));
         CR(b200i_fa(f, D, s));
         CR(E());
+        if (dump)
+            CK(cudaMemcpyAsync(dump->att + (size_t)l * m->hq * D, m->att, qbytes, cudaMemcpyDeviceToDevice, s));
 
         std::memset(&a, 0, sizeof(a));
         a.w = Ly.wo;
@@ -287,6 +298,9 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof) {
             CR(allreduce_sum(m, m->part, m->x, c.d_model, s));
             CR(E());
         }
+        if (dump)
+            CK(cudaMemcpyAsync(dump->x + (size_t)(l + 1) * c.d_model, m->x, c.d_model * sizeof(float),
+                               cudaMemcpyDeviceToDevice, s));
     }
     GemvArgs a;
     std::memset(&a, 0, sizeof(a));
@@ -590,6 +604,40 @@ int b200_model_step_bytes(b200_model* m, int ctx, uint64_t* bytes) {
     b += (uint64_t)q4_bytes(m->voc, c.d_model) + (uint64_t)c.d_model * 4 + (uint64_t)(c.d_model / 32) * 18;
     *bytes = b;
     return B200_OK;
+}
+
+int b200_model_debug_step(b200_model* m, int token, int pos, float* x_host, float* q_host, float* att_host) {
+    if (!m || !x_host || pos < 0 || pos >= m->c.kv_size || token < 0 || token >= m->c.vocab) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    CR(b200i_prepare_device());
+    const b200_llama_config& c = m->c;
+    const size_t nx = (size_t)(c.n_layer + 1) * c.d_model, nq = (size_t)c.n_layer * m->hq * c.head_dim;
+    Dump d;
+    CK(cudaMalloc(&d.x, nx * sizeof(float)));
+    cudaError_t e1 = cudaMalloc(&d.q, nq * sizeof(float));
+    cudaError_t e2 = cudaMalloc(&d.att, nq * sizeof(float));
+    int rc = (e1 == cudaSuccess && e2 == cudaSuccess) ? B200_OK : B200_ENOMEM;
+    if (rc == B200_OK) {
+        m->h_st->token = token;
+        m->h_st->pos = pos;
+        m->h_st->ctx = pos + 1;
+        m->h_st->advance = 0;
+        if (cudaMemcpyAsync(m->st, m->h_st, 4 * sizeof(int), cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
+            rc = B200_ECUDA;
+    }
+    if (rc == B200_OK) rc = enqueue_step(m, m->stream, nullptr, &d);
+    if (rc == B200_OK && cudaStreamSynchronize(m->stream) != cudaSuccess) rc = B200_ECUDA;
+    if (rc == B200_OK && cudaMemcpy(x_host, d.x, nx * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = B200_ECUDA;
+    if (rc == B200_OK && q_host && cudaMemcpy(q_host, d.q, nq * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = B200_ECUDA;
+    if (rc == B200_OK && att_host &&
+        cudaMemcpy(att_host, d.att, nq * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = B200_ECUDA;
+    cudaFree(d.x);
+    if (d.q) cudaFree(d.q);
+    if (d.att) cudaFree(d.att);
+    return rc;
 }
 
 int b200_model_profile(b200_model* m, int iters, float* us) {

@@ -70,6 +70,7 @@ def _lib():
             "b200_model_stream": (P, [P]),
             "b200_model_step_bytes": (C.c_int, [P, C.c_int, C.POINTER(C.c_uint64)]),
             "b200_model_profile": (C.c_int, [P, C.c_int, P]),
+            "b200_model_debug_step": (C.c_int, [P, C.c_int, C.c_int, P, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -169,6 +170,19 @@ class DecodeModel:
         v = C.c_uint64(0)
         B._check(_lib().b200_model_step_bytes(self.h, ctx, C.byref(v)), "step_bytes")
         return int(v.value)
+
+    def debug_step(self, token: int, pos: int):
+        """Layer dump of one eager step: x after embedding and after every
+        layer [(L+1), d], roped q [L, Hq*D] and attention output [L, Hq*D]."""
+        c = self.cfg
+        hqd = c.n_head // self.tp_world * c.head_dim
+        x = np.empty((c.n_layer + 1, c.d_model), np.float32)
+        q = np.empty((c.n_layer, hqd), np.float32)
+        a = np.empty((c.n_layer, hqd), np.float32)
+        B._check(_lib().b200_model_debug_step(self.h, token, pos, x.ctypes.data_as(C.c_void_p),
+                                              q.ctypes.data_as(C.c_void_p), a.ctypes.data_as(C.c_void_p)),
+                 "debug_step")
+        return x, q, a
 
     def profile(self, iters: int = 3) -> dict:
         us = (C.c_float * 8)()

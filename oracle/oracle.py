@@ -77,6 +77,7 @@ def _declare(L):
         "ref_rope_norm": (None, [P, I32, I32, I32, C.c_float]),
         "ref_argmax": (I64, [P, I64]),
         "ref_llama_step": (I64, [P, C.c_int32, C.c_int32, P, P, I32, I32, I32, I32]),
+        "ref_set_accum_mode": (None, [I32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

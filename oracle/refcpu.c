@@ -185,6 +185,14 @@ int32_t ref_dot_block_q8_0_q8_0(const ref_block_q8_0 *w, const ref_block_q8_0 *x
 
 /* ----------------------------------------------------------------- mul_mat */
 
+/* Accumulation order of the block-dot sums in the quantised MUL_MATs:
+ * 0 = fp64 accumulator (default), 1 = fp32 sequential accumulator.  Both are
+ * valid ggml-cpu semantics (ggml's own order depends on the SIMD width); the
+ * switch exists to measure how far two valid orders drift apart downstream of
+ * the discontinuous Q8_0 activation quantisation. */
+static int g_accum_mode = 0;
+void ref_set_accum_mode(int mode) { g_accum_mode = mode; }
+
 static int pick_threads(int nthreads) {
 #ifdef _OPENMP
     return nthreads > 0 ? nthreads : omp_get_max_threads();
@@ -229,11 +237,15 @@ void ref_mul_mat_q4_0(const void *wv, const float *x, float *y, int64_t n, int64
         for (int64_t r = 0; r < n; ++r) {
             const ref_block_q4_0 *row = w + r * nb;
             double acc = 0.0;
+            float accf = 0.0f;
             for (int64_t b = 0; b < nb; ++b) {
                 const int32_t s = ref_dot_block_q4_0_q8_0(row + b, xq + b);
-                acc += (double)(h2f(row[b].d) * xd[b]) * (double)s;
+                if (g_accum_mode == 0)
+                    acc += (double)(h2f(row[b].d) * xd[b]) * (double)s;
+                else
+                    accf += (h2f(row[b].d) * xd[b]) * (float)s;
             }
-            y[r] = (float)acc;
+            y[r] = g_accum_mode == 0 ? (float)acc : accf;
         }
         free(xd);
         free(xq);

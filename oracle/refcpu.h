@@ -59,6 +59,9 @@ void ref_dequantize_q4_0(const ref_block_q4_0 *x, float *y, int64_t k);
 int32_t ref_dot_block_q4_0_q8_0(const ref_block_q4_0 *w, const ref_block_q8_0 *x);
 int32_t ref_dot_block_q8_0_q8_0(const ref_block_q8_0 *w, const ref_block_q8_0 *x);
 
+/* 0: fp64 block-sum accumulator (default); 1: fp32 sequential. */
+void ref_set_accum_mode(int mode);
+
 /* ---- MUL_MAT, M = 1: W rows n contiguous along K; y[n] = sum_k W[n,k] x[k] ---- */
 void ref_mul_mat_f16(const uint16_t *w, const float *x, float *y, int64_t n, int64_t k, int nthreads);
 /* mode 0: ggml-cpu semantics (x -> Q8_0, integer block dots)
