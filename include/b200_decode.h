@@ -58,16 +58,18 @@ int b200_device_status(unsigned int *status, int reset);
  * (ggml_cann_310b_nz_offset/size patch:1551-1562, set_tensor NZ branch
  * patch:1768-1806, get_alloc_size patch:1810-1846, aclnnTransMatmulWeight).
  *
- * The packed layout is a sequence of tiles of R rows x the full K.  A tile is
- * contiguous and a multiple of 16 bytes so the GEMV streams it with one bulk
- * copy.  Inside a tile:
- *   F16 : w[R][K] halves (identical to ggml rows; only the last tile is padded)
- *   Q4_0: qs[R][K/32][16 bytes] then d[R][K/32] f16
- *   Q8_0: qs[R][K/32][bytes 0..15], qs[R][K/32][bytes 16..31], d[R][K/32] f16
- * Rows past n in the last tile are zero.
+ * Packed rows are contiguous (row r at r * row_stride).  Inside a row, with
+ * U = K/32 blocks (Q4_0, Q8_0) or U = K/8 units of 8 halves (F16):
+ *   F16 : K halves, identical to the ggml row           row_stride = 2K
+ *   Q4_0: nibbles qs[U][16], then scales d[U] (f16)      row_stride = 16U + pad16(2U)
+ *   Q8_0: quant bytes 0..15 [U][16], bytes 16..31
+ *         [U][16], then d[U] (f16)                       row_stride = 32U + pad16(2U)
+ * Scale planes are zero-padded to 16 bytes.  Each plane of a row chunk is one
+ * 16-byte-aligned bulk copy, and 32 lanes reading 32 consecutive blocks issue
+ * conflict-free 16-byte shared-memory loads.
  * ---------------------------------------------------------------------- */
-int64_t b200_packed_rows_per_tile(int type, int64_t n, int64_t k);
-size_t b200_packed_size(int type, int64_t n, int64_t k); /* 0 when unsupported */
+int64_t b200_packed_row_stride(int type, int64_t n, int64_t k); /* 0 when unsupported */
+size_t b200_packed_size(int type, int64_t n, int64_t k);        /* 0 when unsupported */
 /* src: ggml rows (n rows of k elements, row stride = ggml_row_size) on the device. */
 int b200_repack(int type, const void *src, void *dst, int64_t n, int64_t k, b200_stream_t stream);
 /* Packs 2*n_each rows: packed row 2i is src_even row i, 2i+1 is src_odd row i

@@ -72,7 +72,7 @@ def _declare(L):
         "b200_version": (C.c_char_p, []),
         "b200_strerror": (C.c_char_p, [C.c_int]),
         "b200_device_status": (C.c_int, [C.POINTER(C.c_uint), C.c_int]),
-        "b200_packed_rows_per_tile": (I64, [C.c_int, I64, I64]),
+        "b200_packed_row_stride": (I64, [C.c_int, I64, I64]),
         "b200_packed_size": (C.c_size_t, [C.c_int, I64, I64]),
         "b200_repack": (C.c_int, [C.c_int, P, P, I64, I64, P]),
         "b200_repack_interleave2": (C.c_int, [C.c_int, P, P, P, I64, I64, P]),
@@ -128,8 +128,8 @@ def packed_size(wtype: int, n: int, k: int) -> int:
     return int(lib().b200_packed_size(wtype, n, k))
 
 
-def rows_per_tile(wtype: int, n: int, k: int) -> int:
-    return int(lib().b200_packed_rows_per_tile(wtype, n, k))
+def row_stride(wtype: int, n: int, k: int) -> int:
+    return int(lib().b200_packed_row_stride(wtype, n, k))
 
 
 class PackedWeight:

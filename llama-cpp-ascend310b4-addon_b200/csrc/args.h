@@ -20,57 +20,106 @@ enum GemvFmt { FMT_F16 = 0, FMT_Q4 = 1, FMT_Q4W = 2, FMT_Q8 = 3 };
 enum GemvPro { PRO_PLAIN = 0, PRO_RMSNORM = 1 };
 enum GemvEpi { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_ARGMAX = 4 };
 
-constexpr int kGemvThreads = 256;
-constexpr int64_t kTileTarget = 32768;  // preferred tile bytes
-constexpr int64_t kTileMax = 65536;     // largest tile one stage may hold
-constexpr int kMaxR = 32;
-constexpr int kMaxSlots = 8;            // kGemvThreads / 32
+constexpr int kGemvWarps = 16;              // warps per CTA; each runs its own copy ring
+constexpr int kGemvThreads = 32 * kGemvWarps;
+constexpr int kGemvStagesMax = 4;           // copy-ring depth per warp
+constexpr int64_t kGemvSmemBudget = 200 * 1024;
 
+// Packed layout: rows are contiguous, row r at r * rs.  Inside a row:
+//   F16 : K halves                                       rs = 2K
+//   Q4_0: qs[U][16 bytes], then d[U] f16 padded to 16     rs = 16U + pad16(2U)
+//   Q8_0: qs bytes 0..15 [U][16], bytes 16..31 [U][16],
+//         then d[U] f16 padded to 16                      rs = 32U + pad16(2U)
+// (U = K/8 units of 8 halves for F16, K/32 blocks for Q4_0/Q8_0.)  Planes
+// are split so that 32 lanes reading consecutive units issue conflict-free
+// 16-byte shared-memory loads, and every plane start is 16-byte aligned for
+// the bulk copies.
+//
+// A warp streams its rows in chunks: a chunk is either units [u0, u0+kc) of
+// one row (rpc == 1; one bulk copy per plane) or rpc whole consecutive rows
+// when rows are short (one bulk copy).  Inside a staged chunk, unit i of a
+// row sits at 16 i in plane 0, 16 pw + 16 i in plane 1 (Q8_0), and the scale
+// at (Q8_0: 32 pw, Q4_0: 16 pw) + 2 i, where pw = kc (rpc == 1) or U.
 struct GemvPlan {
     int type;
     int64_t n, k;
-    int U;             // units per row: 8 halves (F16) or one 32-block (Q4_0/Q8_0)
-    int64_t rowbytes;  // packed bytes per row
-    int R;             // rows per tile
-    int64_t tile_bytes;
-    int64_t ntiles;
+    int U;              // units per row
+    int ub;             // bytes per unit (16, 18, 34)
+    int64_t rs;         // packed row stride
+    int rpc;            // rows per chunk
+    int kc;             // units per chunk row (== U when rpc > 1)
+    int nchunk;         // chunks per row (1 when rpc > 1)
+    int tpr;            // lanes per row (32 / rpc)
+    int upl;            // units per lane per chunk row
+    int64_t stage_bytes;
 };
 
 B200_HD inline int64_t pad16(int64_t v) { return (v + 15) & ~int64_t(15); }
+
+B200_HD inline int64_t gemv_stage_bytes_rpc1(int type, int kc) {
+    if (type == B200_TYPE_F16) return 16 * (int64_t)kc;
+    if (type == B200_TYPE_Q4_0) return 16 * (int64_t)kc + pad16(2 * (int64_t)kc);
+    return 32 * (int64_t)kc + pad16(2 * (int64_t)kc);
+}
 
 B200_HD inline bool make_plan(int type, int64_t n, int64_t k, GemvPlan* p) {
     if (n <= 0 || k <= 0) return false;
     p->type = type;
     p->n = n;
     p->k = k;
+    int kc_max;
     if (type == B200_TYPE_F16) {
         if (k % 8) return false;
         p->U = (int)(k / 8);
-        p->rowbytes = 2 * k;
+        p->ub = 16;
+        p->rs = 2 * k;
+        kc_max = 256;
     } else if (type == B200_TYPE_Q4_0) {
         if (k % 32) return false;
         p->U = (int)(k / 32);
-        p->rowbytes = k / 2 + k / 16;
+        p->ub = 18;
+        p->rs = 16 * (int64_t)p->U + pad16(2 * (int64_t)p->U);
+        kc_max = 128;
     } else if (type == B200_TYPE_Q8_0) {
         if (k % 32) return false;
         p->U = (int)(k / 32);
-        p->rowbytes = k + k / 16;
+        p->ub = 34;
+        p->rs = 32 * (int64_t)p->U + pad16(2 * (int64_t)p->U);
+        kc_max = 128;
     } else {
         return false;
     }
-    int R = kMaxR;
-    while (R > 1 && R * p->rowbytes > kTileTarget) R >>= 1;
-    p->R = R;
-    p->tile_bytes = pad16(R * p->rowbytes);
-    if (p->tile_bytes > kTileMax) return false;
-    p->ntiles = (n + R - 1) / R;
+    if (k > (int64_t)1 << 24) return false;
+    const int U = p->U;
+    if (U >= 64) {
+        p->rpc = 1;
+        p->tpr = 32;
+        p->nchunk = (U + kc_max - 1) / kc_max;
+        int kc = (U + p->nchunk - 1) / p->nchunk;
+        kc = (kc + 7) & ~7;  // chunk starts keep the scale plane 16-byte aligned
+        p->kc = kc;
+        p->nchunk = (U + kc - 1) / kc;
+        p->upl = (kc + 31) / 32;
+        p->stage_bytes = gemv_stage_bytes_rpc1(type, kc);
+    } else {
+        int rpc = 32;
+        while (rpc > 1 && rpc * U > 128) rpc >>= 1;
+        p->rpc = rpc;
+        p->tpr = 32 / rpc;
+        p->kc = U;
+        p->nchunk = 1;
+        p->upl = (U + p->tpr - 1) / p->tpr;
+        p->stage_bytes = rpc * p->rs;
+    }
     return true;
 }
 
+B200_HD inline int64_t gemv_packed_bytes(const GemvPlan& p) { return p.n * p.rs; }
+
 struct GemvArgs {
     const uint8_t* w;
-    int64_t tile_bytes, ntiles;
-    int R, RG, U, stages;
+    GemvPlan p;
+    int stages;
     int64_t n, k;
     // prologue
     const float* x;

@@ -20,7 +20,12 @@ __global__ void __launch_bounds__(kFaThreads) fa_decode_kernel(const FaArgs a) {
     constexpr int NW = kFaThreads / 32;
     __shared__ __align__(16) float qs[kFaMaxG][D];
     __shared__ float sc[kFaMaxG][kFaChunk];
-    __shared__ float red[NW][kFaMaxG][D];
+    // Cross-warp reduction buffer [NW][kFaMaxG][D]; reused by the merging CTA
+    // for the split weights [kFaMaxG][kFaTargetCtas].
+    constexpr int kRed = NW * kFaMaxG * D > kFaMaxG * kFaTargetCtas ? NW * kFaMaxG * D : kFaMaxG * kFaTargetCtas;
+    __shared__ float redbuf[kRed];
+    auto red = reinterpret_cast<float (*)[kFaMaxG][D]>(redbuf);
+    auto wts = reinterpret_cast<float (*)[kFaTargetCtas]>(redbuf);
     __shared__ float m_run[kFaMaxG], l_run[kFaMaxG], alpha[kFaMaxG];
     __shared__ int is_last;
 
@@ -196,7 +201,8 @@ __global__ void __launch_bounds__(kFaThreads) fa_decode_kernel(const FaArgs a) {
     __threadfence();
 
     const int n_act = (nchunks_ctx + a.chunks_per_split - 1) / a.chunks_per_split;
-    // weights w_s = exp(m_s - M) per head, kept in sc[h][*] when they fit.
+    // Merge: w[h][s] = exp(m_s - M_h) / L_h computed once into shared memory,
+    // then every (head, dim) output is an unrolled dot over the splits.
     for (int h = warp; h < hn; h += NW) {
         float M = -INFINITY;
         for (int s = lane; s < n_act; s += 32) M = fmaxf(M, __ldcg(&a.part_ml[((int64_t)s * a.Hq + h0 + h) * 2]));
@@ -205,27 +211,30 @@ __global__ void __launch_bounds__(kFaThreads) fa_decode_kernel(const FaArgs a) {
         for (int s = lane; s < n_act; s += 32) {
             const float ms = __ldcg(&a.part_ml[((int64_t)s * a.Hq + h0 + h) * 2]);
             const float ls = __ldcg(&a.part_ml[((int64_t)s * a.Hq + h0 + h) * 2 + 1]);
-            L += ms == -INFINITY ? 0.f : ls * expf(ms - M);
+            const float e = (ms == -INFINITY) ? 0.f : expf(ms - M);
+            wts[h][s] = e;
+            L += ls * e;
         }
         L = warp_sum(L);
-        if (lane == 0) {
-            m_run[h] = M;
-            l_run[h] = (L > 0.f) ? 1.0f / L : 0.f;
-        }
+        const float inv = (L > 0.f) ? 1.0f / L : 0.f;
+        __syncwarp();
+        for (int s = lane; s < n_act; s += 32) wts[h][s] *= inv;
     }
     __syncthreads();
     for (int idx = tid; idx < hn * D; idx += kFaThreads) {
         const int h = idx / D, d = idx - (idx / D) * D;
-        const float M = m_run[h];
-        float o = 0.f;
-        if (M != -INFINITY) {
-            for (int s = 0; s < n_act; ++s) {
-                const float ms = __ldcg(&a.part_ml[((int64_t)s * a.Hq + h0 + h) * 2]);
-                if (ms == -INFINITY) continue;
-                o = fmaf(__ldcg(&a.part_o[((int64_t)s * a.Hq + h0 + h) * D + d]), expf(ms - M), o);
-            }
+        const float* po = a.part_o + (int64_t)(h0 + h) * D + d;
+        const int64_t stride = (int64_t)a.Hq * D;
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+        int s = 0;
+        for (; s + 4 <= n_act; s += 4) {
+            o0 = fmaf(__ldcg(po + (int64_t)(s + 0) * stride), wts[h][s + 0], o0);
+            o1 = fmaf(__ldcg(po + (int64_t)(s + 1) * stride), wts[h][s + 1], o1);
+            o2 = fmaf(__ldcg(po + (int64_t)(s + 2) * stride), wts[h][s + 2], o2);
+            o3 = fmaf(__ldcg(po + (int64_t)(s + 3) * stride), wts[h][s + 3], o3);
         }
-        a.out[(int64_t)(h0 + h) * D + d] = o * l_run[h];
+        for (; s < n_act; ++s) o0 = fmaf(__ldcg(po + (int64_t)s * stride), wts[h][s], o0);
+        a.out[(int64_t)(h0 + h) * D + d] = (o0 + o1) + (o2 + o3);
     }
 }
 

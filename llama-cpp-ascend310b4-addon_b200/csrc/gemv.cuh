@@ -1,19 +1,23 @@
-// gemv.cuh -- M=1 matrix-vector kernels streamed from the packed tile layout.
+// gemv.cuh -- M=1 matrix-vector kernels streamed from the packed row layout.
 //
-// One persistent CTA per SM owns a contiguous range of tiles (R rows x K).
-// Thread 0 keeps `stages` tiles in flight with cp.async.bulk into a shared
-// memory ring (one mbarrier per stage, bounded waits); the 256 threads hold
-// their slice of the activation in registers for the whole kernel, so every
-// byte of weight is read from HBM once and from shared memory once.
+// Structure (one CTA per SM, 16 warps):
+//   * prologue: the CTA turns x into the form the dot needs, once, in shared
+//     memory -- Q8_0 blocks (ggml quantize_row_q8_0_ref rule) for Q4_0/Q8_0
+//     weights, f16-rounded values for F16 weights and the W4A16 mode --
+//     optionally fusing RMSNorm * weight;
+//   * main loop: every warp owns a contiguous range of rows and streams them
+//     through its own ring of shared-memory stages with cp.async.bulk
+//     (lane 0 issues, an mbarrier per stage, bounded waits).  Warps never
+//     synchronise with each other after the prologue, so the memory system
+//     always has ~16 x stages x chunk bytes in flight per SM;
+//   * lanes split a row's units; a row's sum is a warp (or lane-group)
+//     reduction, and the epilogue (store, residual add, SwiGLU pair,
+//     RoPE + KV-cache write, argmax) runs on the lane that holds it.
 //
-// Activation handling follows ggml-cpu's MUL_MAT vec_dot_type conversion:
-//   F16  : x -> f16, fp32 FMA over f16 products
-//   Q4_0 : x -> Q8_0 blocks (quantize_row_q8_0_ref rule), dp4a integer block
-//          dots, fp32 sum of d_w * d_x * dot (ggml mode), or x -> f16 and an
-//          fp32 FMA over dequantised nibbles (W4A16 mode)
-//   Q8_0 : x -> Q8_0 blocks, dp4a block dots
-// Prologues fuse RMSNorm * weight; epilogues fuse the residual add, SwiGLU,
-// RoPE + KV-cache write, and argmax (the decode neighbours of MUL_MAT).
+// Arithmetic follows ggml-cpu's MUL_MAT with src1 converted to the weight's
+// vec_dot_type: F16 -> fp32 FMA over f16 products; Q4_0/Q8_0 -> integer
+// dp4a block dots, fp32 sum of d_w * d_x * dot; W4A16 -> fp32 FMA over
+// dequantised nibbles and f16-rounded x.
 #pragma once
 
 #include "args.h"
@@ -27,6 +31,8 @@ __device__ __forceinline__ unsigned int float_key(float f) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+// (value, index) packed so that a larger value wins and, on ties, the
+// smaller index wins (ggml_argmax returns the first maximum).
 __device__ __forceinline__ unsigned long long pack_argmax(float v, int64_t idx) {
     return ((unsigned long long)float_key(v) << 32) | (unsigned long long)(0xffffffffu - (unsigned int)idx);
 }
@@ -72,57 +78,216 @@ __device__ __forceinline__ void store_block_q8_0(uint8_t* dst, uint16_t dh, cons
     }
 }
 
-template <int FMT>
-struct MaxNU {
-    static constexpr int value = FMT == FMT_Q4W ? 2 : 8;
-};
-
-// Chooses the number of row groups for a launch: the largest power of two
-// that divides R and keeps every thread at <= MAXNU units.
-inline int choose_row_groups(const GemvPlan& p, int maxnu) {
-    for (int rg = 32; rg >= 1; rg >>= 1) {
-        if (rg > p.R || p.R % rg) continue;
-        const int tpr = kGemvThreads / rg;
-        if ((p.U + tpr - 1) / tpr <= maxnu) return rg;
-    }
-    return 0;
+// Bytes of the activation region at the start of shared memory.
+B200_HD inline int64_t gemv_x_bytes(int fmt, const GemvPlan& p) {
+    if (fmt == FMT_Q4 || fmt == FMT_Q8) return pad16(40 * (int64_t)p.U);  // xq[U][32] + {d, sum}[U]
+    return pad16(2 * p.k);                                                // f16 x[K]
 }
 
-template <int FMT, int MAXNU, bool DEBUG>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int S = a.stages;
-    uint8_t* ring = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (int64_t)S * a.tile_bytes);
-    float* part = reinterpret_cast<float*>(full + S);  // [2][kMaxR][kMaxSlots]
-    float* red = part + 2 * kMaxR * kMaxSlots;         // [32]
+// ------------------------------------------------------------- epilogues
 
-    const int tid = threadIdx.x;
-    const int TPR = kGemvThreads / a.RG;
-    const int g = tid / TPR;
-    const int j = tid - g * TPR;
-    const int nslot = TPR > 32 ? TPR / 32 : 1;
-    const int slot = TPR > 32 ? (j >> 5) : 0;
-    const int R = a.R, U = a.U;
+__device__ __forceinline__ void epi_row(const GemvArgs& a, int64_t n, float v, unsigned long long& best) {
+    if (a.epi == EPI_STORE) {
+        a.y[n] = v;
+    } else if (a.epi == EPI_ADD) {
+        a.y[n] = __fadd_rn(v, a.res[n]);
+    } else if (a.epi == EPI_ARGMAX) {
+        a.y[n] = v;
+        const unsigned long long k = pack_argmax(v, n + a.row_offset);
+        best = k > best ? k : best;
+    }
+}
 
-    const int64_t G = gridDim.x;
-    const int64_t t0 = (int64_t)blockIdx.x * a.ntiles / G;
-    const int64_t t1 = (int64_t)(blockIdx.x + 1) * a.ntiles / G;
-    const int nt = (int)(t1 - t0);
-    const uint32_t tb = (uint32_t)a.tile_bytes;
-
-    if (tid == 0) {
-        for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
-        mbar_fence_init();
-        for (int s = 0; s < S && s < nt; ++s) {
-            mbar_arrive_expect_tx(&full[s], tb);
-            bulk_g2s(ring + (int64_t)s * tb, a.w + (t0 + s) * a.tile_bytes, tb, &full[s]);
+// Rows n (even) and n + 1.
+__device__ __forceinline__ void epi_pair(const GemvArgs& a, int64_t n, float v0, float v1) {
+    if (a.epi == EPI_SWIGLU) {
+        // ggml swiglu: silu(g) * u with silu(g) = g / (1 + exp(-g))
+        const float sg = __fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0)));
+        a.y[n / 2] = __fmul_rn(sg, v1);
+    } else if (a.epi == EPI_QKV) {
+        const int pos = *a.pos;
+        if (n < a.nq + a.nkv) {
+            // ggml rope, NORM mode: theta_i = pos * theta_scale^i, built by
+            // repeated fp32 multiplication as ggml_rope_cache_init does.
+            const int local = (int)(n < a.nq ? n : n - a.nq);
+            const int i0 = local % a.head_dim;
+            float theta = (float)pos;
+            for (int t = 0; t < i0 / 2; ++t) theta = __fmul_rn(theta, a.theta_scale);
+            float sn, cs;
+            sincosf(theta, &sn, &cs);
+            const float r0 = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
+            const float r1 = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cs));
+            if (n < a.nq) {
+                a.y[n] = r0;
+                a.y[n + 1] = r1;
+            } else {
+                uint16_t* kr = a.kc + (int64_t)pos * a.nkv + local;
+                kr[0] = f2h(r0);
+                kr[1] = f2h(r1);
+            }
+        } else {
+            const int local = (int)(n - a.nq - a.nkv);
+            uint16_t* vr = a.vc + (int64_t)pos * a.nkv + local;
+            vr[0] = f2h(v0);
+            vr[1] = f2h(v1);
         }
     }
+}
 
-    // ---- prologue: RMSNorm scale (optional) ----
+// ------------------------------------------------------------ unit dots
+
+// Contribution of one unit: `row` is the staged chunk row, `pw` its plane
+// width, `i` the unit's index in the chunk row, `u` its index in the full row.
+template <int FMT, bool DEBUG>
+__device__ __forceinline__ float unit_dot(const uint8_t* row, int pw, int i, int u, const uint8_t* xr,
+                                          int32_t* dots, int64_t nrow, int U) {
+    if constexpr (FMT == FMT_F16) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(row + 16 * i);
+        const uint4 xv = *reinterpret_cast<const uint4*>(xr + 16 * u);
+        const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+        const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 wf = __half22float2(wh[e]);
+            const float2 xf = __half22float2(xh[e]);
+            acc = fmaf(wf.x, xf.x, acc);
+            acc = fmaf(wf.y, xf.y, acc);
+        }
+        return acc;
+    } else if constexpr (FMT == FMT_Q4W) {
+        const uint4 qv = *reinterpret_cast<const uint4*>(row + 16 * i);
+        const float dw = h2f(*reinterpret_cast<const uint16_t*>(row + 16 * pw + 2 * i));
+        const uint4* x4 = reinterpret_cast<const uint4*>(xr + 64 * u);
+        const unsigned int wq[4] = {qv.x, qv.y, qv.z, qv.w};
+        float p = 0.f;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {  // elements 0..15 (low nibbles), then 16..31 (high nibbles)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const uint4 xv = x4[hf * 2 + e];
+                const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float2 xf = __half22float2(xh[t]);
+                    const int j = e * 8 + t * 2;  // element index within the half
+                    const unsigned int w = wq[j >> 2];
+                    const int sh = 8 * (j & 3) + 4 * hf;
+                    const int q0 = (int)((w >> sh) & 0xfu) - 8;
+                    const int q1 = (int)((w >> (sh + 8)) & 0xfu) - 8;
+                    p = fmaf((float)q0, xf.x, p);
+                    p = fmaf((float)q1, xf.y, p);
+                }
+            }
+        }
+        return dw * p;
+    } else {
+        const int4* xq = reinterpret_cast<const int4*>(xr + 32 * u);
+        const int4 xa = xq[0], xb = xq[1];
+        const int2 ds = reinterpret_cast<const int2*>(xr + 32 * U)[u];
+        const float xd = __int_as_float(ds.x);
+        int sumi = 0;
+        float dw;
+        if constexpr (FMT == FMT_Q4) {
+            const uint4 qv = *reinterpret_cast<const uint4*>(row + 16 * i);
+            dw = h2f(*reinterpret_cast<const uint16_t*>(row + 16 * pw + 2 * i));
+            sumi = dp4a((int)(qv.x & 0x0f0f0f0fu), xa.x, sumi);
+            sumi = dp4a((int)(qv.y & 0x0f0f0f0fu), xa.y, sumi);
+            sumi = dp4a((int)(qv.z & 0x0f0f0f0fu), xa.z, sumi);
+            sumi = dp4a((int)(qv.w & 0x0f0f0f0fu), xa.w, sumi);
+            sumi = dp4a((int)((qv.x >> 4) & 0x0f0f0f0fu), xb.x, sumi);
+            sumi = dp4a((int)((qv.y >> 4) & 0x0f0f0f0fu), xb.y, sumi);
+            sumi = dp4a((int)((qv.z >> 4) & 0x0f0f0f0fu), xb.z, sumi);
+            sumi = dp4a((int)((qv.w >> 4) & 0x0f0f0f0fu), xb.w, sumi);
+            sumi -= 8 * ds.y;  // nibbles are stored +8
+        } else {
+            const uint4 lo = *reinterpret_cast<const uint4*>(row + 16 * i);
+            const uint4 hi = *reinterpret_cast<const uint4*>(row + 16 * pw + 16 * i);
+            dw = h2f(*reinterpret_cast<const uint16_t*>(row + 32 * pw + 2 * i));
+            sumi = dp4a((int)lo.x, xa.x, sumi);
+            sumi = dp4a((int)lo.y, xa.y, sumi);
+            sumi = dp4a((int)lo.z, xa.z, sumi);
+            sumi = dp4a((int)lo.w, xa.w, sumi);
+            sumi = dp4a((int)hi.x, xb.x, sumi);
+            sumi = dp4a((int)hi.y, xb.y, sumi);
+            sumi = dp4a((int)hi.z, xb.z, sumi);
+            sumi = dp4a((int)hi.w, xb.w, sumi);
+        }
+        if constexpr (DEBUG) dots[nrow * U + u] = sumi;
+        return (dw * xd) * (float)sumi;
+    }
+}
+
+// ------------------------------------------------------------ the kernel
+
+template <int FMT, bool DEBUG>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvPlan& P = a.p;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int S = a.stages;
+    const int64_t xbytes = gemv_x_bytes(FMT, P);
+    uint8_t* xr = smem;
+    uint8_t* rings = smem + xbytes;
+    uint8_t* ring = rings + (int64_t)warp * S * P.stage_bytes;
+    uint64_t* bars_all = reinterpret_cast<uint64_t*>(rings + (int64_t)kGemvWarps * S * P.stage_bytes);
+    uint64_t* bars = bars_all + warp * S;
+    float* red = reinterpret_cast<float*>(bars_all + kGemvWarps * S);  // [kGemvWarps]
+
+    // ---- this warp's rows ----
+    const bool pair = a.epi == EPI_SWIGLU || a.epi == EPI_QKV;
+    const int64_t item_rows = P.rpc > 1 ? P.rpc : (pair ? 2 : 1);
+    const int64_t items = (P.n + item_rows - 1) / item_rows;
+    const int64_t gw = (int64_t)blockIdx.x * kGemvWarps + warp, ngw = (int64_t)gridDim.x * kGemvWarps;
+    const int64_t it0 = gw * items / ngw, it1 = (gw + 1) * items / ngw;
+    const int64_t row_begin = it0 * item_rows;
+    const int64_t row_end = min(it1 * item_rows, P.n);
+    const int64_t nq = P.rpc > 1 ? (it1 - it0) : (row_end - row_begin) * P.nchunk;
+
+    // Lane 0 only: stage chunk q into ring slot s.
+    auto issue = [&](int64_t q, int s) {
+        uint8_t* dst = ring + (int64_t)s * P.stage_bytes;
+        uint64_t* bar = &bars[s];
+        if (P.rpc > 1) {
+            const int64_t r0 = row_begin + q * P.rpc;
+            const int64_t nr = min((int64_t)P.rpc, P.n - r0);
+            const uint32_t bytes = (uint32_t)(nr * P.rs);
+            mbar_arrive_expect_tx(bar, bytes);
+            bulk_g2s(dst, a.w + r0 * P.rs, bytes, bar);
+        } else {
+            const int64_t row = row_begin + q / P.nchunk;
+            const int u0 = (int)(q % P.nchunk) * P.kc;
+            const int nu = min(P.kc, P.U - u0);
+            const uint8_t* base = a.w + row * P.rs;
+            const uint32_t b0 = (uint32_t)(16 * nu);
+            if constexpr (FMT == FMT_F16) {
+                mbar_arrive_expect_tx(bar, b0);
+                bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
+            } else if constexpr (FMT == FMT_Q8) {
+                const uint32_t b1 = (uint32_t)pad16(2 * nu);
+                mbar_arrive_expect_tx(bar, 2 * b0 + b1);
+                bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
+                bulk_g2s(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 16 * (int64_t)u0, b0, bar);
+                bulk_g2s(dst + 32 * P.kc, base + 32 * (int64_t)P.U + 2 * (int64_t)u0, b1, bar);
+            } else {
+                const uint32_t b1 = (uint32_t)pad16(2 * nu);
+                mbar_arrive_expect_tx(bar, b0 + b1);
+                bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
+                bulk_g2s(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 2 * (int64_t)u0, b1, bar);
+            }
+        }
+    };
+
+    if (lane == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+        mbar_fence_init();
+        for (int s = 0; s < S && s < nq; ++s) issue(s, s);
+    }
+
+    // ---- prologue: the activation, once per CTA, into shared memory ----
     float nscale = 1.f;
-    if (a.pro == PRO_RMSNORM) {
+    const bool norm = a.pro == PRO_RMSNORM;
+    if (norm) {
         float ss = 0.f;
         const float4* x4 = reinterpret_cast<const float4*>(a.x);
         for (int64_t i = tid; i < a.k / 4; i += kGemvThreads) {
@@ -133,69 +298,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             ss = fmaf(v.w, v.w, ss);
         }
         ss = warp_sum(ss);
-        if ((tid & 31) == 0) red[tid >> 5] = ss;
-    }
-    __syncthreads();  // barrier init visible; norm partials ready
-    if (a.pro == PRO_RMSNORM) {
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < kGemvThreads / 32; ++w) tot += red[w];
+        for (int w = 0; w < kGemvWarps; ++w) tot += red[w];
         const float mean = __fdiv_rn(tot, (float)a.k);
         nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
     }
-
-    // ---- activation slice into registers ----
-    float xf[(FMT == FMT_F16) ? MAXNU * 8 : (FMT == FMT_Q4W ? MAXNU * 32 : 1)];
-    int xq[(FMT == FMT_Q4 || FMT == FMT_Q8) ? MAXNU * 8 : 1];
-    float xd[(FMT == FMT_Q4 || FMT == FMT_Q8) ? MAXNU : 1];
-    int xs[(FMT == FMT_Q4) ? MAXNU : 1];
-#pragma unroll
-    for (int i = 0; i < MAXNU; ++i) {
-        const int u = j + TPR * i;
-        const bool valid = u < U;
-        if constexpr (FMT == FMT_F16) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) xf[i * 8 + e] = 0.f;
-            if (valid) {
-                const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)u * 8);
-                float v[8];
-                *reinterpret_cast<float4*>(&v[0]) = src[0];
-                *reinterpret_cast<float4*>(&v[4]) = src[1];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    float t = v[e];
-                    if (a.pro == PRO_RMSNORM) t = __fmul_rn(__fmul_rn(t, nscale), a.norm_w[(int64_t)u * 8 + e]);
-                    xf[i * 8 + e] = round_f16(t);
-                }
-            }
-        } else if constexpr (FMT == FMT_Q4W) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) xf[i * 32 + e] = 0.f;
-            if (valid) {
-                const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)u * 32);
-                const float4* wn = reinterpret_cast<const float4*>(a.norm_w + (int64_t)u * 32);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    float4 v = src[e];
-                    if (a.pro == PRO_RMSNORM) {
-                        const float4 w4 = wn[e];
-                        v.x = __fmul_rn(__fmul_rn(v.x, nscale), w4.x);
-                        v.y = __fmul_rn(__fmul_rn(v.y, nscale), w4.y);
-                        v.z = __fmul_rn(__fmul_rn(v.z, nscale), w4.z);
-                        v.w = __fmul_rn(__fmul_rn(v.w, nscale), w4.w);
-                    }
-                    xf[i * 32 + 4 * e + 0] = round_f16(v.x);
-                    xf[i * 32 + 4 * e + 1] = round_f16(v.y);
-                    xf[i * 32 + 4 * e + 2] = round_f16(v.z);
-                    xf[i * 32 + 4 * e + 3] = round_f16(v.w);
-                }
-            }
-        } else {
-            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)(valid ? u : 0) * 32);
-            const float4* wn = reinterpret_cast<const float4*>(a.norm_w + (int64_t)(valid ? u : 0) * 32);
-            const bool norm = a.pro == PRO_RMSNORM;
+    if constexpr (FMT == FMT_Q4 || FMT == FMT_Q8) {
+        int4* xq = reinterpret_cast<int4*>(xr);
+        int2* xds = reinterpret_cast<int2*>(xr + 32 * (int64_t)P.U);
+        for (int b = tid; b < P.U; b += kGemvThreads) {
+            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)b * 32);
+            const float4* wn = reinterpret_cast<const float4*>(a.norm_w + (int64_t)b * 32);
             auto load = [&](int e) -> float4 {
-                if (!valid) return make_float4(0.f, 0.f, 0.f, 0.f);
                 float4 v = src[e];
                 if (norm) {
                     const float4 w4 = wn[e];
@@ -211,186 +328,103 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             uint16_t dh;
             int qs;
             quantize_block32(load, q, d, dh, qs);
+            xq[2 * b] = make_int4(q[0], q[1], q[2], q[3]);
+            xq[2 * b + 1] = make_int4(q[4], q[5], q[6], q[7]);
+            xds[b] = make_int2(__float_as_int(d), qs);
+            if (a.xq_out != nullptr && blockIdx.x == 0) store_block_q8_0(a.xq_out + (int64_t)b * 34, dh, q);
+        }
+    } else {
+        uint4* xh = reinterpret_cast<uint4*>(xr);
+        for (int64_t i = tid; i < a.k / 8; i += kGemvThreads) {
+            const float4* src = reinterpret_cast<const float4*>(a.x + i * 8);
+            float v[8];
+            *reinterpret_cast<float4*>(&v[0]) = src[0];
+            *reinterpret_cast<float4*>(&v[4]) = src[1];
+            if (norm) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) xq[i * 8 + e] = q[e];
-            xd[i] = d;
-            if constexpr (FMT == FMT_Q4) xs[i] = qs;
-            if (a.xq_out != nullptr && blockIdx.x == 0 && g == 0 && valid)
-                store_block_q8_0(a.xq_out + (int64_t)u * 34, dh, q);
+                for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], nscale), a.norm_w[i * 8 + e]);
+            }
+            uint4 o;
+            __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+            xh[i] = o;
         }
     }
+    __syncthreads();  // activation ready; also publishes every warp's barrier init
 
-    // ---- stream the tiles ----
-    for (int it = 0; it < nt; ++it) {
-        const int s = it % S;
-        const uint32_t parity = (uint32_t)((it / S) & 1);
-        const bool ok = mbar_wait_bounded(&full[s], parity);
-        const uint8_t* tile = ring + (int64_t)s * tb;
-        const int64_t tglob = t0 + it;
-        float* pbuf = part + (it & 1) * kMaxR * kMaxSlots;
-        if (ok) {
-            for (int r = g; r < R; r += a.RG) {
-                float acc = 0.f;
-#pragma unroll
-                for (int i = 0; i < MAXNU; ++i) {
-                    const int u = j + TPR * i;
-                    if (u < U) {
-                        if constexpr (FMT == FMT_F16) {
-                            const uint4 wv = *reinterpret_cast<const uint4*>(tile + ((int64_t)r * a.k + (int64_t)u * 8) * 2);
-                            const __half2* h = reinterpret_cast<const __half2*>(&wv);
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float2 f = __half22float2(h[e]);
-                                acc = fmaf(f.x, xf[i * 8 + 2 * e], acc);
-                                acc = fmaf(f.y, xf[i * 8 + 2 * e + 1], acc);
-                            }
-                        } else if constexpr (FMT == FMT_Q4 || FMT == FMT_Q4W) {
-                            const int64_t bi = (int64_t)r * U + u;
-                            const uint4 qv = *reinterpret_cast<const uint4*>(tile + bi * 16);
-                            const float dw = h2f(*reinterpret_cast<const uint16_t*>(tile + (int64_t)R * U * 16 + bi * 2));
-                            const unsigned int wq[4] = {qv.x, qv.y, qv.z, qv.w};
-                            if constexpr (FMT == FMT_Q4) {
-                                int sumi = 0;
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) {
-                                    sumi = dp4a((int)(wq[e] & 0x0f0f0f0fu), xq[i * 8 + e], sumi);
-                                    sumi = dp4a((int)((wq[e] >> 4) & 0x0f0f0f0fu), xq[i * 8 + 4 + e], sumi);
-                                }
-                                sumi -= 8 * xs[i];
-                                if constexpr (DEBUG) {
-                                    const int64_t nrow = tglob * R + r;
-                                    if (nrow < a.n) a.dots[nrow * U + u] = sumi;
-                                }
-                                acc = fmaf(dw * xd[i], (float)sumi, acc);
-                            } else {
-                                float p = 0.f;
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) {
-#pragma unroll
-                                    for (int b = 0; b < 4; ++b) {
-                                        const int lo = (int)((wq[e] >> (8 * b)) & 0xfu) - 8;
-                                        const int hi = (int)((wq[e] >> (8 * b + 4)) & 0xfu) - 8;
-                                        p = fmaf((float)lo, xf[i * 32 + 4 * e + b], p);
-                                        p = fmaf((float)hi, xf[i * 32 + 16 + 4 * e + b], p);
-                                    }
-                                }
-                                acc = fmaf(dw, p, acc);
-                            }
-                        } else {  // FMT_Q8
-                            const int64_t bi = (int64_t)r * U + u;
-                            const uint4 lo = *reinterpret_cast<const uint4*>(tile + bi * 16);
-                            const uint4 hi = *reinterpret_cast<const uint4*>(tile + (int64_t)R * U * 16 + bi * 16);
-                            const float dw = h2f(*reinterpret_cast<const uint16_t*>(tile + (int64_t)R * U * 32 + bi * 2));
-                            int sumi = 0;
-                            sumi = dp4a((int)lo.x, xq[i * 8 + 0], sumi);
-                            sumi = dp4a((int)lo.y, xq[i * 8 + 1], sumi);
-                            sumi = dp4a((int)lo.z, xq[i * 8 + 2], sumi);
-                            sumi = dp4a((int)lo.w, xq[i * 8 + 3], sumi);
-                            sumi = dp4a((int)hi.x, xq[i * 8 + 4], sumi);
-                            sumi = dp4a((int)hi.y, xq[i * 8 + 5], sumi);
-                            sumi = dp4a((int)hi.z, xq[i * 8 + 6], sumi);
-                            sumi = dp4a((int)hi.w, xq[i * 8 + 7], sumi);
-                            if constexpr (DEBUG) {
-                                const int64_t nrow = tglob * R + r;
-                                if (nrow < a.n) a.dots[nrow * U + u] = sumi;
-                            }
-                            acc = fmaf(dw * xd[i], (float)sumi, acc);
-                        }
-                    }
-                }
-                acc = group_sum(acc, TPR < 32 ? TPR : 32);
-                if ((j & 31) == 0) pbuf[r * kMaxSlots + slot] = acc;
-            }
-        }
-        // Stage s is free once every thread passed this barrier.
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) {
-                // Drain the copies still in flight (bounded), then leave.
-                for (int k2 = it + 1; k2 < nt && k2 < it + S; ++k2)
-                    mbar_wait_bounded(&full[k2 % S], (uint32_t)((k2 / S) & 1));
-            }
+    // ---- stream this warp's chunks ----
+    float acc = 0.f, pend = 0.f;
+    unsigned long long best = 0ull;
+    for (int64_t q = 0; q < nq; ++q) {
+        const int s = (int)(q % S);
+        const uint32_t parity = (uint32_t)((q / S) & 1);
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[s], parity));
+        if (!ok) {
+            if (lane == 0)
+                for (int64_t q2 = q + 1; q2 < nq && q2 < q + S; ++q2)
+                    mbar_wait_bounded(&bars[q2 % S], (uint32_t)((q2 / S) & 1));
             return;
         }
-        if (tid == 0 && it + S < nt) {
-            mbar_arrive_expect_tx(&full[s], tb);
-            bulk_g2s(ring + (int64_t)s * tb, a.w + (t0 + it + S) * a.tile_bytes, tb, &full[s]);
-        }
-
-        // ---- finalize the tile's rows (warp 0) ----
-        if (tid < 32) {
-            const int64_t nbase = tglob * R;
-            auto rowsum = [&](int r) {
-                float v = 0.f;
-                for (int q = 0; q < nslot; ++q) v += pbuf[r * kMaxSlots + q];
-                return v;
-            };
-            if (a.epi == EPI_STORE || a.epi == EPI_ADD) {
-                if (tid < R) {
-                    const int64_t n = nbase + tid;
-                    if (n < a.n) {
-                        float v = rowsum(tid);
-                        if (a.epi == EPI_ADD) v = __fadd_rn(v, a.res[n]);
-                        a.y[n] = v;
+        const uint8_t* st = ring + (int64_t)s * P.stage_bytes;
+        if (P.rpc > 1) {
+            const int64_t r0 = row_begin + q * P.rpc;
+            const int rr = lane / P.tpr, li = lane - rr * P.tpr;
+            const int nr = (int)min((int64_t)P.rpc, P.n - r0);
+            float v = 0.f;
+            if (rr < nr) {
+                const uint8_t* row = st + (int64_t)rr * P.rs;
+                for (int j = 0; j < P.upl; ++j) {
+                    const int u = li + P.tpr * j;
+                    if (u < P.U) v += unit_dot<FMT, DEBUG>(row, P.U, u, u, xr, a.dots, r0 + rr, P.U);
+                }
+            }
+            v = group_sum(v, P.tpr);
+            const float vn = __shfl_down_sync(0xffffffffu, v, P.tpr < 32 ? P.tpr : 0);
+            if (li == 0 && rr < nr) {
+                if (pair) {
+                    if ((rr & 1) == 0) epi_pair(a, r0 + rr, v, vn);
+                } else {
+                    epi_row(a, r0 + rr, v, best);
+                }
+            }
+        } else {
+            const int c = (int)(q % P.nchunk);
+            const int u0 = c * P.kc;
+            const int nu = min(P.kc, P.U - u0);
+            const int64_t row = row_begin + q / P.nchunk;
+            for (int j = 0; j < P.upl; ++j) {
+                const int i = lane + 32 * j;
+                if (i < nu) acc += unit_dot<FMT, DEBUG>(st, P.kc, i, u0 + i, xr, a.dots, row, P.U);
+            }
+            if (c == P.nchunk - 1) {
+                const float v = warp_sum(acc);
+                acc = 0.f;
+                if (lane == 0) {
+                    if (pair) {
+                        if (((row - row_begin) & 1) == 0)
+                            pend = v;
+                        else
+                            epi_pair(a, row - 1, pend, v);
+                    } else {
+                        epi_row(a, row, v, best);
                     }
                 }
-            } else if (a.epi == EPI_SWIGLU) {
-                if (2 * tid < R) {
-                    const int64_t n = nbase + 2 * tid;
-                    if (n < a.n) {
-                        const float gt = rowsum(2 * tid), up = rowsum(2 * tid + 1);
-                        const float sg = __fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt)));
-                        a.y[n / 2] = __fmul_rn(sg, up);
-                    }
-                }
-            } else if (a.epi == EPI_QKV) {
-                if (2 * tid < R) {
-                    const int64_t n = nbase + 2 * tid;
-                    if (n < a.n) {
-                        const float v0 = rowsum(2 * tid), v1 = rowsum(2 * tid + 1);
-                        const int pos = *a.pos;
-                        if (n < a.nq + a.nkv) {
-                            const int local = (int)(n < a.nq ? n : n - a.nq);
-                            const int i0 = local % a.head_dim;
-                            float theta = (float)pos;
-                            for (int t = 0; t < i0 / 2; ++t) theta = __fmul_rn(theta, a.theta_scale);
-                            float sn, cs;
-                            sincosf(theta, &sn, &cs);
-                            const float r0 = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
-                            const float r1 = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cs));
-                            if (n < a.nq) {
-                                a.y[n] = r0;
-                                a.y[n + 1] = r1;
-                            } else {
-                                uint16_t* kr = a.kc + (int64_t)pos * a.nkv + local;
-                                kr[0] = f2h(r0);
-                                kr[1] = f2h(r1);
-                            }
-                        } else {
-                            const int local = (int)(n - a.nq - a.nkv);
-                            uint16_t* vr = a.vc + (int64_t)pos * a.nkv + local;
-                            vr[0] = f2h(v0);
-                            vr[1] = f2h(v1);
-                        }
-                    }
-                }
-            } else if (a.epi == EPI_ARGMAX) {
-                unsigned long long best = 0ull;
-                if (tid < R) {
-                    const int64_t n = nbase + tid;
-                    if (n < a.n) {
-                        const float v = rowsum(tid);
-                        a.y[n] = v;
-                        best = pack_argmax(v, n + a.row_offset);
-                    }
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-                    best = other > best ? other : best;
-                }
-                if (tid == 0 && best != 0ull) atomicMax(a.amax, best);
             }
         }
+        __syncwarp();  // every lane is done reading stage s
+        if (lane == 0 && q + S < nq) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(q + S, s);
+        }
+    }
+    if (a.epi == EPI_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane == 0 && best != 0ull) atomicMax(a.amax, best);
     }
 }
 

@@ -28,7 +28,7 @@ constexpr size_t kSmemBudget = 200 * 1024;
 
 int g_sms[kMaxDevices];
 std::mutex g_attr_mu;
-bool g_attr_done[kMaxDevices][16][2];
+bool g_attr_done[kMaxDevices][4][2];
 
 int current_device() {
     int d = 0;
@@ -73,105 +73,80 @@ int cuda_status(cudaError_t e) {
 // Opts a GEMV instantiation into large dynamic shared memory, once per device.
 // Done before any stream capture (b200i_prepare_device) so that capturing a
 // decode step never calls it.
-template <int FMT, int NU, bool DEBUG>
+template <int FMT, bool DEBUG>
 int set_gemv_attr(int dev) {
     std::lock_guard<std::mutex> lk(g_attr_mu);
-    const int slot = FMT * 4 + (NU == 1 ? 0 : NU == 2 ? 1 : NU == 4 ? 2 : 3);
-    if (dev < 0 || dev >= kMaxDevices || g_attr_done[dev][slot][DEBUG ? 1 : 0]) return B200_OK;
+    if (dev < 0 || dev >= kMaxDevices || g_attr_done[dev][FMT][DEBUG ? 1 : 0]) return B200_OK;
     cudaError_t e =
-        cudaFuncSetAttribute(gemv_kernel<FMT, NU, DEBUG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(gemv_kernel<FMT, DEBUG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return cuda_status(e);
-    g_attr_done[dev][slot][DEBUG ? 1 : 0] = true;
+    g_attr_done[dev][FMT][DEBUG ? 1 : 0] = true;
     return B200_OK;
 }
 
-template <int FMT, bool DEBUG>
-int set_gemv_attrs_fmt(int dev) {
-    CR_((set_gemv_attr<FMT, 1, DEBUG>(dev)));
-    CR_((set_gemv_attr<FMT, 2, DEBUG>(dev)));
-    if constexpr (MaxNU<FMT>::value >= 4) {
-        CR_((set_gemv_attr<FMT, 4, DEBUG>(dev)));
-        CR_((set_gemv_attr<FMT, 8, DEBUG>(dev)));
-    }
-    return B200_OK;
+// Shared memory of one GEMV launch: activation region, kGemvWarps rings of
+// `stages` chunks, their barriers, and a small reduction scratch.
+size_t gemv_smem_bytes(int fmt, const GemvPlan& p, int stages) {
+    return (size_t)gemv_x_bytes(fmt, p) + (size_t)kGemvWarps * stages * (size_t)p.stage_bytes +
+           (size_t)kGemvWarps * stages * sizeof(uint64_t) + kGemvWarps * sizeof(float);
 }
 
-template <int FMT, int NU, bool DEBUG>
-int launch_gemv_nu(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
-    const int dev = current_device();
-    const int grid = (int)std::min<int64_t>(p.ntiles, sm_count(dev));
-    const int64_t per_cta = (p.ntiles + grid - 1) / grid;
-    const size_t fixed = (size_t)(2 * kMaxR * kMaxSlots + 32) * sizeof(float) + 16 * sizeof(uint64_t);
-    int64_t S = (int64_t)((kSmemBudget - fixed) / (size_t)p.tile_bytes);
-    const int cap = stage_cap();
-    if (cap > 0) S = std::min<int64_t>(S, cap);
-    S = std::max<int64_t>(1, std::min<int64_t>(S, per_cta));
-    const size_t smem = (size_t)S * p.tile_bytes + (size_t)S * sizeof(uint64_t) +
-                        (size_t)(2 * kMaxR * kMaxSlots + 32) * sizeof(float);
-    CR_((set_gemv_attr<FMT, NU, DEBUG>(dev)));
-    a.tile_bytes = p.tile_bytes;
-    a.ntiles = p.ntiles;
-    a.R = p.R;
-    a.U = p.U;
-    a.n = p.n;
-    a.k = p.k;
-    a.stages = (int)S;
-    gemv_kernel<FMT, NU, DEBUG><<<grid, kGemvThreads, smem, st>>>(a);
-    return cuda_status(cudaGetLastError());
-}
-
-// Picks the row-group split and the smallest register footprint that covers
-// this thread's share of the activation.
 template <int FMT, bool DEBUG>
 int launch_gemv_t(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
-    a.RG = choose_row_groups(p, MaxNU<FMT>::value);
-    if (a.RG == 0) return B200_EUNSUPPORTED;
-    const int tpr = kGemvThreads / a.RG;
-    const int nu = (p.U + tpr - 1) / tpr;
-    if (nu <= 1) return launch_gemv_nu<FMT, 1, DEBUG>(a, p, st);
-    if (nu <= 2) return launch_gemv_nu<FMT, 2, DEBUG>(a, p, st);
-    if constexpr (MaxNU<FMT>::value >= 4) {
-        if (nu <= 4) return launch_gemv_nu<FMT, 4, DEBUG>(a, p, st);
-        return launch_gemv_nu<FMT, 8, DEBUG>(a, p, st);
-    }
-    return B200_EUNSUPPORTED;
+    const int dev = current_device();
+    CR_((set_gemv_attr<FMT, DEBUG>(dev)));
+    const bool pair = a.epi == EPI_SWIGLU || a.epi == EPI_QKV;
+    if (pair && (p.n & 1)) return B200_EINVAL;
+    const int64_t item_rows = p.rpc > 1 ? p.rpc : (pair ? 2 : 1);
+    const int64_t items = (p.n + item_rows - 1) / item_rows;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (items + kGemvWarps - 1) / kGemvWarps));
+    int S = kGemvStagesMax;
+    const int cap = stage_cap();
+    if (cap > 0) S = std::min(S, cap);
+    while (S > 1 && gemv_smem_bytes(FMT, p, S) > (size_t)kGemvSmemBudget) --S;
+    const size_t smem = gemv_smem_bytes(FMT, p, S);
+    if (smem > 227 * 1024) return B200_EUNSUPPORTED;
+    a.p = p;
+    a.n = p.n;
+    a.k = p.k;
+    a.stages = S;
+    gemv_kernel<FMT, DEBUG><<<grid, kGemvThreads, smem, st>>>(a);
+    return cuda_status(cudaGetLastError());
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// ggml rows -> packed rows (layout in args.h).  One thread per (row, unit).
 __global__ void repack_kernel(int type, const uint8_t* src0, const uint8_t* src1, int interleave, uint8_t* dst,
-                              int64_t n, int64_t k, int R, int U, int64_t tile_bytes, int64_t total) {
+                              int64_t n, int U, int64_t rs, int64_t total) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= total) return;
-    const int64_t tile = idx / ((int64_t)R * U);
-    const int64_t rem = idx - tile * (int64_t)R * U;
-    const int r = (int)(rem / U);
-    const int u = (int)(rem - (int64_t)r * U);
-    const int64_t p = tile * R + r;
-    if (p >= n) return;  // destination pre-zeroed
+    const int64_t p = idx / U;
+    const int u = (int)(idx - p * U);
+    if (p >= n) return;
     const uint8_t* src = src0;
     int64_t sr = p;
     if (interleave) {
         src = (p & 1) ? src1 : src0;
         sr = p >> 1;
     }
-    uint8_t* t = dst + tile * tile_bytes;
+    uint8_t* row = dst + p * rs;
     if (type == B200_TYPE_F16) {
-        const uint8_t* s = src + sr * (2 * k) + (int64_t)u * 16;
-        uint8_t* d = t + ((int64_t)r * k + (int64_t)u * 8) * 2;
+        const uint8_t* s = src + sr * (16 * (int64_t)U) + (int64_t)u * 16;
+        uint8_t* d = row + (int64_t)u * 16;
         for (int i = 0; i < 16; ++i) d[i] = s[i];
     } else if (type == B200_TYPE_Q4_0) {
         const uint8_t* s = src + (sr * U + u) * 18;
-        uint8_t* q = t + ((int64_t)r * U + u) * 16;
-        uint8_t* dd = t + (int64_t)R * U * 16 + ((int64_t)r * U + u) * 2;
+        uint8_t* q = row + (int64_t)u * 16;
+        uint8_t* dd = row + 16 * (int64_t)U + 2 * (int64_t)u;
         dd[0] = s[0];
         dd[1] = s[1];
         for (int i = 0; i < 16; ++i) q[i] = s[2 + i];
     } else {
         const uint8_t* s = src + (sr * U + u) * 34;
-        uint8_t* lo = t + ((int64_t)r * U + u) * 16;
-        uint8_t* hi = t + (int64_t)R * U * 16 + ((int64_t)r * U + u) * 16;
-        uint8_t* dd = t + (int64_t)R * U * 32 + ((int64_t)r * U + u) * 2;
+        uint8_t* lo = row + (int64_t)u * 16;
+        uint8_t* hi = row + 16 * (int64_t)U + (int64_t)u * 16;
+        uint8_t* dd = row + 32 * (int64_t)U + 2 * (int64_t)u;
         dd[0] = s[0];
         dd[1] = s[1];
         for (int i = 0; i < 16; ++i) {
@@ -251,12 +226,12 @@ int b200i_sm_count() { return sm_count(current_device()); }
 int b200i_prepare_device() {
     const int dev = current_device();
     sm_count(dev);
-    CR_((set_gemv_attrs_fmt<FMT_F16, false>(dev)));
-    CR_((set_gemv_attrs_fmt<FMT_Q4, false>(dev)));
-    CR_((set_gemv_attrs_fmt<FMT_Q4W, false>(dev)));
-    CR_((set_gemv_attrs_fmt<FMT_Q8, false>(dev)));
-    CR_((set_gemv_attrs_fmt<FMT_Q4, true>(dev)));
-    CR_((set_gemv_attrs_fmt<FMT_Q8, true>(dev)));
+    CR_((set_gemv_attr<FMT_F16, false>(dev)));
+    CR_((set_gemv_attr<FMT_Q4, false>(dev)));
+    CR_((set_gemv_attr<FMT_Q4W, false>(dev)));
+    CR_((set_gemv_attr<FMT_Q8, false>(dev)));
+    CR_((set_gemv_attr<FMT_Q4, true>(dev)));
+    CR_((set_gemv_attr<FMT_Q8, true>(dev)));
     return B200_OK;
 }
 
@@ -326,30 +301,29 @@ int b200_device_status(unsigned int* status, int reset) {
     return rc;
 }
 
-int64_t b200_packed_rows_per_tile(int type, int64_t n, int64_t k) {
+int64_t b200_packed_row_stride(int type, int64_t n, int64_t k) {
     GemvPlan p;
-    return make_plan(type, n, k, &p) ? p.R : 0;
+    return make_plan(type, n, k, &p) ? p.rs : 0;
 }
 
 size_t b200_packed_size(int type, int64_t n, int64_t k) {
     GemvPlan p;
-    return make_plan(type, n, k, &p) ? (size_t)(p.ntiles * p.tile_bytes) : 0;
+    return make_plan(type, n, k, &p) ? (size_t)gemv_packed_bytes(p) : 0;
 }
 
 static int repack_impl(int type, const void* s0, const void* s1, int interleave, void* dst, int64_t n,
                        int64_t k, cudaStream_t st) {
     GemvPlan p;
     if (!make_plan(type, n, k, &p)) return B200_EUNSUPPORTED;
-    if (!s0 || !dst || (interleave && !s1)) return B200_EINVAL;
-    int rc = cuda_status(cudaMemsetAsync(dst, 0, (size_t)(p.ntiles * p.tile_bytes), st));
+    if (!s0 || !dst || (interleave && !s1) || !aligned16(dst)) return B200_EINVAL;
+    int rc = cuda_status(cudaMemsetAsync(dst, 0, (size_t)gemv_packed_bytes(p), st));
     if (rc) return rc;
-    const int64_t total = p.ntiles * p.R * p.U;
+    const int64_t total = p.n * p.U;
     const int threads = 256;
     const int64_t blocks = (total + threads - 1) / threads;
     repack_kernel<<<(unsigned)blocks, threads, 0, st>>>(type, static_cast<const uint8_t*>(s0),
                                                         static_cast<const uint8_t*>(s1), interleave,
-                                                        static_cast<uint8_t*>(dst), n, k, p.R, p.U,
-                                                        p.tile_bytes, total);
+                                                        static_cast<uint8_t*>(dst), n, p.U, p.rs, total);
     return cuda_status(cudaGetLastError());
 }
 

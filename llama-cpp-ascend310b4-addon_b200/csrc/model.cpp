@@ -387,10 +387,6 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
     const size_t p_down = b200_packed_size(B200_TYPE_Q4_0, c.d_model, m->ff);
     const size_t p_head = b200_packed_size(B200_TYPE_Q4_0, m->voc, c.d_model);
     if (!p_qkv || !p_o || !p_gu || !p_down || !p_head) return fail(B200_EUNSUPPORTED);
-    // pair epilogues (RoPE pairs, gate/up pairs) need two rows per tile
-    if (b200_packed_rows_per_tile(B200_TYPE_Q4_0, m->qkv_rows, c.d_model) < 2 ||
-        b200_packed_rows_per_tile(B200_TYPE_Q4_0, 2 * (int64_t)m->ff, c.d_model) < 2)
-        return fail(B200_EUNSUPPORTED);
     const size_t kv_bytes = (size_t)c.kv_size * m->hkv * D * 2;
     m->L.resize(c.n_layer);
     for (auto& Ly : m->L) {

@@ -45,12 +45,12 @@ def test_version_and_errors():
 def test_packed_size_layout(wtype, n, k):
     import b200_decode as B
 
-    r = B.rows_per_tile(wtype, n, k)
-    assert r >= 1 and (r & (r - 1)) == 0
-    rowbytes = {1: 2 * k, 2: k // 2 + k // 16, 8: k + k // 16}[wtype]
-    tile = (r * rowbytes + 15) // 16 * 16
-    assert B.packed_size(wtype, n, k) == tile * ((n + r - 1) // r)
-    assert tile <= 65536
+    u = k // 8 if wtype == 1 else k // 32
+    pad16 = lambda v: (v + 15) // 16 * 16
+    rs = {1: 2 * k, 2: 16 * u + pad16(2 * u), 8: 32 * u + pad16(2 * u)}[wtype]
+    assert B.row_stride(wtype, n, k) == rs
+    assert B.packed_size(wtype, n, k) == rs * n
+    assert rs % 16 == 0
 
 
 def test_unsupported_shapes_report_zero():
