@@ -50,7 +50,9 @@ struct GemvPlan {
     int kc;             // units per chunk row (== U when rpc > 1)
     int nchunk;         // chunks per row (1 when rpc > 1)
     int tpr;            // lanes per row (32 / rpc)
+    int tpr_log2;
     int upl;            // units per lane per chunk row
+    int full_upl;       // units per lane of a full chunk (rpc == 1 and kc % 64 == 0), else 0
     int64_t stage_bytes;
 };
 
@@ -79,7 +81,7 @@ B200_HD inline bool make_plan(int type, int64_t n, int64_t k, GemvPlan* p) {
         p->U = (int)(k / 32);
         p->ub = 18;
         p->rs = 16 * (int64_t)p->U + pad16(2 * (int64_t)p->U);
-        kc_max = 128;
+        kc_max = 256;
     } else if (type == B200_TYPE_Q8_0) {
         if (k % 32) return false;
         p->U = (int)(k / 32);
@@ -94,21 +96,38 @@ B200_HD inline bool make_plan(int type, int64_t n, int64_t k, GemvPlan* p) {
     if (U >= 64) {
         p->rpc = 1;
         p->tpr = 32;
-        p->nchunk = (U + kc_max - 1) / kc_max;
-        int kc = (U + p->nchunk - 1) / p->nchunk;
-        kc = (kc + 7) & ~7;  // chunk starts keep the scale plane 16-byte aligned
+        p->tpr_log2 = 5;
+        // Chunk width: a multiple of 64 (every full chunk gives each lane the
+        // same even number of units and keeps the scale plane 16-byte
+        // aligned); prefer the widest one that divides the row, so that no
+        // row ends in a partial chunk.
+        int kc = 0;
+        for (int c = kc_max; c >= 64; c -= 64)
+            if (U % c == 0) {
+                kc = c;
+                break;
+            }
+        if (kc == 0) {
+            const int nch = (U + kc_max - 1) / kc_max;
+            kc = (((U + nch - 1) / nch) + 63) & ~63;
+            if (kc > kc_max) kc = kc_max;
+        }
         p->kc = kc;
         p->nchunk = (U + kc - 1) / kc;
         p->upl = (kc + 31) / 32;
+        p->full_upl = (kc % 64 == 0) ? kc / 32 : 0;
         p->stage_bytes = gemv_stage_bytes_rpc1(type, kc);
     } else {
         int rpc = 32;
         while (rpc > 1 && rpc * U > 128) rpc >>= 1;
         p->rpc = rpc;
         p->tpr = 32 / rpc;
+        p->tpr_log2 = 0;
+        while ((1 << p->tpr_log2) < p->tpr) ++p->tpr_log2;
         p->kc = U;
         p->nchunk = 1;
         p->upl = (U + p->tpr - 1) / p->tpr;
+        p->full_upl = 0;
         p->stage_bytes = rpc * p->rs;
     }
     return true;

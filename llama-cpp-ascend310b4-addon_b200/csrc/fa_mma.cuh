@@ -1,0 +1,313 @@
+// fa_mma.cuh -- single-token GQA flash-decoding on tensor cores (head_dim 64
+// and 128).
+//
+// Grid (split, kv head, q-head chunk), 128 threads.  The query heads of one
+// GQA group (up to 8) form the M dimension of mma.sync m16n8k16 (rows 8..15
+// are zero), so each K/V tile is read from HBM once for the whole group:
+//   S = Q K^T : A = f16(q) (held in registers for the whole split), B = K
+//               tile via ldmatrix from an XOR-swizzled shared-memory stage;
+//   P V       : A = P (the S accumulator layout re-used as the A operand),
+//               B = V tile via ldmatrix.trans.  P is split into an f16 high
+//               part and an f16 residual so the product keeps ~22 bits.
+// K/V chunks of 64 positions stream through a 3-stage cp.async ring (rows
+// past the context are zero-filled).  Each warp owns 16 positions of every
+// chunk and keeps its own online-softmax state (max, sum, output); the four
+// warps are combined at the end, and splits are merged by the last CTA of
+// the (kv head, head chunk), as in fa.cuh.
+#pragma once
+
+#include "args.h"
+#include "common.cuh"
+
+namespace b200 {
+
+constexpr int kFmStages = 3;
+
+__device__ __forceinline__ void mma_16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t r[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// 16-byte async copy; src_bytes == 0 zero-fills the destination.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Shared memory of fa_mma_kernel<D>: kFmStages x (K tile + V tile) of
+// kFaChunk rows x D halves; reused after the loop for the warp combine.
+B200_HD inline size_t fa_mma_smem_bytes(int D) { return (size_t)kFmStages * 2 * kFaChunk * D * 2; }
+
+template <int D>
+__global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
+    constexpr int KT = D / 16;       // k tiles of the QK^T product
+    constexpr int NT = D / 8;        // n tiles of the PV product
+    constexpr int GR = D / 8;        // 16-byte granules per K/V row
+    constexpr int ROWB = 2 * D;      // bytes per K/V row in shared memory
+    constexpr int TILE = kFaChunk * ROWB;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float wm[4][kFaMaxG], wl[4][kFaMaxG];
+    __shared__ int is_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int split = blockIdx.x, hk = blockIdx.y, gc = blockIdx.z;
+    const int h0 = hk * a.G + gc * kFaMaxG;
+    const int hn = min(kFaMaxG, a.G - gc * kFaMaxG);
+
+    int ctx = a.n_kv;
+    if (a.kv_len != nullptr) {
+        const int kl = a.kv_len[0];
+        if (kl > 0 && kl < a.n_kv) ctx = kl;
+    }
+    const int nchunks_ctx = (ctx + kFaChunk - 1) / kFaChunk;
+    const int c_begin = split * a.chunks_per_split;
+    const int c_end = min(c_begin + a.chunks_per_split, nchunks_ctx);
+    const bool active = c_begin < c_end;
+    const uint32_t sbase = smem_u32(smem);
+
+    float m_run = -INFINITY, l_run = 0.f;  // head g of this warp's positions
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+    if (active) {
+        // Q fragments (A operand, rows = heads; rows 8..15 are zero)
+        uint32_t qa[KT][2];
+        {
+            const bool hv = g < hn;
+            const float* qr = a.q + (int64_t)(h0 + (hv ? g : 0)) * D;
+#pragma unroll
+            for (int kt = 0; kt < KT; ++kt) {
+                const float2 x0 = *reinterpret_cast<const float2*>(qr + 16 * kt + 2 * t);
+                const float2 x1 = *reinterpret_cast<const float2*>(qr + 16 * kt + 2 * t + 8);
+                qa[kt][0] = hv ? pack_half2(x0.x, x0.y) : 0u;
+                qa[kt][1] = hv ? pack_half2(x1.x, x1.y) : 0u;
+            }
+        }
+        auto load_chunk = [&](int c, int stage) {
+            const uint32_t kst = sbase + (uint32_t)(stage * 2 * TILE);
+            const uint32_t vst = kst + TILE;
+            const int p0 = c * kFaChunk;
+#pragma unroll
+            for (int i = 0; i < kFaChunk * GR / 128; ++i) {
+                const int idx = tid + 128 * i;
+                const int r = idx / GR, cg = idx - (idx / GR) * GR;
+                const int p = p0 + r;
+                const bool ok = p < ctx;
+                const uint32_t off = (uint32_t)(r * ROWB + ((cg ^ (r & 7)) << 4));
+                const uint8_t* ks = a.k + (ok ? ((int64_t)p * a.k_nb1 + (int64_t)hk * a.k_nb2 + cg * 16) : 0);
+                const uint8_t* vs = a.v + (ok ? ((int64_t)p * a.v_nb1 + (int64_t)hk * a.v_nb2 + cg * 16) : 0);
+                cp_async16(kst + off, ks, ok ? 16 : 0);
+                cp_async16(vst + off, vs, ok ? 16 : 0);
+            }
+        };
+        const int nc = c_end - c_begin;
+        load_chunk(c_begin, 0);
+        cp_async_commit();
+        if (nc > 1) load_chunk(c_begin + 1, 1);
+        cp_async_commit();
+
+        for (int ci = 0; ci < nc; ++ci) {
+            const int c = c_begin + ci;
+            const int stage = ci % kFmStages;
+            if (ci + 2 < nc) load_chunk(c + 2, (ci + 2) % kFmStages);
+            cp_async_commit();
+            cp_async_wait<2>();
+            __syncthreads();  // chunk c is in shared memory for every warp
+
+            const uint32_t kst = sbase + (uint32_t)(stage * 2 * TILE);
+            const uint32_t vst = kst + TILE;
+            const int pw = 16 * warp;  // this warp's 16 positions in the chunk
+            // ---- S = Q K^T over 2 n-tiles of 8 positions ----
+            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            {
+                const int mi = lane >> 3, ri = lane & 7;
+                const int j = mi >> 1, hh = mi & 1;
+                const int r = pw + 8 * j + ri;
+#pragma unroll
+                for (int kt = 0; kt < KT; ++kt) {
+                    uint32_t b[4];
+                    ldsm_x4(b, kst + (uint32_t)(r * ROWB + (((2 * kt + hh) ^ ri) << 4)));
+                    const uint32_t af[4] = {qa[kt][0], 0u, qa[kt][1], 0u};
+                    mma_16816(s[0], af, b[0], b[1]);
+                    mma_16816(s[1], af, b[2], b[3]);
+                }
+            }
+            // ---- scale, mask, online softmax (rows = head g) ----
+            const int pbase = c * kFaChunk + pw;
+            float sv[4];
+            float cmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int p = pbase + 8 * j + 2 * t + e;
+                    float mv = 0.f;
+                    if (a.mask != nullptr && p < ctx) mv = h2f(a.mask[p]);
+                    float x = (p < ctx && mv != -INFINITY) ? __fadd_rn(__fmul_rn(s[j][e], a.scale), mv) : -INFINITY;
+                    sv[2 * j + e] = x;
+                    cmax = fmaxf(cmax, x);
+                }
+            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
+            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
+            const float m_new = fmaxf(m_run, cmax);
+            float alpha = 1.f;
+            float pv[4];
+            if (m_new == -INFINITY) {
+                pv[0] = pv[1] = pv[2] = pv[3] = 0.f;
+            } else {
+                alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) pv[e] = sv[e] == -INFINITY ? 0.f : expf(sv[e] - m_new);
+            }
+            float psum = (pv[0] + pv[1]) + (pv[2] + pv[3]);
+            psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+            psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+            l_run = l_run * alpha + psum;
+            m_run = m_new;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                o[n][0] *= alpha;
+                o[n][1] *= alpha;
+            }
+            // ---- O += P V, P = P_hi + P_lo in f16 ----
+            const uint32_t ph0 = pack_half2(pv[0], pv[1]), ph1 = pack_half2(pv[2], pv[3]);
+            const __half2 h0v = *reinterpret_cast<const __half2*>(&ph0);
+            const __half2 h1v = *reinterpret_cast<const __half2*>(&ph1);
+            const float2 f0 = __half22float2(h0v), f1 = __half22float2(h1v);
+            const uint32_t pl0 = pack_half2(pv[0] - f0.x, pv[1] - f0.y), pl1 = pack_half2(pv[2] - f1.x, pv[3] - f1.y);
+            const uint32_t pa_hi[4] = {ph0, 0u, ph1, 0u};
+            const uint32_t pa_lo[4] = {pl0, 0u, pl1, 0u};
+            {
+                const int mi = lane >> 3, ri = lane & 7;
+                const int ph = mi & 1, jn = mi >> 1;
+                const int r = pw + 8 * ph + ri;
+#pragma unroll
+                for (int jj = 0; jj < NT / 2; ++jj) {
+                    uint32_t b[4];
+                    ldsm_x4_trans(b, vst + (uint32_t)(r * ROWB + (((2 * jj + jn) ^ ri) << 4)));
+                    mma_16816(o[2 * jj], pa_hi, b[0], b[1]);
+                    mma_16816(o[2 * jj], pa_lo, b[0], b[1]);
+                    mma_16816(o[2 * jj + 1], pa_hi, b[2], b[3]);
+                    mma_16816(o[2 * jj + 1], pa_lo, b[2], b[3]);
+                }
+            }
+            __syncthreads();  // stage may be refilled by the next iteration
+        }
+        cp_async_wait<0>();
+    }
+
+    // ---- combine the 4 warps (shared memory re-used) ----
+    float* wo = reinterpret_cast<float*>(smem);  // [4][kFaMaxG][D]
+    __syncthreads();
+    if (t == 0) {
+        wm[warp][g] = m_run;
+        wl[warp][g] = l_run;
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+        wo[((warp * kFaMaxG) + g) * D + 8 * n + 2 * t] = o[n][0];
+        wo[((warp * kFaMaxG) + g) * D + 8 * n + 2 * t + 1] = o[n][1];
+    }
+    __syncthreads();
+    if (active) {
+        for (int idx = tid; idx < hn * D; idx += 128) {
+            const int h = idx / D, d = idx - (idx / D) * D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][h]);
+            float ov = 0.f, lv = 0.f;
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const float e = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
+                    ov = fmaf(wo[((w * kFaMaxG) + h) * D + d], e, ov);
+                    lv = fmaf(wl[w][h], e, lv);
+                }
+            }
+            a.part_o[((int64_t)split * a.Hq + h0 + h) * D + d] = ov;
+            if (d == 0) {
+                a.part_ml[((int64_t)split * a.Hq + h0 + h) * 2 + 0] = M;
+                a.part_ml[((int64_t)split * a.Hq + h0 + h) * 2 + 1] = lv;
+            }
+        }
+    }
+
+    // ---- ticket: the last CTA of this (kv head, chunk) merges the splits ----
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        unsigned int* tk = a.tickets + hk * a.gchunks + gc;
+        const unsigned int old = atomicAdd(tk, 1u);
+        is_last = old == (unsigned int)(a.n_splits - 1);
+        if (is_last) *tk = 0u;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+
+    const int n_act = (nchunks_ctx + a.chunks_per_split - 1) / a.chunks_per_split;
+    float* wts = reinterpret_cast<float*>(smem);  // [kFaMaxG][n_act]
+    for (int h = warp; h < hn; h += 4) {
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < n_act; s2 += 32) M = fmaxf(M, __ldcg(&a.part_ml[((int64_t)s2 * a.Hq + h0 + h) * 2]));
+        M = warp_max(M);
+        float L = 0.f;
+        for (int s2 = lane; s2 < n_act; s2 += 32) {
+            const float ms = __ldcg(&a.part_ml[((int64_t)s2 * a.Hq + h0 + h) * 2]);
+            const float ls = __ldcg(&a.part_ml[((int64_t)s2 * a.Hq + h0 + h) * 2 + 1]);
+            const float e = (ms == -INFINITY) ? 0.f : expf(ms - M);
+            wts[h * n_act + s2] = e;
+            L += ls * e;
+        }
+        L = warp_sum(L);
+        const float inv = (L > 0.f) ? 1.0f / L : 0.f;
+        __syncwarp();
+        for (int s2 = lane; s2 < n_act; s2 += 32) wts[h * n_act + s2] *= inv;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < hn * D; idx += 128) {
+        const int h = idx / D, d = idx - (idx / D) * D;
+        const float* po = a.part_o + (int64_t)(h0 + h) * D + d;
+        const int64_t stride = (int64_t)a.Hq * D;
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+        int s2 = 0;
+        for (; s2 + 4 <= n_act; s2 += 4) {
+            o0 = fmaf(__ldcg(po + (int64_t)(s2 + 0) * stride), wts[h * n_act + s2 + 0], o0);
+            o1 = fmaf(__ldcg(po + (int64_t)(s2 + 1) * stride), wts[h * n_act + s2 + 1], o1);
+            o2 = fmaf(__ldcg(po + (int64_t)(s2 + 2) * stride), wts[h * n_act + s2 + 2], o2);
+            o3 = fmaf(__ldcg(po + (int64_t)(s2 + 3) * stride), wts[h * n_act + s2 + 3], o3);
+        }
+        for (; s2 < n_act; ++s2) o0 = fmaf(__ldcg(po + (int64_t)s2 * stride), wts[h * n_act + s2], o0);
+        a.out[(int64_t)(h0 + h) * D + d] = (o0 + o1) + (o2 + o3);
+    }
+}
+
+}  // namespace b200

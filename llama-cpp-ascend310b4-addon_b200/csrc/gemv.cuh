@@ -78,9 +78,16 @@ __device__ __forceinline__ void store_block_q8_0(uint8_t* dst, uint16_t dh, cons
     }
 }
 
+// Exact int -> float for |v| < 2^22 on the integer/FMA pipes (the int->float
+// conversion instruction runs on the narrow transcendental pipe): the bits of
+// 1.5 * 2^23 + v, minus 1.5 * 2^23.
+__device__ __forceinline__ float small_int_to_float(int v) {
+    return __int_as_float(0x4B400000 + v) - 12582912.0f;
+}
+
 // Bytes of the activation region at the start of shared memory.
 B200_HD inline int64_t gemv_x_bytes(int fmt, const GemvPlan& p) {
-    if (fmt == FMT_Q4 || fmt == FMT_Q8) return pad16(40 * (int64_t)p.U);  // xq[U][32] + {d, sum}[U]
+    if (fmt == FMT_Q4 || fmt == FMT_Q8) return pad16(40 * (int64_t)p.U);  // xq planes 2 x [U][16] + {d, sum}[U]
     return pad16(2 * p.k);                                                // f16 x[K]
 }
 
@@ -136,11 +143,18 @@ __device__ __forceinline__ void epi_pair(const GemvArgs& a, int64_t n, float v0,
 
 // ------------------------------------------------------------ unit dots
 
-// Contribution of one unit: `row` is the staged chunk row, `pw` its plane
-// width, `i` the unit's index in the chunk row, `u` its index in the full row.
+template <int FMT>
+struct GemvTraits {
+    // units per lane per chunk row, upper bound (plan: kc <= 128 for Q8_0, 256 otherwise)
+    static constexpr int kMaxUpl = FMT == FMT_Q8 ? 4 : 8;
+};
+
+// Sum of one staged chunk row for this lane: units i = i0 + step*j (j < upl,
+// i < nu) of a row whose planes are `pw` units wide; `u0` is the row offset of
+// unit 0 of the chunk.  All loads of the row are issued before the math.
 template <int FMT, bool DEBUG>
-__device__ __forceinline__ float unit_dot(const uint8_t* row, int pw, int i, int u, const uint8_t* xr,
-                                          int32_t* dots, int64_t nrow, int U) {
+__device__ __forceinline__ float unit_dot(const uint8_t* row, int pw, int i, int u, const uint8_t* xr, int U,
+                                          int32_t* dots, int64_t nrow) {
     if constexpr (FMT == FMT_F16) {
         const uint4 wv = *reinterpret_cast<const uint4*>(row + 16 * i);
         const uint4 xv = *reinterpret_cast<const uint4*>(xr + 16 * u);
@@ -170,57 +184,168 @@ __device__ __forceinline__ float unit_dot(const uint8_t* row, int pw, int i, int
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
                     const float2 xf = __half22float2(xh[t]);
-                    const int j = e * 8 + t * 2;  // element index within the half
-                    const unsigned int w = wq[j >> 2];
-                    const int sh = 8 * (j & 3) + 4 * hf;
-                    const int q0 = (int)((w >> sh) & 0xfu) - 8;
-                    const int q1 = (int)((w >> (sh + 8)) & 0xfu) - 8;
-                    p = fmaf((float)q0, xf.x, p);
-                    p = fmaf((float)q1, xf.y, p);
+                    const int jj = e * 8 + t * 2;  // element index within the half
+                    const unsigned int w = wq[jj >> 2];
+                    const int sh = 8 * (jj & 3) + 4 * hf;
+                    // nibble - 8 as a float without an int->float conversion:
+                    // the bits 2^23 + nibble, minus (2^23 + 8)
+                    const float q0 = __uint_as_float(0x4B000000u | ((w >> sh) & 0xfu)) - 8388616.0f;
+                    const float q1 = __uint_as_float(0x4B000000u | ((w >> (sh + 8)) & 0xfu)) - 8388616.0f;
+                    p = fmaf(q0, xf.x, p);
+                    p = fmaf(q1, xf.y, p);
                 }
             }
         }
         return dw * p;
     } else {
-        const int4* xq = reinterpret_cast<const int4*>(xr + 32 * u);
-        const int4 xa = xq[0], xb = xq[1];
-        const int2 ds = reinterpret_cast<const int2*>(xr + 32 * U)[u];
-        const float xd = __int_as_float(ds.x);
-        int sumi = 0;
+        const int4 xa = reinterpret_cast<const int4*>(xr)[u];
+        const int4 xb = reinterpret_cast<const int4*>(xr + 16 * (int64_t)U)[u];
+        const int2 ds = reinterpret_cast<const int2*>(xr + 32 * (int64_t)U)[u];
+        int s0, s1;
         float dw;
         if constexpr (FMT == FMT_Q4) {
             const uint4 qv = *reinterpret_cast<const uint4*>(row + 16 * i);
             dw = h2f(*reinterpret_cast<const uint16_t*>(row + 16 * pw + 2 * i));
-            sumi = dp4a((int)(qv.x & 0x0f0f0f0fu), xa.x, sumi);
-            sumi = dp4a((int)(qv.y & 0x0f0f0f0fu), xa.y, sumi);
-            sumi = dp4a((int)(qv.z & 0x0f0f0f0fu), xa.z, sumi);
-            sumi = dp4a((int)(qv.w & 0x0f0f0f0fu), xa.w, sumi);
-            sumi = dp4a((int)((qv.x >> 4) & 0x0f0f0f0fu), xb.x, sumi);
-            sumi = dp4a((int)((qv.y >> 4) & 0x0f0f0f0fu), xb.y, sumi);
-            sumi = dp4a((int)((qv.z >> 4) & 0x0f0f0f0fu), xb.z, sumi);
-            sumi = dp4a((int)((qv.w >> 4) & 0x0f0f0f0fu), xb.w, sumi);
-            sumi -= 8 * ds.y;  // nibbles are stored +8
+            s0 = dp4a((int)(qv.x & 0x0f0f0f0fu), xa.x, 0);
+            s1 = dp4a((int)((qv.x >> 4) & 0x0f0f0f0fu), xb.x, 0);
+            s0 = dp4a((int)(qv.y & 0x0f0f0f0fu), xa.y, s0);
+            s1 = dp4a((int)((qv.y >> 4) & 0x0f0f0f0fu), xb.y, s1);
+            s0 = dp4a((int)(qv.z & 0x0f0f0f0fu), xa.z, s0);
+            s1 = dp4a((int)((qv.z >> 4) & 0x0f0f0f0fu), xb.z, s1);
+            s0 = dp4a((int)(qv.w & 0x0f0f0f0fu), xa.w, s0);
+            s1 = dp4a((int)((qv.w >> 4) & 0x0f0f0f0fu), xb.w, s1);
+            s0 -= 8 * ds.y;  // nibbles are stored +8
         } else {
             const uint4 lo = *reinterpret_cast<const uint4*>(row + 16 * i);
             const uint4 hi = *reinterpret_cast<const uint4*>(row + 16 * pw + 16 * i);
             dw = h2f(*reinterpret_cast<const uint16_t*>(row + 32 * pw + 2 * i));
-            sumi = dp4a((int)lo.x, xa.x, sumi);
-            sumi = dp4a((int)lo.y, xa.y, sumi);
-            sumi = dp4a((int)lo.z, xa.z, sumi);
-            sumi = dp4a((int)lo.w, xa.w, sumi);
-            sumi = dp4a((int)hi.x, xb.x, sumi);
-            sumi = dp4a((int)hi.y, xb.y, sumi);
-            sumi = dp4a((int)hi.z, xb.z, sumi);
-            sumi = dp4a((int)hi.w, xb.w, sumi);
+            s0 = dp4a((int)lo.x, xa.x, 0);
+            s1 = dp4a((int)hi.x, xb.x, 0);
+            s0 = dp4a((int)lo.y, xa.y, s0);
+            s1 = dp4a((int)hi.y, xb.y, s1);
+            s0 = dp4a((int)lo.z, xa.z, s0);
+            s1 = dp4a((int)hi.z, xb.z, s1);
+            s0 = dp4a((int)lo.w, xa.w, s0);
+            s1 = dp4a((int)hi.w, xb.w, s1);
         }
+        const int sumi = s0 + s1;
         if constexpr (DEBUG) dots[nrow * U + u] = sumi;
-        return (dw * xd) * (float)sumi;
+        return (dw * __int_as_float(ds.x)) * small_int_to_float(sumi);
+    }
+}
+
+// Generic chunk row (tails, short rows): units i = i0 + step*j, j < upl, i < nu.
+template <int FMT, bool DEBUG>
+__device__ __forceinline__ float chunk_row_dot(const uint8_t* row, int pw, int i0, int step, int upl, int nu, int u0,
+                                               const uint8_t* xr, int U, int32_t* dots, int64_t nrow) {
+    float acc = 0.f;
+    for (int j = 0; j < upl; ++j) {
+        const int i = i0 + step * j;
+        if (i < nu) acc += unit_dot<FMT, DEBUG>(row, pw, i, u0 + i, xr, U, dots, nrow);
+    }
+    return acc;
+}
+
+// Full chunk on the one-row path: exactly UPL units per lane at compile-time
+// offsets (unit j of this lane is chunk unit lane + 32 j), no predicates.
+template <int FMT, bool DEBUG, int UPL>
+__device__ __forceinline__ float chunk_full_dot(const uint8_t* st, int kc, int lane, int u0, const uint8_t* xr, int U,
+                                                int32_t* dots, int64_t nrow) {
+    float acc = 0.f;
+    if constexpr (FMT == FMT_Q4 || FMT == FMT_Q8) {
+        const uint8_t* wq = st + 16 * lane;
+        const uint8_t* wh = st + 16 * kc + 16 * lane;                           // Q8_0 bytes 16..31
+        const uint8_t* wd = st + (FMT == FMT_Q8 ? 32 : 16) * kc + 2 * lane;     // scales
+        const int4* xpa = reinterpret_cast<const int4*>(xr) + u0 + lane;
+        const int4* xpb = reinterpret_cast<const int4*>(xr + 16 * (int64_t)U) + u0 + lane;
+        const int2* xpd = reinterpret_cast<const int2*>(xr + 32 * (int64_t)U) + u0 + lane;
+#pragma unroll
+        for (int j0 = 0; j0 < UPL; j0 += 2) {
+            constexpr int Bt = 2;
+            uint4 wa[Bt], wb[Bt];
+            int4 xa[Bt], xb[Bt];
+            int2 ds[Bt];
+            uint16_t dwh[Bt];
+#pragma unroll
+            for (int b = 0; b < Bt; ++b) {
+                const int j = j0 + b;
+                if (j < UPL) {
+                    wa[b] = *reinterpret_cast<const uint4*>(wq + 512 * j);
+                    if constexpr (FMT == FMT_Q8) wb[b] = *reinterpret_cast<const uint4*>(wh + 512 * j);
+                    dwh[b] = *reinterpret_cast<const uint16_t*>(wd + 64 * j);
+                    xa[b] = xpa[32 * j];
+                    xb[b] = xpb[32 * j];
+                    ds[b] = xpd[32 * j];
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < Bt; ++b) {
+                const int j = j0 + b;
+                if (j < UPL) {
+                    int s0, s1;
+                    if constexpr (FMT == FMT_Q4) {
+                        const uint4 qv = wa[b];
+                        s0 = dp4a((int)(qv.x & 0x0f0f0f0fu), xa[b].x, 0);
+                        s1 = dp4a((int)((qv.x >> 4) & 0x0f0f0f0fu), xb[b].x, 0);
+                        s0 = dp4a((int)(qv.y & 0x0f0f0f0fu), xa[b].y, s0);
+                        s1 = dp4a((int)((qv.y >> 4) & 0x0f0f0f0fu), xb[b].y, s1);
+                        s0 = dp4a((int)(qv.z & 0x0f0f0f0fu), xa[b].z, s0);
+                        s1 = dp4a((int)((qv.z >> 4) & 0x0f0f0f0fu), xb[b].z, s1);
+                        s0 = dp4a((int)(qv.w & 0x0f0f0f0fu), xa[b].w, s0);
+                        s1 = dp4a((int)((qv.w >> 4) & 0x0f0f0f0fu), xb[b].w, s1);
+                        s0 -= 8 * ds[b].y;  // nibbles are stored +8
+                    } else {
+                        s0 = dp4a((int)wa[b].x, xa[b].x, 0);
+                        s1 = dp4a((int)wb[b].x, xb[b].x, 0);
+                        s0 = dp4a((int)wa[b].y, xa[b].y, s0);
+                        s1 = dp4a((int)wb[b].y, xb[b].y, s1);
+                        s0 = dp4a((int)wa[b].z, xa[b].z, s0);
+                        s1 = dp4a((int)wb[b].z, xb[b].z, s1);
+                        s0 = dp4a((int)wa[b].w, xa[b].w, s0);
+                        s1 = dp4a((int)wb[b].w, xb[b].w, s1);
+                    }
+                    const int sumi = s0 + s1;
+                    if constexpr (DEBUG) dots[nrow * U + u0 + lane + 32 * j] = sumi;
+                    acc = fmaf(h2f(dwh[b]) * __int_as_float(ds[b].x), small_int_to_float(sumi), acc);
+                }
+            }
+        }
+        return acc;
+    } else if constexpr (FMT == FMT_F16) {
+        const uint8_t* wp = st + 16 * lane;
+        const uint8_t* xp = xr + 16 * (int64_t)(u0 + lane);
+#pragma unroll
+        for (int j0 = 0; j0 < UPL; j0 += 2) {
+            uint4 wv[2], xv[2];
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                wv[b] = *reinterpret_cast<const uint4*>(wp + 512 * (j0 + b));
+                xv[b] = *reinterpret_cast<const uint4*>(xp + 512 * (j0 + b));
+            }
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const __half2* wh = reinterpret_cast<const __half2*>(&wv[b]);
+                const __half2* xh = reinterpret_cast<const __half2*>(&xv[b]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 wf = __half22float2(wh[e]);
+                    const float2 xf = __half22float2(xh[e]);
+                    acc = fmaf(wf.x, xf.x, acc);
+                    acc = fmaf(wf.y, xf.y, acc);
+                }
+            }
+        }
+        return acc;
+    } else {
+        return chunk_row_dot<FMT, DEBUG>(st, kc, lane, 32, UPL, kc, u0, xr, U, dots, nrow);
     }
 }
 
 // ------------------------------------------------------------ the kernel
 
-template <int FMT, bool DEBUG>
+// UPL: units per lane of this plan's full chunks (P.full_upl), or 0 when the
+// plan has none; fixed at compile time so those chunks run fully unrolled.
+template <int FMT, bool DEBUG, int UPL>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& P = a.p;
@@ -234,29 +359,67 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     uint64_t* bars = bars_all + warp * S;
     float* red = reinterpret_cast<float*>(bars_all + kGemvWarps * S);  // [kGemvWarps]
 
-    // ---- this warp's rows ----
+    // ---- work distribution ----
+    // rpc > 1 (short rows): every warp owns a contiguous range of row groups
+    // and runs the epilogue itself.  rpc == 1: every CTA owns a contiguous,
+    // balanced range of rows [cr0, cr1); its chunk sequence (row-major) is
+    // split evenly over the 16 warps, row partials meet in shared memory and
+    // the epilogue runs at the end over the CTA's rows.
     const bool pair = a.epi == EPI_SWIGLU || a.epi == EPI_QKV;
-    const int64_t item_rows = P.rpc > 1 ? P.rpc : (pair ? 2 : 1);
-    const int64_t items = (P.n + item_rows - 1) / item_rows;
-    const int64_t gw = (int64_t)blockIdx.x * kGemvWarps + warp, ngw = (int64_t)gridDim.x * kGemvWarps;
-    const int64_t it0 = gw * items / ngw, it1 = (gw + 1) * items / ngw;
-    const int64_t row_begin = it0 * item_rows;
-    const int64_t row_end = min(it1 * item_rows, P.n);
-    const int64_t nq = P.rpc > 1 ? (it1 - it0) : (row_end - row_begin) * P.nchunk;
+    int64_t row_begin, row_end, nq, q_begin = 0;
+    int64_t cr0 = 0, cr1 = 0;
+    if (P.rpc > 1) {
+        const int64_t items = (P.n + P.rpc - 1) / P.rpc;
+        const int64_t gw = (int64_t)blockIdx.x * kGemvWarps + warp, ngw = (int64_t)gridDim.x * kGemvWarps;
+        const int64_t it0 = gw * items / ngw, it1 = (gw + 1) * items / ngw;
+        row_begin = it0 * P.rpc;
+        row_end = min(it1 * P.rpc, P.n);
+        nq = it1 - it0;
+    } else {
+        const int64_t item_rows = pair ? 2 : 1;
+        const int64_t items = (P.n + item_rows - 1) / item_rows;
+        cr0 = (int64_t)blockIdx.x * items / gridDim.x * item_rows;
+        cr1 = min((int64_t)(blockIdx.x + 1) * items / gridDim.x * item_rows, P.n);
+        const int64_t R = cr1 - cr0;
+        int64_t q_end;
+        if (R >= kGemvWarps) {
+            // >= nchunk chunks per warp: a row meets at most two warps
+            const int64_t total = R * P.nchunk;
+            q_begin = (int64_t)warp * total / kGemvWarps;
+            q_end = (int64_t)(warp + 1) * total / kGemvWarps;
+        } else {
+            // few rows: whole rows per warp
+            q_begin = ((int64_t)warp * R / kGemvWarps) * P.nchunk;
+            q_end = ((int64_t)(warp + 1) * R / kGemvWarps) * P.nchunk;
+        }
+        nq = q_end - q_begin;
+        row_begin = cr0 + q_begin / P.nchunk;
+        row_end = cr1;
+    }
+    // Row partials of this CTA (rpc == 1): part0 gets the partial of the warp
+    // that holds the row's first chunk, part1 the rest (at most two warps
+    // share a row; see the launcher), summed in that order.
+    float* part0 = red + kGemvWarps;
+    float* part1 = part0 + (P.rpc > 1 ? 0 : (cr1 - cr0));
 
-    // Lane 0 only: stage chunk q into ring slot s.
-    auto issue = [&](int64_t q, int s) {
+    // Lane 0 only: stage the next chunk into ring slot s.  The issue cursor
+    // (row offset, chunk in row) advances by one chunk per call; the loop
+    // below keeps the same order, so no division is needed on the hot path.
+    int64_t irow = 0;
+    int ic = P.rpc > 1 ? 0 : (int)(q_begin % P.nchunk);
+    auto issue = [&](int s) {
         uint8_t* dst = ring + (int64_t)s * P.stage_bytes;
         uint64_t* bar = &bars[s];
         if (P.rpc > 1) {
-            const int64_t r0 = row_begin + q * P.rpc;
+            const int64_t r0 = row_begin + irow;
             const int64_t nr = min((int64_t)P.rpc, P.n - r0);
             const uint32_t bytes = (uint32_t)(nr * P.rs);
             mbar_arrive_expect_tx(bar, bytes);
             bulk_g2s(dst, a.w + r0 * P.rs, bytes, bar);
+            irow += P.rpc;
         } else {
-            const int64_t row = row_begin + q / P.nchunk;
-            const int u0 = (int)(q % P.nchunk) * P.kc;
+            const int64_t row = row_begin + irow;
+            const int u0 = ic * P.kc;
             const int nu = min(P.kc, P.U - u0);
             const uint8_t* base = a.w + row * P.rs;
             const uint32_t b0 = (uint32_t)(16 * nu);
@@ -275,13 +438,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
                 bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
                 bulk_g2s(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 2 * (int64_t)u0, b1, bar);
             }
+            if (++ic == P.nchunk) {
+                ic = 0;
+                ++irow;
+            }
         }
     };
 
     if (lane == 0) {
         for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
         mbar_fence_init();
-        for (int s = 0; s < S && s < nq; ++s) issue(s, s);
+        for (int s = 0; s < S && s < nq; ++s) issue(s);
     }
 
     // ---- prologue: the activation, once per CTA, into shared memory ----
@@ -328,8 +495,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             uint16_t dh;
             int qs;
             quantize_block32(load, q, d, dh, qs);
-            xq[2 * b] = make_int4(q[0], q[1], q[2], q[3]);
-            xq[2 * b + 1] = make_int4(q[4], q[5], q[6], q[7]);
+            xq[b] = make_int4(q[0], q[1], q[2], q[3]);
+            xq[P.U + b] = make_int4(q[4], q[5], q[6], q[7]);
             xds[b] = make_int2(__float_as_int(d), qs);
             if (a.xq_out != nullptr && blockIdx.x == 0) store_block_q8_0(a.xq_out + (int64_t)b * 34, dh, q);
         }
@@ -354,31 +521,42 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     __syncthreads();  // activation ready; also publishes every warp's barrier init
 
     // ---- stream this warp's chunks ----
-    float acc = 0.f, pend = 0.f;
+    if (P.rpc == 1) {
+        for (int64_t r = tid; r < 2 * (cr1 - cr0); r += kGemvThreads) part0[r] = 0.f;
+        __syncthreads();
+    }
+    float acc = 0.f;
     unsigned long long best = 0ull;
+    int s = 0;
+    uint32_t parity = 0;
+    int64_t crow = 0;                                             // rows consumed (offset from row_begin)
+    int cc = P.rpc > 1 ? 0 : (int)(q_begin % P.nchunk);           // chunk within the row
+    bool first_part = cc == 0;                                    // this warp holds the row's first chunk
+    const int rr = lane >> P.tpr_log2, li = lane & (P.tpr - 1);
     for (int64_t q = 0; q < nq; ++q) {
-        const int s = (int)(q % S);
-        const uint32_t parity = (uint32_t)((q / S) & 1);
         const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[s], parity));
         if (!ok) {
-            if (lane == 0)
-                for (int64_t q2 = q + 1; q2 < nq && q2 < q + S; ++q2)
-                    mbar_wait_bounded(&bars[q2 % S], (uint32_t)((q2 / S) & 1));
-            return;
+            if (lane == 0) {
+                int s2 = s;
+                uint32_t p2 = parity;
+                for (int64_t q2 = q + 1; q2 < nq && q2 < q + S; ++q2) {
+                    if (++s2 == S) {
+                        s2 = 0;
+                        p2 ^= 1u;
+                    }
+                    mbar_wait_bounded(&bars[s2], p2);
+                }
+            }
+            break;  // the status word records the timeout; still meet the CTA barrier below
         }
         const uint8_t* st = ring + (int64_t)s * P.stage_bytes;
         if (P.rpc > 1) {
-            const int64_t r0 = row_begin + q * P.rpc;
-            const int rr = lane / P.tpr, li = lane - rr * P.tpr;
+            const int64_t r0 = row_begin + crow;
             const int nr = (int)min((int64_t)P.rpc, P.n - r0);
             float v = 0.f;
-            if (rr < nr) {
-                const uint8_t* row = st + (int64_t)rr * P.rs;
-                for (int j = 0; j < P.upl; ++j) {
-                    const int u = li + P.tpr * j;
-                    if (u < P.U) v += unit_dot<FMT, DEBUG>(row, P.U, u, u, xr, a.dots, r0 + rr, P.U);
-                }
-            }
+            if (rr < nr)
+                v = chunk_row_dot<FMT, DEBUG>(st + (int64_t)rr * P.rs, P.U, li, P.tpr, P.upl, P.U, 0, xr, P.U,
+                                              a.dots, r0 + rr);
             v = group_sum(v, P.tpr);
             const float vn = __shfl_down_sync(0xffffffffu, v, P.tpr < 32 ? P.tpr : 0);
             if (li == 0 && rr < nr) {
@@ -388,34 +566,45 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
                     epi_row(a, r0 + rr, v, best);
                 }
             }
+            crow += P.rpc;
         } else {
-            const int c = (int)(q % P.nchunk);
-            const int u0 = c * P.kc;
+            const int u0 = cc * P.kc;
             const int nu = min(P.kc, P.U - u0);
-            const int64_t row = row_begin + q / P.nchunk;
-            for (int j = 0; j < P.upl; ++j) {
-                const int i = lane + 32 * j;
-                if (i < nu) acc += unit_dot<FMT, DEBUG>(st, P.kc, i, u0 + i, xr, a.dots, row, P.U);
-            }
-            if (c == P.nchunk - 1) {
+            const int64_t row = row_begin + crow;
+            if (UPL > 0 && nu == P.kc)
+                acc += chunk_full_dot<FMT, DEBUG, (UPL > 0 ? UPL : 2)>(st, P.kc, lane, u0, xr, P.U, a.dots, row);
+            else
+                acc += chunk_row_dot<FMT, DEBUG>(st, P.kc, lane, 32, P.upl, nu, u0, xr, P.U, a.dots, row);
+            const bool row_done = ++cc == P.nchunk;
+            if (row_done || q == nq - 1) {
                 const float v = warp_sum(acc);
                 acc = 0.f;
-                if (lane == 0) {
-                    if (pair) {
-                        if (((row - row_begin) & 1) == 0)
-                            pend = v;
-                        else
-                            epi_pair(a, row - 1, pend, v);
-                    } else {
-                        epi_row(a, row, v, best);
-                    }
+                if (lane == 0) (first_part ? part0 : part1)[row - cr0] = v;
+                if (row_done) {
+                    cc = 0;
+                    ++crow;
+                    first_part = true;
                 }
             }
         }
         __syncwarp();  // every lane is done reading stage s
         if (lane == 0 && q + S < nq) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(q + S, s);
+            issue(s);
+        }
+        if (++s == S) {
+            s = 0;
+            parity ^= 1u;
+        }
+    }
+    if (P.rpc == 1) {
+        __syncthreads();  // all row partials of the CTA are in shared memory
+        const int64_t nrows = cr1 - cr0;
+        if (pair) {
+            for (int64_t r = 2 * (int64_t)tid; r < nrows; r += 2 * kGemvThreads)
+                epi_pair(a, cr0 + r, part0[r] + part1[r], part0[r + 1] + part1[r + 1]);
+        } else {
+            for (int64_t r = tid; r < nrows; r += kGemvThreads) epi_row(a, cr0 + r, part0[r] + part1[r], best);
         }
     }
     if (a.epi == EPI_ARGMAX) {

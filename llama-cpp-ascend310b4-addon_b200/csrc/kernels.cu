@@ -15,6 +15,7 @@
 
 #include "common.cuh"
 #include "fa.cuh"
+#include "fa_mma.cuh"
 #include "gemv.cuh"
 #include "internal.h"
 #include "model_ops.cuh"
@@ -28,7 +29,7 @@ constexpr size_t kSmemBudget = 200 * 1024;
 
 int g_sms[kMaxDevices];
 std::mutex g_attr_mu;
-bool g_attr_done[kMaxDevices][4][2];
+bool g_attr_done[kMaxDevices][4][2][5];
 
 int current_device() {
     int d = 0;
@@ -73,45 +74,78 @@ int cuda_status(cudaError_t e) {
 // Opts a GEMV instantiation into large dynamic shared memory, once per device.
 // Done before any stream capture (b200i_prepare_device) so that capturing a
 // decode step never calls it.
-template <int FMT, bool DEBUG>
+template <int FMT, bool DEBUG, int UPL>
 int set_gemv_attr(int dev) {
     std::lock_guard<std::mutex> lk(g_attr_mu);
-    if (dev < 0 || dev >= kMaxDevices || g_attr_done[dev][FMT][DEBUG ? 1 : 0]) return B200_OK;
-    cudaError_t e =
-        cudaFuncSetAttribute(gemv_kernel<FMT, DEBUG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    const int slot = UPL / 2;  // 0, 2, 4, 6, 8 -> 0..4
+    if (dev < 0 || dev >= kMaxDevices || g_attr_done[dev][FMT][DEBUG ? 1 : 0][slot]) return B200_OK;
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<FMT, DEBUG, UPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024);
     if (e != cudaSuccess) return cuda_status(e);
-    g_attr_done[dev][FMT][DEBUG ? 1 : 0] = true;
+    g_attr_done[dev][FMT][DEBUG ? 1 : 0][slot] = true;
+    return B200_OK;
+}
+
+template <int FMT, bool DEBUG>
+int set_gemv_attrs(int dev) {
+    CR_((set_gemv_attr<FMT, DEBUG, 0>(dev)));
+    CR_((set_gemv_attr<FMT, DEBUG, 2>(dev)));
+    CR_((set_gemv_attr<FMT, DEBUG, 4>(dev)));
+    if constexpr (FMT != FMT_Q8) {
+        CR_((set_gemv_attr<FMT, DEBUG, 6>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 8>(dev)));
+    }
     return B200_OK;
 }
 
 // Shared memory of one GEMV launch: activation region, kGemvWarps rings of
 // `stages` chunks, their barriers, and a small reduction scratch.
-size_t gemv_smem_bytes(int fmt, const GemvPlan& p, int stages) {
+size_t gemv_smem_bytes(int fmt, const GemvPlan& p, int stages, int64_t rows_per_cta) {
     return (size_t)gemv_x_bytes(fmt, p) + (size_t)kGemvWarps * stages * (size_t)p.stage_bytes +
-           (size_t)kGemvWarps * stages * sizeof(uint64_t) + kGemvWarps * sizeof(float);
+           (size_t)kGemvWarps * stages * sizeof(uint64_t) + kGemvWarps * sizeof(float) +
+           (p.rpc > 1 ? 0 : (size_t)(2 * rows_per_cta) * sizeof(float));
 }
 
-template <int FMT, bool DEBUG>
-int launch_gemv_t(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
+template <int FMT, bool DEBUG, int UPL>
+int launch_gemv_u(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
     const int dev = current_device();
-    CR_((set_gemv_attr<FMT, DEBUG>(dev)));
+    CR_((set_gemv_attr<FMT, DEBUG, UPL>(dev)));
     const bool pair = a.epi == EPI_SWIGLU || a.epi == EPI_QKV;
     if (pair && (p.n & 1)) return B200_EINVAL;
     const int64_t item_rows = p.rpc > 1 ? p.rpc : (pair ? 2 : 1);
     const int64_t items = (p.n + item_rows - 1) / item_rows;
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (items + kGemvWarps - 1) / kGemvWarps));
+    const int64_t grid64 = p.rpc > 1 ? std::min<int64_t>(sm_count(dev), (items + kGemvWarps - 1) / kGemvWarps)
+                                     : std::min<int64_t>(sm_count(dev), items);
+    const int grid = (int)std::max<int64_t>(1, grid64);
+    const int64_t rows_per_cta = ((items + grid - 1) / grid) * item_rows;
     int S = kGemvStagesMax;
     const int cap = stage_cap();
     if (cap > 0) S = std::min(S, cap);
-    while (S > 1 && gemv_smem_bytes(FMT, p, S) > (size_t)kGemvSmemBudget) --S;
-    const size_t smem = gemv_smem_bytes(FMT, p, S);
+    while (S > 1 && gemv_smem_bytes(FMT, p, S, rows_per_cta) > (size_t)kGemvSmemBudget) --S;
+    const size_t smem = gemv_smem_bytes(FMT, p, S, rows_per_cta);
     if (smem > 227 * 1024) return B200_EUNSUPPORTED;
     a.p = p;
     a.n = p.n;
     a.k = p.k;
     a.stages = S;
-    gemv_kernel<FMT, DEBUG><<<grid, kGemvThreads, smem, st>>>(a);
+    gemv_kernel<FMT, DEBUG, UPL><<<grid, kGemvThreads, smem, st>>>(a);
     return cuda_status(cudaGetLastError());
+}
+
+template <int FMT, bool DEBUG>
+int launch_gemv_t(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
+    switch (p.full_upl) {
+        case 2: return launch_gemv_u<FMT, DEBUG, 2>(a, p, st);
+        case 4: return launch_gemv_u<FMT, DEBUG, 4>(a, p, st);
+        case 6:
+            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 6>(a, p, st);
+            break;
+        case 8:
+            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 8>(a, p, st);
+            break;
+        default: break;
+    }
+    return launch_gemv_u<FMT, DEBUG, 0>(a, p, st);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -209,12 +243,34 @@ int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st) {
     }
 }
 
+int set_fa_attrs() {
+    static bool done[kMaxDevices];
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    if (dev < 0 || dev >= kMaxDevices || done[dev]) return B200_OK;
+    cudaError_t e = cudaFuncSetAttribute(fa_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)fa_mma_smem_bytes(128));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fa_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)fa_mma_smem_bytes(64));
+    if (e != cudaSuccess) return cuda_status(e);
+    done[dev] = true;
+    return B200_OK;
+}
+
+// head_dim 64 / 128: tensor-core kernel (fa_mma.cuh); 256: CUDA-core kernel (fa.cuh).
 int b200i_fa(const FaArgs& in, int D, cudaStream_t st) {
     FaArgs a = in;
     dim3 grid(a.n_splits, a.Hkv, a.gchunks);
     switch (D) {
-        case 64: fa_decode_kernel<64><<<grid, kFaThreads, 0, st>>>(a); break;
-        case 128: fa_decode_kernel<128><<<grid, kFaThreads, 0, st>>>(a); break;
+        case 64:
+            CR_(set_fa_attrs());
+            fa_mma_kernel<64><<<grid, 128, fa_mma_smem_bytes(64), st>>>(a);
+            break;
+        case 128:
+            CR_(set_fa_attrs());
+            fa_mma_kernel<128><<<grid, 128, fa_mma_smem_bytes(128), st>>>(a);
+            break;
         case 256: fa_decode_kernel<256><<<grid, kFaThreads, 0, st>>>(a); break;
         default: return B200_EUNSUPPORTED;
     }
@@ -223,15 +279,18 @@ int b200i_fa(const FaArgs& in, int D, cudaStream_t st) {
 
 int b200i_sm_count() { return sm_count(current_device()); }
 
+int set_fa_attrs();
+
 int b200i_prepare_device() {
     const int dev = current_device();
     sm_count(dev);
-    CR_((set_gemv_attr<FMT_F16, false>(dev)));
-    CR_((set_gemv_attr<FMT_Q4, false>(dev)));
-    CR_((set_gemv_attr<FMT_Q4W, false>(dev)));
-    CR_((set_gemv_attr<FMT_Q8, false>(dev)));
-    CR_((set_gemv_attr<FMT_Q4, true>(dev)));
-    CR_((set_gemv_attr<FMT_Q8, true>(dev)));
+    CR_((set_gemv_attrs<FMT_F16, false>(dev)));
+    CR_((set_gemv_attrs<FMT_Q4, false>(dev)));
+    CR_((set_gemv_attrs<FMT_Q4W, false>(dev)));
+    CR_((set_gemv_attrs<FMT_Q8, false>(dev)));
+    CR_((set_gemv_attrs<FMT_Q4, true>(dev)));
+    CR_((set_gemv_attrs<FMT_Q8, true>(dev)));
+    CR_(set_fa_attrs());
     return B200_OK;
 }
 
