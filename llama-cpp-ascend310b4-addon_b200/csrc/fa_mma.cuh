@@ -12,14 +12,20 @@
 // K/V chunks of 64 positions stream through a 3-stage cp.async ring (rows
 // past the context are zero-filled).  Each warp owns 16 positions of every
 // chunk and keeps its own online-softmax state (max, sum, output); the four
-// warps are combined at the end, and splits are merged by the last CTA of
-// the (kv head, head chunk), as in fa.cuh.
+// warps are combined in shared memory.  The splits of one (kv head, head
+// chunk) form one thread-block cluster: after a cluster barrier every CTA
+// merges a slice of the outputs by reading its peers' partial results through
+// distributed shared memory, so partials never leave the SMs.
 #pragma once
+
+#include <cooperative_groups.h>
 
 #include "args.h"
 #include "common.cuh"
 
 namespace b200 {
+
+namespace cgx = cooperative_groups;
 
 constexpr int kFmStages = 3;
 
@@ -61,8 +67,14 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 }
 
 // Shared memory of fa_mma_kernel<D>: kFmStages x (K tile + V tile) of
-// kFaChunk rows x D halves; reused after the loop for the warp combine.
-B200_HD inline size_t fa_mma_smem_bytes(int D) { return (size_t)kFmStages * 2 * kFaChunk * D * 2; }
+// kFaChunk rows x D halves; reused after the loop for the warp combine and
+// the cluster merge (which need 5 x kFaMaxG x D floats plus 40 x kFaMaxG).
+constexpr int kFmMaxCluster = 16;
+B200_HD inline size_t fa_mma_smem_bytes(int D) {
+    const size_t ring = (size_t)kFmStages * 2 * kFaChunk * D * 2;
+    const size_t merge = ((size_t)5 * kFaMaxG * D + 48 * kFaMaxG) * sizeof(float);
+    return ring > merge ? ring : merge;
+}
 
 template <int D>
 __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
@@ -73,7 +85,6 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
     constexpr int TILE = kFaChunk * ROWB;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float wm[4][kFaMaxG], wl[4][kFaMaxG];
-    __shared__ int is_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -224,8 +235,13 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
         cp_async_wait<0>();
     }
 
-    // ---- combine the 4 warps (shared memory re-used) ----
-    float* wo = reinterpret_cast<float*>(smem);  // [4][kFaMaxG][D]
+    // ---- combine the 4 warps into this CTA's partial (shared memory re-used) ----
+    float* wo = reinterpret_cast<float*>(smem);             // [4][kFaMaxG][D]
+    float* co = wo + 4 * kFaMaxG * D;                         // [kFaMaxG][D]  this CTA's partial
+    float* wr = co + kFaMaxG * D;                             // [kFaMaxG][16] merge weights
+    float* allm = wr + kFaMaxG * 16;                          // [16][kFaMaxG]
+    float* alll = allm + 16 * kFaMaxG;                        // [16][kFaMaxG]
+    __shared__ float cm[kFaMaxG], cl[kFaMaxG];
     __syncthreads();
     if (t == 0) {
         wm[warp][g] = m_run;
@@ -237,77 +253,66 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
         wo[((warp * kFaMaxG) + g) * D + 8 * n + 2 * t + 1] = o[n][1];
     }
     __syncthreads();
-    if (active) {
-        for (int idx = tid; idx < hn * D; idx += 128) {
-            const int h = idx / D, d = idx - (idx / D) * D;
-            float M = -INFINITY;
+    for (int idx = tid; idx < kFaMaxG * D; idx += 128) {
+        const int h = idx / D, d = idx - (idx / D) * D;
+        float M = -INFINITY;
+        if (active && h < hn)
 #pragma unroll
             for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][h]);
-            float ov = 0.f, lv = 0.f;
-            if (M != -INFINITY) {
+        float ov = 0.f, lv = 0.f;
+        if (M != -INFINITY) {
 #pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    const float e = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
-                    ov = fmaf(wo[((w * kFaMaxG) + h) * D + d], e, ov);
-                    lv = fmaf(wl[w][h], e, lv);
-                }
+            for (int w = 0; w < 4; ++w) {
+                const float e = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
+                ov = fmaf(wo[((w * kFaMaxG) + h) * D + d], e, ov);
+                lv = fmaf(wl[w][h], e, lv);
             }
-            a.part_o[((int64_t)split * a.Hq + h0 + h) * D + d] = ov;
-            if (d == 0) {
-                a.part_ml[((int64_t)split * a.Hq + h0 + h) * 2 + 0] = M;
-                a.part_ml[((int64_t)split * a.Hq + h0 + h) * 2 + 1] = lv;
-            }
+        }
+        co[h * D + d] = ov;
+        if (d == 0) {
+            cm[h] = M;
+            cl[h] = lv;
         }
     }
 
-    // ---- ticket: the last CTA of this (kv head, chunk) merges the splits ----
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        unsigned int* tk = a.tickets + hk * a.gchunks + gc;
-        const unsigned int old = atomicAdd(tk, 1u);
-        is_last = old == (unsigned int)(a.n_splits - 1);
-        if (is_last) *tk = 0u;
+    // ---- cluster merge over the splits (distributed shared memory) ----
+    cgx::cluster_group cluster = cgx::this_cluster();
+    const int S = (int)cluster.num_blocks();
+    const int rank = (int)cluster.block_rank();
+    cluster.sync();  // every CTA's partial is complete and visible
+    if (tid < S * kFaMaxG) {
+        const int r = tid / kFaMaxG, h = tid - (tid / kFaMaxG) * kFaMaxG;
+        allm[r * kFaMaxG + h] = *cluster.map_shared_rank(&cm[h], r);
+        alll[r * kFaMaxG + h] = *cluster.map_shared_rank(&cl[h], r);
     }
     __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-
-    const int n_act = (nchunks_ctx + a.chunks_per_split - 1) / a.chunks_per_split;
-    float* wts = reinterpret_cast<float*>(smem);  // [kFaMaxG][n_act]
-    for (int h = warp; h < hn; h += 4) {
+    if (tid < hn) {
+        const int h = tid;
         float M = -INFINITY;
-        for (int s2 = lane; s2 < n_act; s2 += 32) M = fmaxf(M, __ldcg(&a.part_ml[((int64_t)s2 * a.Hq + h0 + h) * 2]));
-        M = warp_max(M);
+        for (int r = 0; r < S; ++r) M = fmaxf(M, allm[r * kFaMaxG + h]);
         float L = 0.f;
-        for (int s2 = lane; s2 < n_act; s2 += 32) {
-            const float ms = __ldcg(&a.part_ml[((int64_t)s2 * a.Hq + h0 + h) * 2]);
-            const float ls = __ldcg(&a.part_ml[((int64_t)s2 * a.Hq + h0 + h) * 2 + 1]);
-            const float e = (ms == -INFINITY) ? 0.f : expf(ms - M);
-            wts[h * n_act + s2] = e;
-            L += ls * e;
+        for (int r = 0; r < S; ++r) {
+            const float mr = allm[r * kFaMaxG + h];
+            const float e = (mr == -INFINITY) ? 0.f : expf(mr - M);
+            wr[h * 16 + r] = e;
+            L = fmaf(alll[r * kFaMaxG + h], e, L);
         }
-        L = warp_sum(L);
-        const float inv = (L > 0.f) ? 1.0f / L : 0.f;
-        __syncwarp();
-        for (int s2 = lane; s2 < n_act; s2 += 32) wts[h * n_act + s2] *= inv;
+        const float inv = L > 0.f ? 1.0f / L : 0.f;
+        for (int r = 0; r < S; ++r) wr[h * 16 + r] *= inv;
     }
     __syncthreads();
-    for (int idx = tid; idx < hn * D; idx += 128) {
+    const int tot = hn * D;
+    const int o0 = rank * tot / S, o1 = (rank + 1) * tot / S;
+    for (int idx = o0 + tid; idx < o1; idx += 128) {
         const int h = idx / D, d = idx - (idx / D) * D;
-        const float* po = a.part_o + (int64_t)(h0 + h) * D + d;
-        const int64_t stride = (int64_t)a.Hq * D;
-        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-        int s2 = 0;
-        for (; s2 + 4 <= n_act; s2 += 4) {
-            o0 = fmaf(__ldcg(po + (int64_t)(s2 + 0) * stride), wts[h * n_act + s2 + 0], o0);
-            o1 = fmaf(__ldcg(po + (int64_t)(s2 + 1) * stride), wts[h * n_act + s2 + 1], o1);
-            o2 = fmaf(__ldcg(po + (int64_t)(s2 + 2) * stride), wts[h * n_act + s2 + 2], o2);
-            o3 = fmaf(__ldcg(po + (int64_t)(s2 + 3) * stride), wts[h * n_act + s2 + 3], o3);
+        float acc = 0.f;
+        for (int r = 0; r < S; ++r) {
+            const float w = wr[h * 16 + r];
+            if (w != 0.f) acc = fmaf(*cluster.map_shared_rank(co + h * D + d, r), w, acc);
         }
-        for (; s2 < n_act; ++s2) o0 = fmaf(__ldcg(po + (int64_t)s2 * stride), wts[h * n_act + s2], o0);
-        a.out[(int64_t)(h0 + h) * D + d] = (o0 + o1) + (o2 + o3);
+        a.out[(int64_t)(h0 + h) * D + d] = acc;
     }
+    cluster.sync();  // peers finish reading this CTA's shared memory before it exits
 }
 
 }  // namespace b200

@@ -243,38 +243,93 @@ int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st) {
     }
 }
 
-int set_fa_attrs() {
-    static bool done[kMaxDevices];
-    const int dev = current_device();
-    std::lock_guard<std::mutex> lk(g_attr_mu);
-    if (dev < 0 || dev >= kMaxDevices || done[dev]) return B200_OK;
-    cudaError_t e = cudaFuncSetAttribute(fa_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)fa_mma_smem_bytes(128));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(fa_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)fa_mma_smem_bytes(64));
+// Largest cluster (<= 16 CTAs) that the device can schedule for the
+// tensor-core attention kernel, per head dim; set once per device.
+int g_fa_cluster[kMaxDevices][2];
+
+template <int D>
+int fa_cluster_size(int dev) {
+    const int slot = D == 64 ? 0 : 1;
+    if (g_fa_cluster[dev][slot] > 0) return g_fa_cluster[dev][slot];
+    cudaError_t e = cudaFuncSetAttribute(fa_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)fa_mma_smem_bytes(D));
     if (e != cudaSuccess) return cuda_status(e);
-    done[dev] = true;
-    return B200_OK;
+    e = cudaFuncSetAttribute(fa_mma_kernel<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    int best = 1;
+    for (int cs = e == cudaSuccess ? kFmMaxCluster : 8; cs >= 2; cs >>= 1) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(cs, 1, 1);
+        cfg.blockDim = dim3(128, 1, 1);
+        cfg.dynamicSmemBytes = fa_mma_smem_bytes(D);
+        cudaLaunchAttribute at;
+        at.id = cudaLaunchAttributeClusterDimension;
+        at.val.clusterDim.x = cs;
+        at.val.clusterDim.y = 1;
+        at.val.clusterDim.z = 1;
+        cfg.attrs = &at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, fa_mma_kernel<D>, &cfg) == cudaSuccess && n > 0) {
+            best = cs;
+            break;
+        }
+    }
+    cudaGetLastError();
+    g_fa_cluster[dev][slot] = best;
+    return best;
 }
 
-// head_dim 64 / 128: tensor-core kernel (fa_mma.cuh); 256: CUDA-core kernel (fa.cuh).
+int set_fa_attrs() {
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return B200_EINVAL;
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    const int a = fa_cluster_size<64>(dev);
+    const int b = fa_cluster_size<128>(dev);
+    return (a < 0) ? a : (b < 0 ? b : B200_OK);
+}
+
+template <int D>
+int launch_fa_mma(FaArgs a, cudaStream_t st) {
+    const int dev = current_device();
+    int cs;
+    {
+        std::lock_guard<std::mutex> lk(g_attr_mu);
+        cs = fa_cluster_size<D>(dev);
+    }
+    if (cs < 0) return cs;
+    const int nchunks = (a.n_kv + kFaChunk - 1) / kFaChunk;
+    const int S = std::max(1, std::min(cs, nchunks));
+    a.n_splits = S;
+    a.chunks_per_split = (nchunks + S - 1) / S;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, a.Hkv, a.gchunks);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.dynamicSmemBytes = fa_mma_smem_bytes(D);
+    cfg.stream = st;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = S;
+    at.val.clusterDim.y = 1;
+    at.val.clusterDim.z = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, fa_mma_kernel<D>, a));
+}
+
+// head_dim 64 / 128: tensor-core cluster kernel (fa_mma.cuh); 256: CUDA-core
+// kernel with global partials (fa.cuh).
 int b200i_fa(const FaArgs& in, int D, cudaStream_t st) {
     FaArgs a = in;
-    dim3 grid(a.n_splits, a.Hkv, a.gchunks);
     switch (D) {
-        case 64:
-            CR_(set_fa_attrs());
-            fa_mma_kernel<64><<<grid, 128, fa_mma_smem_bytes(64), st>>>(a);
-            break;
-        case 128:
-            CR_(set_fa_attrs());
-            fa_mma_kernel<128><<<grid, 128, fa_mma_smem_bytes(128), st>>>(a);
-            break;
-        case 256: fa_decode_kernel<256><<<grid, kFaThreads, 0, st>>>(a); break;
+        case 64: return launch_fa_mma<64>(a, st);
+        case 128: return launch_fa_mma<128>(a, st);
+        case 256: {
+            dim3 grid(a.n_splits, a.Hkv, a.gchunks);
+            fa_decode_kernel<256><<<grid, kFaThreads, 0, st>>>(a);
+            return cuda_status(cudaGetLastError());
+        }
         default: return B200_EUNSUPPORTED;
     }
-    return cuda_status(cudaGetLastError());
 }
 
 int b200i_sm_count() { return sm_count(current_device()); }
