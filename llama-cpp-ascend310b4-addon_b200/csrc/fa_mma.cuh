@@ -122,21 +122,25 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
                 qa[kt][1] = hv ? pack_half2(x1.x, x1.y) : 0u;
             }
         }
+        // Each thread always copies granule cg = tid % GR of rows
+        // tid / GR + (128 / GR) i, so its source offsets and the swizzled
+        // destination column are fixed for the whole split.
+        constexpr int RPI = 128 / GR;  // rows covered per pass
+        const int cg = tid % GR, r0 = tid / GR;
+        const uint32_t swz = (uint32_t)((cg ^ (r0 & 7)) << 4);  // (r0 + RPI i) & 7 == r0 & 7
+        const uint8_t* kb = a.k + (int64_t)hk * a.k_nb2 + cg * 16;
+        const uint8_t* vb = a.v + (int64_t)hk * a.v_nb2 + cg * 16;
         auto load_chunk = [&](int c, int stage) {
-            const uint32_t kst = sbase + (uint32_t)(stage * 2 * TILE);
+            const uint32_t kst = sbase + (uint32_t)(stage * 2 * TILE) + (uint32_t)(r0 * ROWB) + swz;
             const uint32_t vst = kst + TILE;
-            const int p0 = c * kFaChunk;
+            const int p0 = c * kFaChunk + r0;
+            const uint8_t* kp = kb + (int64_t)p0 * a.k_nb1;
+            const uint8_t* vp = vb + (int64_t)p0 * a.v_nb1;
 #pragma unroll
-            for (int i = 0; i < kFaChunk * GR / 128; ++i) {
-                const int idx = tid + 128 * i;
-                const int r = idx / GR, cg = idx - (idx / GR) * GR;
-                const int p = p0 + r;
-                const bool ok = p < ctx;
-                const uint32_t off = (uint32_t)(r * ROWB + ((cg ^ (r & 7)) << 4));
-                const uint8_t* ks = a.k + (ok ? ((int64_t)p * a.k_nb1 + (int64_t)hk * a.k_nb2 + cg * 16) : 0);
-                const uint8_t* vs = a.v + (ok ? ((int64_t)p * a.v_nb1 + (int64_t)hk * a.v_nb2 + cg * 16) : 0);
-                cp_async16(kst + off, ks, ok ? 16 : 0);
-                cp_async16(vst + off, vs, ok ? 16 : 0);
+            for (int i = 0; i < kFaChunk / RPI; ++i) {
+                const bool ok = p0 + RPI * i < ctx;
+                cp_async16(kst + (uint32_t)(RPI * i * ROWB), ok ? kp + (int64_t)RPI * i * a.k_nb1 : a.k, ok ? 16 : 0);
+                cp_async16(vst + (uint32_t)(RPI * i * ROWB), ok ? vp + (int64_t)RPI * i * a.v_nb1 : a.v, ok ? 16 : 0);
             }
         };
         const int nc = c_end - c_begin;

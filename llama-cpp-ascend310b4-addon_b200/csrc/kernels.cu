@@ -243,20 +243,24 @@ int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st) {
     }
 }
 
-// Largest cluster (<= 16 CTAs) that the device can schedule for the
-// tensor-core attention kernel, per head dim; set once per device.
-int g_fa_cluster[kMaxDevices][2];
+// How many clusters of each size (16, 8, 4, 2 CTAs) of the tensor-core
+// attention kernel can be resident at once, per head dim; set once per device.
+int g_fa_active[kMaxDevices][2][5];
+bool g_fa_ready[kMaxDevices][2];
 
 template <int D>
-int fa_cluster_size(int dev) {
+int fa_cluster_probe(int dev) {
     const int slot = D == 64 ? 0 : 1;
-    if (g_fa_cluster[dev][slot] > 0) return g_fa_cluster[dev][slot];
+    if (g_fa_ready[dev][slot]) return B200_OK;
     cudaError_t e = cudaFuncSetAttribute(fa_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)fa_mma_smem_bytes(D));
     if (e != cudaSuccess) return cuda_status(e);
-    e = cudaFuncSetAttribute(fa_mma_kernel<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    int best = 1;
-    for (int cs = e == cudaSuccess ? kFmMaxCluster : 8; cs >= 2; cs >>= 1) {
+    const bool nonportable =
+        cudaFuncSetAttribute(fa_mma_kernel<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+    for (int li = 0; li < 5; ++li) {
+        const int cs = 16 >> li;  // 16, 8, 4, 2, 1
+        g_fa_active[dev][slot][li] = 0;
+        if (cs > 8 && !nonportable) continue;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(cs, 1, 1);
         cfg.blockDim = dim3(128, 1, 1);
@@ -269,36 +273,50 @@ int fa_cluster_size(int dev) {
         cfg.attrs = &at;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, fa_mma_kernel<D>, &cfg) == cudaSuccess && n > 0) {
-            best = cs;
-            break;
-        }
+        if (cudaOccupancyMaxActiveClusters(&n, fa_mma_kernel<D>, &cfg) == cudaSuccess) g_fa_active[dev][slot][li] = n;
     }
     cudaGetLastError();
-    g_fa_cluster[dev][slot] = best;
-    return best;
+    if (g_fa_active[dev][slot][4] <= 0) g_fa_active[dev][slot][4] = 1;
+    g_fa_ready[dev][slot] = true;
+    return B200_OK;
+}
+
+// Cluster size for `needed` clusters over `nchunks` chunks: the largest size
+// whose clusters all fit on the device at once, else the one that keeps the
+// most CTAs resident.
+template <int D>
+int fa_pick_cluster(int dev, int needed, int nchunks) {
+    const int slot = D == 64 ? 0 : 1;
+    int best = 1, best_ctas = 0;
+    for (int li = 0; li < 5; ++li) {
+        const int cs = 16 >> li;
+        const int act = g_fa_active[dev][slot][li];
+        if (act <= 0) continue;
+        const int use = std::min(cs, nchunks);
+        if (act >= needed) return std::max(1, use);
+        const int ctas = act * use;
+        if (ctas > best_ctas) {
+            best_ctas = ctas;
+            best = use;
+        }
+    }
+    return std::max(1, best);
 }
 
 int set_fa_attrs() {
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return B200_EINVAL;
     std::lock_guard<std::mutex> lk(g_attr_mu);
-    const int a = fa_cluster_size<64>(dev);
-    const int b = fa_cluster_size<128>(dev);
-    return (a < 0) ? a : (b < 0 ? b : B200_OK);
+    CR_(fa_cluster_probe<64>(dev));
+    return fa_cluster_probe<128>(dev);
 }
 
 template <int D>
 int launch_fa_mma(FaArgs a, cudaStream_t st) {
     const int dev = current_device();
-    int cs;
-    {
-        std::lock_guard<std::mutex> lk(g_attr_mu);
-        cs = fa_cluster_size<D>(dev);
-    }
-    if (cs < 0) return cs;
+    CR_(set_fa_attrs());
     const int nchunks = (a.n_kv + kFaChunk - 1) / kFaChunk;
-    const int S = std::max(1, std::min(cs, nchunks));
+    const int S = fa_pick_cluster<D>(dev, a.Hkv * a.gchunks, nchunks);
     a.n_splits = S;
     a.chunks_per_split = (nchunks + S - 1) / S;
     cudaLaunchConfig_t cfg = {};
