@@ -122,6 +122,34 @@ int b200_fa_decode(const float *q, const void *k, const void *v, const void *mas
                    int64_t v_nb1, int64_t v_nb2, float scale, void *workspace, size_t workspace_size,
                    b200_stream_t stream);
 
+/* Allocation-free FLASH_ATTN_EXT (no counterpart in the reference: the
+ * reference's attention always takes its scratch from the CANN memory pool).
+ *
+ * For callers that cannot allocate device memory when attention runs: a
+ * plugin inside an engine whose pool owns every byte of the GPU and must not
+ * see foreign allocations, code that runs between another component's
+ * allocations and must not shift them, and hosts that link only the kernels
+ * and have no buffer to lend.  Arguments and results are those of
+ * b200_fa_decode, minus the workspace; the split-KV partials go to a fixed
+ * B200_FA_STATIC_SCRATCH_BYTES array inside the library's device image, which
+ * every GPU that loads the library holds until the process exits.
+ *   - Calls whose b200_fa_workspace_size exceeds that size return
+ *     B200_ESCRATCH and launch nothing.
+ *   - The first call on a device looks up the array's device address (no
+ *     allocation); make that first call before any stream capture.
+ *   - One array per device is shared by every call on that device: calls that
+ *     overlap on the GPU (other streams, other threads) race and corrupt each
+ *     other's results.  Calls in one stream are ordered and safe; each call
+ *     clears its own counters first, so an earlier call's leftovers do not
+ *     matter.
+ * Every head_dim (64, 128, 256) uses the CUDA-core split-KV kernel. */
+#define B200_ESCRATCH (-7) /* request larger than a fixed static scratch array */
+#define B200_FA_STATIC_SCRATCH_BYTES ((size_t)4 << 20)
+int b200_fa_decode_static_scratch(const float *q, const void *k, const void *v, const void *mask,
+                                  const int32_t *kv_len, float *out, int head_dim, int n_head, int n_head_kv,
+                                  int n_kv, int64_t k_nb1, int64_t k_nb2, int64_t v_nb1, int64_t v_nb2, float scale,
+                                  b200_stream_t stream);
+
 /* Host helper mirroring llama-graph.cpp set_input_kv_lengths_impl
  * (patch:2900-2916): out[r] = 1 + index of the last finite entry of mask row
  * r (at least 1).  mask f16 host array [n_rows][n_kv]. */

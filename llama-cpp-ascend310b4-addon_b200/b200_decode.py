@@ -36,6 +36,8 @@ OK = 0
 EINVAL = -1
 ECUDA = -2
 EUNSUPPORTED = -3
+ESCRATCH = -7
+FA_STATIC_SCRATCH_BYTES = 4 << 20
 
 _lib = None
 
@@ -85,6 +87,10 @@ def _declare(L):
         "b200_fa_decode": (
             C.c_int,
             [P, P, P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, I64, I64, I64, I64, C.c_float, P, C.c_size_t, P],
+        ),
+        "b200_fa_decode_static_scratch": (
+            C.c_int,
+            [P, P, P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, I64, I64, I64, I64, C.c_float, P],
         ),
         "b200_kv_lengths_from_mask_f16": (C.c_int, [P, I64, I64, P]),
     }
@@ -248,6 +254,32 @@ def flash_attn_ext(q, k, v, mask=None, scale: float = 1.0, max_bias: float = 0.0
         _ptr(workspace), workspace.numel(), _stream(q.device),
     )
     _check(rc, "flash_attn_ext")
+    return out
+
+
+def flash_attn_ext_static_scratch(q, k, v, mask=None, scale: float = 1.0, kv_lengths=None, out=None):
+    """flash_attn_ext that allocates nothing on the device.
+
+    For hosts that cannot hand over or allocate a workspace: the partials go
+    to the library's fixed per-device static array (FA_STATIC_SCRATCH_BYTES).
+    Calls larger than that raise B200Error(ESCRATCH); calls that overlap on
+    one GPU share the array and race.  Only ``out`` may be allocated here, and
+    only when the caller passes none."""
+    torch = _torch()
+    hq, d = q.shape
+    n_kv, hkv, d2 = k.shape
+    if d2 != d or tuple(v.shape) != tuple(k.shape):
+        raise B200Error(EINVAL, "flash_attn_ext_static_scratch shapes")
+    if k.stride(2) != 1 or v.stride(2) != 1 or not q.is_contiguous():
+        raise B200Error(EINVAL, "flash_attn_ext_static_scratch needs contiguous q and head dim")
+    if out is None:
+        out = torch.empty((hq, d), dtype=torch.float32, device=q.device)
+    es = k.element_size()
+    rc = lib().b200_fa_decode_static_scratch(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(mask), _ptr(kv_lengths), _ptr(out), d, hq, hkv, n_kv,
+        k.stride(0) * es, k.stride(1) * es, v.stride(0) * es, v.stride(1) * es, float(scale), _stream(q.device),
+    )
+    _check(rc, "flash_attn_ext_static_scratch")
     return out
 
 

@@ -416,6 +416,7 @@ const char* b200_strerror(int code) {
         case B200_ENOMEM: return "out of memory";
         case B200_ENCCL: return "NCCL error";
         case B200_ESTATE: return "invalid state";
+        case B200_ESCRATCH: return "request exceeds the fixed static scratch (B200_FA_STATIC_SCRATCH_BYTES)";
         default: return "unknown status";
     }
 }
@@ -556,3 +557,86 @@ int b200_fa_decode(const float* q, const void* k, const void* v, const void* mas
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free attention for callers that may not allocate device memory
+// (an engine's pool owns the GPU; the caller runs between another
+// component's allocations; the host links only the kernels).  The split-KV
+// partials and merge tickets live in this fixed array of the module's device
+// image: each GPU that loads the library holds its own copy until exit.
+// In host code `g_fa_static_scratch` is only a handle for the runtime; the
+// device address comes from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_fa_static_scratch[B200_FA_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_static_scratch_mu;
+unsigned char* g_static_scratch_dev[kMaxDevices];
+
+// Device address of g_fa_static_scratch on the current device, looked up on
+// the first call there (with that device current) and cached.
+int static_scratch(unsigned char** out) {
+    int dev = -1;
+    CR_(cuda_status(cudaGetDevice(&dev)));
+    if (dev < 0 || dev >= kMaxDevices) return B200_EINVAL;
+    std::lock_guard<std::mutex> lk(g_static_scratch_mu);
+    if (g_static_scratch_dev[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_fa_static_scratch);
+        if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? cuda_status(e) : B200_ECUDA;
+        g_static_scratch_dev[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = g_static_scratch_dev[dev];
+    return B200_OK;
+}
+
+}  // namespace
+
+extern "C" int b200_fa_decode_static_scratch(const float* q, const void* k, const void* v, const void* mask,
+                                             const int32_t* kv_len, float* out, int head_dim, int n_head,
+                                             int n_head_kv, int n_kv, int64_t k_nb1, int64_t k_nb2, int64_t v_nb1,
+                                             int64_t v_nb2, float scale, b200_stream_t stream) {
+    if (!q || !k || !v || !out) return B200_EINVAL;
+    if (n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv || n_kv <= 0) return B200_EINVAL;
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256) return B200_EUNSUPPORTED;
+    if (!aligned16(k) || !aligned16(v) || (k_nb1 & 15) || (k_nb2 & 15) || (v_nb1 & 15) || (v_nb2 & 15))
+        return B200_EINVAL;
+    const FaLayout L = fa_layout(head_dim, n_head, n_head_kv, n_kv);
+    if (L.total > B200_FA_STATIC_SCRATCH_BYTES) return B200_ESCRATCH;
+    unsigned char* ws = nullptr;
+    CR_(static_scratch(&ws));
+    const cudaStream_t st = (cudaStream_t)stream;
+    // The merge tickets must start at zero; the partials are written before
+    // they are read.
+    CR_(cuda_status(cudaMemsetAsync(ws + L.off_tickets, 0, (size_t)n_head_kv * L.gchunks * sizeof(unsigned int), st)));
+    FaArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = q;
+    a.k = static_cast<const uint8_t*>(k);
+    a.v = static_cast<const uint8_t*>(v);
+    a.mask = static_cast<const uint16_t*>(mask);
+    a.kv_len = kv_len;
+    a.out = out;
+    a.Hq = n_head;
+    a.Hkv = n_head_kv;
+    a.G = n_head / n_head_kv;
+    a.gchunks = L.gchunks;
+    a.n_kv = n_kv;
+    a.n_splits = L.n_splits;
+    a.chunks_per_split = L.chunks_per_split;
+    a.k_nb1 = k_nb1;
+    a.k_nb2 = k_nb2;
+    a.v_nb1 = v_nb1;
+    a.v_nb2 = v_nb2;
+    a.scale = scale;
+    a.part_o = reinterpret_cast<float*>(ws + L.off_o);
+    a.part_ml = reinterpret_cast<float*>(ws + L.off_ml);
+    a.tickets = reinterpret_cast<unsigned int*>(ws + L.off_tickets);
+    const dim3 grid(L.n_splits, n_head_kv, L.gchunks);
+    switch (head_dim) {
+        case 64: fa_decode_kernel<64><<<grid, kFaThreads, 0, st>>>(a); break;
+        case 128: fa_decode_kernel<128><<<grid, kFaThreads, 0, st>>>(a); break;
+        default: fa_decode_kernel<256><<<grid, kFaThreads, 0, st>>>(a); break;
+    }
+    return cuda_status(cudaGetLastError());
+}
