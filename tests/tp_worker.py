@@ -1,0 +1,139 @@
+"""One rank of the tensor-parallel model parity check (run by torchrun).
+
+Every rank builds its shard of the same synthetic model (b200_model_create
+with tp_world = WORLD_SIZE, NCCL over the GPUs), runs layer-dump steps and
+captured-graph greedy steps -- the same collective sequence on every rank --
+and sends its shards and dumps to rank 0 over a CPU (gloo) group.  Rank 0
+reassembles the unsharded weights, caches and activations, checks every stage
+against the oracle per layer (teacher forced), and writes a JSON report.
+
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
+        --master-port P tests/tp_worker.py --out report.json
+"""
+import argparse
+import datetime
+import json
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+sys.path[:0] = [HERE, os.path.join(ROOT, "llama-cpp-ascend310b4-addon_b200"), os.path.join(ROOT, "oracle")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+SHAPES = {
+    "small": dict(n_layer=2, d_model=512, n_head=8, n_head_kv=2, head_dim=64, d_ff=1024, vocab=2048, kv_size=96),
+    "llama70b": dict(n_layer=2, d_model=8192, n_head=64, n_head_kv=8, head_dim=128, d_ff=28672, vocab=128256,
+                     kv_size=4224),
+}
+N_PREFILL = {"small": 40, "llama70b": 4096}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--shape", default="small", choices=list(SHAPES))
+    args = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+
+    import decode_model as M
+
+    cfg = M.LlamaConfig(**SHAPES[args.shape])
+    n_prefill = N_PREFILL[args.shape]
+    obj = [M.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    m = M.DecodeModel(cfg, device=local, tp_rank=rank, tp_world=world, nccl_id=obj[0])
+    m.init_synthetic(seed=11, sigma=0.02)
+    m.fill_kv_synthetic(seed=12, n_pos=n_prefill)
+
+    L = cfg.n_layer
+    mine = {"w": {}, "kv": [], "steps": [], "greedy": []}
+    for which in (M.W_TOK_EMBD, M.W_LM_HEAD):
+        mine["w"][(which, -1)] = m.export_weight(which)
+    for which in (M.W_Q, M.W_K, M.W_V, M.W_O, M.W_GATE, M.W_UP, M.W_DOWN):
+        for l in range(L):
+            mine["w"][(which, l)] = m.export_weight(which, l)
+    for l in range(L):
+        mine["kv"].append((m.export_kv(l, 0, n_prefill), m.export_kv(l, 1, n_prefill)))
+
+    toks = [3, 1999] if args.shape == "small" else [128000, 9906]
+    for i, t in enumerate(toks):
+        x, q, a = m.debug_step(t, n_prefill + i)
+        off, logits = m.logits()
+        mine["steps"].append((t, n_prefill + i, x, q, a, off, logits))
+
+    m.capture()
+    t = 42
+    for i in range(4):
+        t = m.decode(t, n_prefill + len(toks) + i)
+        mine["greedy"].append(int(t))
+    torch.cuda.synchronize()
+    status = int(__import__("b200_decode").device_status(reset=True))
+
+    gathered = [None] * world if rank == 0 else None
+    dist.gather_object(mine, gathered, dst=0)
+    dist.barrier()
+    m.close()
+
+    if rank == 0:
+        report = {"world": world, "shape": args.shape, "status": status,
+                  "greedy": [g["greedy"] for g in gathered]}
+        report.update(check(cfg, n_prefill, gathered, M))
+        with open(args.out, "w") as f:
+            json.dump(report, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def check(cfg, n_prefill, parts, M):
+    from model_ref import per_layer_errors
+
+    L = cfg.n_layer
+    d = cfg.d_model
+
+    def rows(which, l):
+        return np.concatenate([p["w"][(which, l)].reshape(-1, d // 32 * 18) for p in parts]).reshape(-1)
+
+    def cols(which, l):
+        return np.concatenate([p["w"][(which, l)].reshape(d, -1) for p in parts], axis=1).reshape(-1)
+
+    W = {"tok_embd": parts[0]["w"][(M.W_TOK_EMBD, -1)], "lm_head": rows(M.W_LM_HEAD, -1)}
+    for key, which in (("wq", M.W_Q), ("wk", M.W_K), ("wv", M.W_V), ("wgate", M.W_GATE), ("wup", M.W_UP)):
+        W[key] = [np.ascontiguousarray(rows(which, l)) for l in range(L)]
+    for key, which in (("wo", M.W_O), ("wdown", M.W_DOWN)):
+        W[key] = [np.ascontiguousarray(cols(which, l)) for l in range(L)]
+    W["attn_norm"] = [np.ones(d, np.float32) for _ in range(L)]
+    W["ffn_norm"] = [np.ones(d, np.float32) for _ in range(L)]
+    W["out_norm"] = np.ones(d, np.float32)
+    kvd = cfg.n_head_kv * cfg.head_dim
+    kc, vc = [], []
+    for l in range(L):
+        k = np.zeros((cfg.kv_size, kvd), np.float16)
+        v = np.zeros((cfg.kv_size, kvd), np.float16)
+        k[:n_prefill] = np.concatenate([p["kv"][l][0] for p in parts], axis=1)
+        v[:n_prefill] = np.concatenate([p["kv"][l][1] for p in parts], axis=1)
+        kc.append(k)
+        vc.append(v)
+    out = {"stages": [], "x_replicated": True, "logit_offsets": []}
+    for s in range(len(parts[0]["steps"])):
+        t, pos = parts[0]["steps"][s][:2]
+        x = parts[0]["steps"][s][2]
+        for p in parts[1:]:
+            out["x_replicated"] &= bool(np.array_equal(p["steps"][s][2], x))
+        q = np.concatenate([p["steps"][s][3] for p in parts], axis=1)
+        a = np.concatenate([p["steps"][s][4] for p in parts], axis=1)
+        out["logit_offsets"].append([int(p["steps"][s][5]) for p in parts])
+        logits = np.concatenate([p["steps"][s][6] for p in parts])
+        e = per_layer_errors(cfg, W, kc, vc, x, q, a, logits, t, pos)
+        out["stages"].append({k: [float(v[0]), float(v[1])] for k, v in e.items()})
+    return out
+
+
+if __name__ == "__main__":
+    main()
