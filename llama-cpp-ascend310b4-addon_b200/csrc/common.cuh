@@ -81,6 +81,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 __device__ __forceinline__ void record_status(unsigned int bit) { atomicOr(&g_status, bit); }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while the previous kernel in the stream is still
+// finishing; griddep_wait() returns once that kernel has completed and its
+// writes are visible.  Everything before it may read only data no earlier
+// kernel writes (weights) and write only shared memory.  In a normal launch
+// both are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

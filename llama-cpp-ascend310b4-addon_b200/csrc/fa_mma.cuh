@@ -1,7 +1,7 @@
 // fa_mma.cuh -- single-token GQA flash-decoding on tensor cores (head_dim 64
 // and 128).
 //
-// Grid (split, kv head, q-head chunk), 128 threads.  The query heads of one
+// Grid (split, kv head, q-head chunk), two groups of 4 warps.  The query heads of one
 // GQA group (up to 8) form the M dimension of mma.sync m16n8k16 (rows 8..15
 // are zero), so each K/V tile is read from HBM once for the whole group:
 //   S = Q K^T : A = f16(q) (held in registers for the whole split), B = K
@@ -9,13 +9,16 @@
 //   P V       : A = P (the S accumulator layout re-used as the A operand),
 //               B = V tile via ldmatrix.trans.  P is split into an f16 high
 //               part and an f16 residual so the product keeps ~22 bits.
-// K/V chunks of 64 positions stream through a 3-stage cp.async ring (rows
-// past the context are zero-filled).  Each warp owns 16 positions of every
-// chunk and keeps its own online-softmax state (max, sum, output); the four
-// warps are combined in shared memory.  The splits of one (kv head, head
-// chunk) form one thread-block cluster: after a cluster barrier every CTA
-// merges a slice of the outputs by reading its peers' partial results through
-// distributed shared memory, so partials never leave the SMs.
+// K/V chunks of 64 positions stream through 3-stage cp.async rings (rows
+// past the context are zero-filled).  The two warp groups walk alternate
+// chunks of the split, each with its own ring and named barrier, so two
+// independent load/mma/softmax chains run per SM.  Each warp owns 16
+// positions of its group's chunks and keeps its own online-softmax state
+// (max, sum, output); the eight warps are combined in shared memory.  The
+// splits of one (kv head, head chunk) form one thread-block cluster: after a
+// cluster barrier every CTA merges a slice of the outputs by reading its
+// peers' partial results through distributed shared memory, so partials never
+// leave the SMs.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -28,6 +31,11 @@ namespace b200 {
 namespace cgx = cooperative_groups;
 
 constexpr int kFmStages = 3;
+constexpr int kFmGroups = 2;  // warp groups walking alternate chunks
+constexpr int kFmThreads = 128 * kFmGroups;
+
+// Barrier of one 128-thread warp group (ids 1.. ; 0 is __syncthreads).
+__device__ __forceinline__ void group_sync(int grp) { asm volatile("bar.sync %0, 128;" ::"r"(grp + 1) : "memory"); }
 
 __device__ __forceinline__ void mma_16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -66,32 +74,37 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Shared memory of fa_mma_kernel<D>: kFmStages x (K tile + V tile) of
-// kFaChunk rows x D halves; reused after the loop for the warp combine and
-// the cluster merge (which need 5 x kFaMaxG x D floats plus 40 x kFaMaxG).
+// Shared memory of fa_mma_kernel<D>: per warp group kFmStages x (K tile + V
+// tile) of kFaChunk rows x D halves; reused after the loop for the warp
+// combine and the cluster merge (which need (4 kFmGroups + 1) x kFaMaxG x D
+// floats plus 48 x kFaMaxG).
 constexpr int kFmMaxCluster = 16;
 B200_HD inline size_t fa_mma_smem_bytes(int D) {
-    const size_t ring = (size_t)kFmStages * 2 * kFaChunk * D * 2;
-    const size_t merge = ((size_t)5 * kFaMaxG * D + 48 * kFaMaxG) * sizeof(float);
+    const size_t ring = (size_t)kFmGroups * kFmStages * 2 * kFaChunk * D * 2;
+    const size_t merge = ((size_t)(4 * kFmGroups + 1) * kFaMaxG * D + 48 * kFaMaxG) * sizeof(float);
     return ring > merge ? ring : merge;
 }
 
 template <int D>
-__global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
+__global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const FaArgs a) {
     constexpr int KT = D / 16;       // k tiles of the QK^T product
     constexpr int NT = D / 8;        // n tiles of the PV product
     constexpr int GR = D / 8;        // 16-byte granules per K/V row
     constexpr int ROWB = 2 * D;      // bytes per K/V row in shared memory
     constexpr int TILE = kFaChunk * ROWB;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float wm[4][kFaMaxG], wl[4][kFaMaxG];
+    constexpr int NW = 4 * kFmGroups;  // warps per CTA
+    __shared__ float wm[NW][kFaMaxG], wl[NW][kFaMaxG];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int grp = warp >> 2, gw = warp & 3, gtid = tid & 127;  // warp group, warp and thread in it
     const int g = lane >> 2, t = lane & 3;
     const int split = blockIdx.x, hk = blockIdx.y, gc = blockIdx.z;
     const int h0 = hk * a.G + gc * kFaMaxG;
     const int hn = min(kFaMaxG, a.G - gc * kFaMaxG);
 
+    griddep_wait();  // q, the new K/V row and kv_len come from earlier kernels
+    griddep_launch_dependents();
     int ctx = a.n_kv;
     if (a.kv_len != nullptr) {
         const int kl = a.kv_len[0];
@@ -108,8 +121,39 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
 #pragma unroll
     for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
-    if (active) {
-        // Q fragments (A operand, rows = heads; rows 8..15 are zero)
+    // this group's chunks: c_begin + grp + kFmGroups * i, i < ncg
+    const int ncg = active ? (c_end - c_begin - grp + kFmGroups - 1) / kFmGroups : 0;
+    if (ncg > 0) {
+        const uint32_t gbase = sbase + (uint32_t)(grp * kFmStages * 2 * TILE);
+        // Each thread always copies granule cg = gtid % GR of rows
+        // gtid / GR + (128 / GR) i, so its source offsets and the swizzled
+        // destination column are fixed for the whole split.
+        constexpr int RPI = 128 / GR;  // rows covered per pass
+        const int cg = gtid % GR, r0 = gtid / GR;
+        const uint32_t swz = (uint32_t)((cg ^ (r0 & 7)) << 4);  // (r0 + RPI i) & 7 == r0 & 7
+        const uint8_t* kb = a.k + (int64_t)hk * a.k_nb2 + cg * 16;
+        const uint8_t* vb = a.v + (int64_t)hk * a.v_nb2 + cg * 16;
+        auto load_chunk = [&](int c, int stage) {
+            const uint32_t kst = gbase + (uint32_t)(stage * 2 * TILE) + (uint32_t)(r0 * ROWB) + swz;
+            const uint32_t vst = kst + TILE;
+            const int p0 = c * kFaChunk + r0;
+            const uint8_t* kp = kb + (int64_t)p0 * a.k_nb1;
+            const uint8_t* vp = vb + (int64_t)p0 * a.v_nb1;
+#pragma unroll
+            for (int i = 0; i < kFaChunk / RPI; ++i) {
+                const bool ok = p0 + RPI * i < ctx;
+                cp_async16(kst + (uint32_t)(RPI * i * ROWB), ok ? kp + (int64_t)RPI * i * a.k_nb1 : a.k, ok ? 16 : 0);
+                cp_async16(vst + (uint32_t)(RPI * i * ROWB), ok ? vp + (int64_t)RPI * i * a.v_nb1 : a.v, ok ? 16 : 0);
+            }
+        };
+        const int cfirst = c_begin + grp;
+        load_chunk(cfirst, 0);
+        cp_async_commit();
+        if (ncg > 1) load_chunk(cfirst + kFmGroups, 1);
+        cp_async_commit();
+
+        // Q fragments (A operand, rows = heads; rows 8..15 are zero), loaded
+        // while the first K/V copies are in flight
         uint32_t qa[KT][2];
         {
             const bool hv = g < hn;
@@ -122,44 +166,18 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
                 qa[kt][1] = hv ? pack_half2(x1.x, x1.y) : 0u;
             }
         }
-        // Each thread always copies granule cg = tid % GR of rows
-        // tid / GR + (128 / GR) i, so its source offsets and the swizzled
-        // destination column are fixed for the whole split.
-        constexpr int RPI = 128 / GR;  // rows covered per pass
-        const int cg = tid % GR, r0 = tid / GR;
-        const uint32_t swz = (uint32_t)((cg ^ (r0 & 7)) << 4);  // (r0 + RPI i) & 7 == r0 & 7
-        const uint8_t* kb = a.k + (int64_t)hk * a.k_nb2 + cg * 16;
-        const uint8_t* vb = a.v + (int64_t)hk * a.v_nb2 + cg * 16;
-        auto load_chunk = [&](int c, int stage) {
-            const uint32_t kst = sbase + (uint32_t)(stage * 2 * TILE) + (uint32_t)(r0 * ROWB) + swz;
-            const uint32_t vst = kst + TILE;
-            const int p0 = c * kFaChunk + r0;
-            const uint8_t* kp = kb + (int64_t)p0 * a.k_nb1;
-            const uint8_t* vp = vb + (int64_t)p0 * a.v_nb1;
-#pragma unroll
-            for (int i = 0; i < kFaChunk / RPI; ++i) {
-                const bool ok = p0 + RPI * i < ctx;
-                cp_async16(kst + (uint32_t)(RPI * i * ROWB), ok ? kp + (int64_t)RPI * i * a.k_nb1 : a.k, ok ? 16 : 0);
-                cp_async16(vst + (uint32_t)(RPI * i * ROWB), ok ? vp + (int64_t)RPI * i * a.v_nb1 : a.v, ok ? 16 : 0);
-            }
-        };
-        const int nc = c_end - c_begin;
-        load_chunk(c_begin, 0);
-        cp_async_commit();
-        if (nc > 1) load_chunk(c_begin + 1, 1);
-        cp_async_commit();
 
-        for (int ci = 0; ci < nc; ++ci) {
-            const int c = c_begin + ci;
+        for (int ci = 0; ci < ncg; ++ci) {
+            const int c = cfirst + kFmGroups * ci;
             const int stage = ci % kFmStages;
-            if (ci + 2 < nc) load_chunk(c + 2, (ci + 2) % kFmStages);
+            if (ci + 2 < ncg) load_chunk(c + 2 * kFmGroups, (ci + 2) % kFmStages);
             cp_async_commit();
             cp_async_wait<2>();
-            __syncthreads();  // chunk c is in shared memory for every warp
+            group_sync(grp);  // chunk c is in shared memory for every warp of the group
 
-            const uint32_t kst = sbase + (uint32_t)(stage * 2 * TILE);
+            const uint32_t kst = gbase + (uint32_t)(stage * 2 * TILE);
             const uint32_t vst = kst + TILE;
-            const int pw = 16 * warp;  // this warp's 16 positions in the chunk
+            const int pw = 16 * gw;  // this warp's 16 positions in the chunk
             // ---- S = Q K^T over 2 n-tiles of 8 positions ----
             float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
             {
@@ -234,14 +252,14 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
                     mma_16816(o[2 * jj + 1], pa_lo, b[2], b[3]);
                 }
             }
-            __syncthreads();  // stage may be refilled by the next iteration
+            group_sync(grp);  // stage may be refilled by the next iteration
         }
         cp_async_wait<0>();
     }
 
-    // ---- combine the 4 warps into this CTA's partial (shared memory re-used) ----
-    float* wo = reinterpret_cast<float*>(smem);             // [4][kFaMaxG][D]
-    float* co = wo + 4 * kFaMaxG * D;                         // [kFaMaxG][D]  this CTA's partial
+    // ---- combine the NW warps into this CTA's partial (shared memory re-used) ----
+    float* wo = reinterpret_cast<float*>(smem);             // [NW][kFaMaxG][D]
+    float* co = wo + NW * kFaMaxG * D;                        // [kFaMaxG][D]  this CTA's partial
     float* wr = co + kFaMaxG * D;                             // [kFaMaxG][16] merge weights
     float* allm = wr + kFaMaxG * 16;                          // [16][kFaMaxG]
     float* alll = allm + 16 * kFaMaxG;                        // [16][kFaMaxG]
@@ -257,16 +275,16 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
         wo[((warp * kFaMaxG) + g) * D + 8 * n + 2 * t + 1] = o[n][1];
     }
     __syncthreads();
-    for (int idx = tid; idx < kFaMaxG * D; idx += 128) {
+    for (int idx = tid; idx < kFaMaxG * D; idx += kFmThreads) {
         const int h = idx / D, d = idx - (idx / D) * D;
         float M = -INFINITY;
         if (active && h < hn)
 #pragma unroll
-            for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][h]);
+            for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][h]);
         float ov = 0.f, lv = 0.f;
         if (M != -INFINITY) {
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
+            for (int w = 0; w < NW; ++w) {
                 const float e = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
                 ov = fmaf(wo[((w * kFaMaxG) + h) * D + d], e, ov);
                 lv = fmaf(wl[w][h], e, lv);
@@ -307,7 +325,7 @@ __global__ void __launch_bounds__(128) fa_mma_kernel(const FaArgs a) {
     __syncthreads();
     const int tot = hn * D;
     const int o0 = rank * tot / S, o1 = (rank + 1) * tot / S;
-    for (int idx = o0 + tid; idx < o1; idx += 128) {
+    for (int idx = o0 + tid; idx < o1; idx += kFmThreads) {
         const int h = idx / D, d = idx - (idx / D) * D;
         float acc = 0.f;
         for (int r = 0; r < S; ++r) {

@@ -450,6 +450,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         mbar_fence_init();
         for (int s = 0; s < S && s < nq; ++s) issue(s);
     }
+    // The weight stream above reads only constant data, so under a
+    // programmatic launch it overlaps the previous kernel's tail; the
+    // activation, residual and outputs are touched only after this wait.
+    griddep_wait();
+    griddep_launch_dependents();
 
     // ---- prologue: the activation, once per CTA, into shared memory ----
     float nscale = 1.f;

@@ -7,8 +7,11 @@
 
 // GEMV with prologue/epilogue fusion; a.n, a.k, a.w and the fusion fields
 // must be set, the tiling fields are filled in from the packed-layout plan.
-int b200i_gemv(int fmt, b200::GemvArgs a, bool debug, cudaStream_t st);
-int b200i_fa(const b200::FaArgs& a, int head_dim, cudaStream_t st);
+// pdl: launch with programmatic stream serialisation, so the kernel's
+// prologue (weight prefetch) overlaps the tail of the previous kernel in the
+// stream; the kernels wait for that kernel before touching its outputs.
+int b200i_gemv(int fmt, b200::GemvArgs a, bool debug, cudaStream_t st, bool pdl = false);
+int b200i_fa(const b200::FaArgs& a, int head_dim, cudaStream_t st, bool pdl = false);
 int b200i_sm_count();
 // Sets per-kernel attributes and caches device properties; call before capture.
 int b200i_prepare_device();

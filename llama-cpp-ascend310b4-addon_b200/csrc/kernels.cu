@@ -106,8 +106,16 @@ size_t gemv_smem_bytes(int fmt, const GemvPlan& p, int stages, int64_t rows_per_
            (p.rpc > 1 ? 0 : (size_t)(2 * rows_per_cta) * sizeof(float));
 }
 
+// Launch attribute for programmatic dependent launch (see b200i_gemv).
+cudaLaunchAttribute pdl_attr() {
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    return at;
+}
+
 template <int FMT, bool DEBUG, int UPL>
-int launch_gemv_u(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
+int launch_gemv_u(GemvArgs a, const GemvPlan& p, cudaStream_t st, bool pdl) {
     const int dev = current_device();
     CR_((set_gemv_attr<FMT, DEBUG, UPL>(dev)));
     const bool pair = a.epi == EPI_SWIGLU || a.epi == EPI_QKV;
@@ -128,24 +136,35 @@ int launch_gemv_u(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
     a.n = p.n;
     a.k = p.k;
     a.stages = S;
+    if (pdl) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid, 1, 1);
+        cfg.blockDim = dim3(kGemvThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute at = pdl_attr();
+        cfg.attrs = &at;
+        cfg.numAttrs = 1;
+        return cuda_status(cudaLaunchKernelEx(&cfg, gemv_kernel<FMT, DEBUG, UPL>, a));
+    }
     gemv_kernel<FMT, DEBUG, UPL><<<grid, kGemvThreads, smem, st>>>(a);
     return cuda_status(cudaGetLastError());
 }
 
 template <int FMT, bool DEBUG>
-int launch_gemv_t(GemvArgs a, const GemvPlan& p, cudaStream_t st) {
+int launch_gemv_t(GemvArgs a, const GemvPlan& p, cudaStream_t st, bool pdl) {
     switch (p.full_upl) {
-        case 2: return launch_gemv_u<FMT, DEBUG, 2>(a, p, st);
-        case 4: return launch_gemv_u<FMT, DEBUG, 4>(a, p, st);
+        case 2: return launch_gemv_u<FMT, DEBUG, 2>(a, p, st, pdl);
+        case 4: return launch_gemv_u<FMT, DEBUG, 4>(a, p, st, pdl);
         case 6:
-            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 6>(a, p, st);
+            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 6>(a, p, st, pdl);
             break;
         case 8:
-            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 8>(a, p, st);
+            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 8>(a, p, st, pdl);
             break;
         default: break;
     }
-    return launch_gemv_u<FMT, DEBUG, 0>(a, p, st);
+    return launch_gemv_u<FMT, DEBUG, 0>(a, p, st, pdl);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -225,20 +244,20 @@ int gemv_common(int fmt, const void* w, const float* x, float* y, int64_t n, int
 
 // ------------------------------------------------------------------ internal
 
-int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st) {
+int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st, bool pdl) {
     const int type = fmt == FMT_F16 ? B200_TYPE_F16 : (fmt == FMT_Q8 ? B200_TYPE_Q8_0 : B200_TYPE_Q4_0);
     GemvPlan p;
     if (!make_plan(type, a.n, a.k, &p)) return B200_EUNSUPPORTED;
     if (debug) {
-        if (fmt == FMT_Q4) return launch_gemv_t<FMT_Q4, true>(a, p, st);
-        if (fmt == FMT_Q8) return launch_gemv_t<FMT_Q8, true>(a, p, st);
+        if (fmt == FMT_Q4) return launch_gemv_t<FMT_Q4, true>(a, p, st, pdl);
+        if (fmt == FMT_Q8) return launch_gemv_t<FMT_Q8, true>(a, p, st, pdl);
         return B200_EINVAL;
     }
     switch (fmt) {
-        case FMT_F16: return launch_gemv_t<FMT_F16, false>(a, p, st);
-        case FMT_Q4: return launch_gemv_t<FMT_Q4, false>(a, p, st);
-        case FMT_Q4W: return launch_gemv_t<FMT_Q4W, false>(a, p, st);
-        case FMT_Q8: return launch_gemv_t<FMT_Q8, false>(a, p, st);
+        case FMT_F16: return launch_gemv_t<FMT_F16, false>(a, p, st, pdl);
+        case FMT_Q4: return launch_gemv_t<FMT_Q4, false>(a, p, st, pdl);
+        case FMT_Q4W: return launch_gemv_t<FMT_Q4W, false>(a, p, st, pdl);
+        case FMT_Q8: return launch_gemv_t<FMT_Q8, false>(a, p, st, pdl);
         default: return B200_EINVAL;
     }
 }
@@ -263,7 +282,7 @@ int fa_cluster_probe(int dev) {
         if (cs > 8 && !nonportable) continue;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(cs, 1, 1);
-        cfg.blockDim = dim3(128, 1, 1);
+        cfg.blockDim = dim3(kFmThreads, 1, 1);
         cfg.dynamicSmemBytes = fa_mma_smem_bytes(D);
         cudaLaunchAttribute at;
         at.id = cudaLaunchAttributeClusterDimension;
@@ -312,7 +331,7 @@ int set_fa_attrs() {
 }
 
 template <int D>
-int launch_fa_mma(FaArgs a, cudaStream_t st) {
+int launch_fa_mma(FaArgs a, cudaStream_t st, bool pdl) {
     const int dev = current_device();
     CR_(set_fa_attrs());
     const int nchunks = (a.n_kv + kFaChunk - 1) / kFaChunk;
@@ -321,26 +340,27 @@ int launch_fa_mma(FaArgs a, cudaStream_t st) {
     a.chunks_per_split = (nchunks + S - 1) / S;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S, a.Hkv, a.gchunks);
-    cfg.blockDim = dim3(128, 1, 1);
+    cfg.blockDim = dim3(kFmThreads, 1, 1);
     cfg.dynamicSmemBytes = fa_mma_smem_bytes(D);
     cfg.stream = st;
-    cudaLaunchAttribute at;
-    at.id = cudaLaunchAttributeClusterDimension;
-    at.val.clusterDim.x = S;
-    at.val.clusterDim.y = 1;
-    at.val.clusterDim.z = 1;
-    cfg.attrs = &at;
-    cfg.numAttrs = 1;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = S;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1] = pdl_attr();
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 2 : 1;
     return cuda_status(cudaLaunchKernelEx(&cfg, fa_mma_kernel<D>, a));
 }
 
 // head_dim 64 / 128: tensor-core cluster kernel (fa_mma.cuh); 256: CUDA-core
 // kernel with global partials (fa.cuh).
-int b200i_fa(const FaArgs& in, int D, cudaStream_t st) {
+int b200i_fa(const FaArgs& in, int D, cudaStream_t st, bool pdl) {
     FaArgs a = in;
     switch (D) {
-        case 64: return launch_fa_mma<64>(a, st);
-        case 128: return launch_fa_mma<128>(a, st);
+        case 64: return launch_fa_mma<64>(a, st, pdl);
+        case 128: return launch_fa_mma<128>(a, st, pdl);
         case 256: {
             dim3 grid(a.n_splits, a.Hkv, a.gchunks);
             fa_decode_kernel<256><<<grid, kFaThreads, 0, st>>>(a);

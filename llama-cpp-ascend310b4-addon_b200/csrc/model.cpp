@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -114,6 +115,10 @@ struct b200_model {
     uint64_t seed = 0;
     float sigma = 0.f;
     FaLayout fa{};
+    // Programmatic dependent launch between the step's kernels (on unless
+    // B200_PDL=0): each GEMV starts streaming its weights while the previous
+    // kernel drains.
+    bool pdl = true;
 };
 
 namespace {
@@ -180,6 +185,8 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
     const float theta_scale = powf(c.rope_theta, -2.0f / (float)D);
     auto B = [&](int cls) { return prof ? prof->begin(s, cls) : B200_OK; };
     auto E = [&]() { return prof ? prof->end(s) : B200_OK; };
+    // events and dump copies between the kernels would serialise them anyway
+    const bool pdl = m->pdl && !prof && !dump;
 
     CR(B(0));
     CR(b200i_embed(m->tok_embd, c.d_model, c.vocab, m->st, m->x, s));
@@ -207,7 +214,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         a.kc = Ly.kc;
         a.vc = Ly.vc;
         CR(B(1));
-        CR(b200i_gemv(FMT_Q4, a, false, s));
+        CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
         CR(E());
 
         FaArgs f;
@@ -234,7 +241,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         f.tickets = reinterpret_cast<unsigned int*>(ws + m->fa.off_tickets);
         if (dump) CK(cudaMemcpyAsync(dump->q + (size_t)l * m->hq * D, m->q, qbytes, cudaMemcpyDeviceToDevice, s));
         CR(B(2));
-        CR(b200i_fa(f, D, s));
+        CR(b200i_fa(f, D, s, pdl));
         CR(E());
         if (dump)
             CK(cudaMemcpyAsync(dump->att + (size_t)l * m->hq * D, m->att, qbytes, cudaMemcpyDeviceToDevice, s));
@@ -254,7 +261,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
             a.y = m->part;
         }
         CR(B(3));
-        CR(b200i_gemv(FMT_Q4, a, false, s));
+        CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
         CR(E());
         if (m->world > 1) {
             CR(B(7));
@@ -273,7 +280,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         a.epi = EPI_SWIGLU;
         a.y = m->h;
         CR(B(4));
-        CR(b200i_gemv(FMT_Q4, a, false, s));
+        CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
         CR(E());
 
         std::memset(&a, 0, sizeof(a));
@@ -291,7 +298,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
             a.y = m->part;
         }
         CR(B(5));
-        CR(b200i_gemv(FMT_Q4, a, false, s));
+        CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
         CR(E());
         if (m->world > 1) {
             CR(B(7));
@@ -316,7 +323,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
     a.amax = &m->st->amax;
     a.row_offset = (int64_t)m->rank * m->voc;
     CR(B(6));
-    CR(b200i_gemv(FMT_Q4, a, false, s));
+    CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
     CR(E());
     if (m->world > 1) {
         CR(B(7));
@@ -361,6 +368,7 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
     b200_model* m = new b200_model();
     m->c = *cfg;
     m->device = device;
+    if (const char* e = getenv("B200_PDL")) m->pdl = atoi(e) != 0;
     m->rank = tp_rank;
     m->world = tp_world;
     const b200_llama_config& c = m->c;
