@@ -1,6 +1,6 @@
 // common.cuh -- shared device helpers for the sm_100a decode kernels.
 //
-// Bulk-async copies (cp.async.bulk, no multicast) into shared memory signalled
+// Bulk-async copies (cp.async.bulk, one CTA each) into shared memory signalled
 // through mbarriers, bounded waits that report a status word instead of
 // hanging, f16 helpers and warp reductions.
 #pragma once

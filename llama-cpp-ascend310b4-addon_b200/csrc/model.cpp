@@ -142,30 +142,40 @@ int dalloc_t(b200_model* m, T** p, size_t bytes) {
     return B200_OK;
 }
 
-// Regenerates one weight shard of this rank in ggml layout at `dst`;
-// returns its row count and column count through rows/cols.
-int gen_weight(b200_model* m, int layer, int which, uint8_t* dst, int64_t* rows, int64_t* cols) {
+// Shard geometry of one weight on this rank: rows [r0, r0+nr) and columns
+// [c0, c0+nc) of the unsharded [rows][kg] tensor.
+int weight_shard(const b200_model* m, int which, int64_t* r0, int64_t* nr, int64_t* c0, int64_t* nc, int64_t* kg) {
     const b200_llama_config& c = m->c;
     const int D = c.head_dim;
-    const uint64_t s = tensor_seed(m->seed, layer, which);
-    int64_t r0 = 0, nr = 0, c0 = 0, nc = 0, kg = 0;
+    *r0 = 0;
+    *c0 = 0;
     switch (which) {
-        case B200_W_TOK_EMBD: r0 = 0; nr = c.vocab; c0 = 0; nc = c.d_model; kg = c.d_model; break;
-        case B200_W_Q: r0 = (int64_t)m->rank * m->hq * D; nr = (int64_t)m->hq * D; nc = kg = c.d_model; break;
+        case B200_W_TOK_EMBD: *nr = c.vocab; *nc = *kg = c.d_model; break;
+        case B200_W_Q: *r0 = (int64_t)m->rank * m->hq * D; *nr = (int64_t)m->hq * D; *nc = *kg = c.d_model; break;
         case B200_W_K:
-        case B200_W_V: r0 = (int64_t)m->rank * m->hkv * D; nr = (int64_t)m->hkv * D; nc = kg = c.d_model; break;
+        case B200_W_V: *r0 = (int64_t)m->rank * m->hkv * D; *nr = (int64_t)m->hkv * D; *nc = *kg = c.d_model; break;
         case B200_W_O:
-            nr = c.d_model; c0 = (int64_t)m->rank * m->hq * D; nc = (int64_t)m->hq * D; kg = (int64_t)c.n_head * D;
+            *nr = c.d_model; *c0 = (int64_t)m->rank * m->hq * D; *nc = (int64_t)m->hq * D; *kg = (int64_t)c.n_head * D;
             break;
         case B200_W_GATE:
-        case B200_W_UP: r0 = (int64_t)m->rank * m->ff; nr = m->ff; nc = kg = c.d_model; break;
-        case B200_W_DOWN: nr = c.d_model; c0 = (int64_t)m->rank * m->ff; nc = m->ff; kg = c.d_ff; break;
-        case B200_W_LM_HEAD: r0 = (int64_t)m->rank * m->voc; nr = m->voc; nc = kg = c.d_model; break;
+        case B200_W_UP: *r0 = (int64_t)m->rank * m->ff; *nr = m->ff; *nc = *kg = c.d_model; break;
+        case B200_W_DOWN: *nr = c.d_model; *c0 = (int64_t)m->rank * m->ff; *nc = m->ff; *kg = c.d_ff; break;
+        case B200_W_LM_HEAD: *r0 = (int64_t)m->rank * m->voc; *nr = m->voc; *nc = *kg = c.d_model; break;
         default: return B200_EINVAL;
     }
+    return B200_OK;
+}
+
+// Regenerates one weight shard of this rank in ggml layout at `dst`, which
+// holds `cap` bytes; returns its row count and column count through
+// rows/cols.  Refuses (EINVAL, nothing launched) when the shard does not fit.
+int gen_weight(b200_model* m, int layer, int which, uint8_t* dst, size_t cap, int64_t* rows, int64_t* cols) {
+    int64_t r0, nr, c0, nc, kg;
+    CR(weight_shard(m, which, &r0, &nr, &c0, &nc, &kg));
+    if ((size_t)q4_bytes(nr, nc) > cap) return B200_EINVAL;
     *rows = nr;
     *cols = nc;
-    return b200i_synth_q4_0(s, m->sigma, r0, nr, c0, nc, kg, dst, m->stream);
+    return b200i_synth_q4_0(tensor_seed(m->seed, layer, which), m->sigma, r0, nr, c0, nc, kg, dst, m->stream);
 }
 
 int allreduce_sum(b200_model* m, const float* src, float* dst, size_t n, cudaStream_t s) {
@@ -450,25 +460,26 @@ int b200_model_init_synthetic(b200_model* m, uint64_t seed, float sigma) {
     const b200_llama_config& c = m->c;
     const cudaStream_t s = m->stream;
     int64_t r, k;
-    CR(gen_weight(m, -1, B200_W_TOK_EMBD, m->tok_embd, &r, &k));
-    CR(gen_weight(m, -1, B200_W_LM_HEAD, m->staging, &r, &k));
+    CR(gen_weight(m, -1, B200_W_TOK_EMBD, m->tok_embd, (size_t)q4_bytes(c.vocab, c.d_model), &r, &k));
+    CR(gen_weight(m, -1, B200_W_LM_HEAD, m->staging, m->staging_bytes, &r, &k));
     CR(b200_repack(B200_TYPE_Q4_0, m->staging, m->lm_head, r, k, (b200_stream_t)s));
     CR(b200i_fill_f32(m->out_norm, c.d_model, 1.0f, s));
     for (int l = 0; l < c.n_layer; ++l) {
         Layer& Ly = m->L[l];
         int64_t rq, rk, rv;
-        CR(gen_weight(m, l, B200_W_Q, m->staging, &rq, &k));
-        CR(gen_weight(m, l, B200_W_K, m->staging + q4_bytes(rq, k), &rk, &k));
-        CR(gen_weight(m, l, B200_W_V, m->staging + q4_bytes(rq + rk, k), &rv, &k));
+        CR(gen_weight(m, l, B200_W_Q, m->staging, m->staging_bytes, &rq, &k));
+        CR(gen_weight(m, l, B200_W_K, m->staging + q4_bytes(rq, k), m->staging_bytes - q4_bytes(rq, k), &rk, &k));
+        CR(gen_weight(m, l, B200_W_V, m->staging + q4_bytes(rq + rk, k), m->staging_bytes - q4_bytes(rq + rk, k),
+                       &rv, &k));
         CR(b200_repack(B200_TYPE_Q4_0, m->staging, Ly.wqkv, rq + rk + rv, k, (b200_stream_t)s));
-        CR(gen_weight(m, l, B200_W_O, m->staging, &r, &k));
+        CR(gen_weight(m, l, B200_W_O, m->staging, m->staging_bytes, &r, &k));
         CR(b200_repack(B200_TYPE_Q4_0, m->staging, Ly.wo, r, k, (b200_stream_t)s));
         int64_t rg, ru;
-        CR(gen_weight(m, l, B200_W_GATE, m->staging, &rg, &k));
-        CR(gen_weight(m, l, B200_W_UP, m->staging + q4_bytes(rg, k), &ru, &k));
+        CR(gen_weight(m, l, B200_W_GATE, m->staging, m->staging_bytes, &rg, &k));
+        CR(gen_weight(m, l, B200_W_UP, m->staging + q4_bytes(rg, k), m->staging_bytes - q4_bytes(rg, k), &ru, &k));
         CR(b200_repack_interleave2(B200_TYPE_Q4_0, m->staging, m->staging + q4_bytes(rg, k), Ly.wgu, rg, k,
                                    (b200_stream_t)s));
-        CR(gen_weight(m, l, B200_W_DOWN, m->staging, &r, &k));
+        CR(gen_weight(m, l, B200_W_DOWN, m->staging, m->staging_bytes, &r, &k));
         CR(b200_repack(B200_TYPE_Q4_0, m->staging, Ly.wdown, r, k, (b200_stream_t)s));
         CR(b200i_fill_f32(Ly.attn_norm, c.d_model, 1.0f, s));
         CR(b200i_fill_f32(Ly.ffn_norm, c.d_model, 1.0f, s));
@@ -499,16 +510,21 @@ int b200_model_export_weight(b200_model* m, int layer, int which, void* host, si
     if (which != B200_W_TOK_EMBD && which != B200_W_LM_HEAD && (layer < 0 || layer >= m->c.n_layer))
         return B200_EINVAL;
     CK(cudaSetDevice(m->device));
-    int64_t r, k;
-    CR(gen_weight(m, (which == B200_W_TOK_EMBD || which == B200_W_LM_HEAD) ? -1 : layer, which, m->staging, &r, &k));
-    const size_t need = (size_t)q4_bytes(r, k);
+    int64_t r0, nr, c0, nc, kg;
+    CR(weight_shard(m, which, &r0, &nr, &c0, &nc, &kg));
+    const size_t need = (size_t)q4_bytes(nr, nc);
     if (!host) {
         *bytes = need;
-        CK(cudaStreamSynchronize(m->stream));
         return B200_OK;
     }
     if (*bytes < need) return B200_EINVAL;
-    CK(cudaMemcpyAsync(host, m->staging, need, cudaMemcpyDeviceToHost, m->stream));
+    const uint8_t* src = m->tok_embd;  // the embedding table is resident in ggml layout on every rank
+    if (which != B200_W_TOK_EMBD) {
+        int64_t r, k;
+        CR(gen_weight(m, which == B200_W_LM_HEAD ? -1 : layer, which, m->staging, m->staging_bytes, &r, &k));
+        src = m->staging;
+    }
+    CK(cudaMemcpyAsync(host, src, need, cudaMemcpyDeviceToHost, m->stream));
     CK(cudaStreamSynchronize(m->stream));
     *bytes = need;
     return B200_OK;
