@@ -1,0 +1,87 @@
+// allreduce.cuh -- tensor-parallel all-reduce of one activation vector over
+// NVLink peer memory, for the partial sums of the row-split O and down
+// projections (the reference decomposes nothing; this replaces an
+// ncclAllReduce(sum) of d_model floats per call).
+//
+// Every rank's producing GEMV has written its partial into its own buffer
+// (mapped into every peer through CUDA IPC).  This kernel, on every rank:
+//   1. announces "partial of collective seq is complete" by storing seq into
+//      each rank's flag slot for this rank (release, system scope);
+//   2. waits until every rank's announcement for seq has arrived in its own
+//      flags (acquire, system scope; bounded: 2 s, then a status bit);
+//   3. sums the partials of ranks 0..world-1 in that order, reading the peers'
+//      buffers directly over NVLink, and writes the full vector locally.
+// The order is fixed, so every rank gets bit-identical results.  seq grows
+// with the device step counter, so a captured graph replays correctly.
+// Buffer reuse is safe with two partial buffers used alternately: a rank
+// overwrites a buffer two collectives later, after every peer has announced
+// the collective in between, which each does only after finishing this one.
+#pragma once
+
+#include "args.h"
+#include "common.cuh"
+
+namespace b200 {
+
+constexpr int kArThreads = 256;
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Relaxed system-scope 16-byte load (a peer's buffer: no stale L1 copy).
+__device__ __forceinline__ float4 ld_sys_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// Spins until *flag >= want (flags only grow).  Gives up after
+// kWaitTimeoutNs, records B200_DEVSTATUS_TIMEOUT and returns false.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned long long* flag, unsigned long long want) {
+    if (ld_acquire_sys_u64(flag) >= want) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (ld_acquire_sys_u64(flag) >= want) return true;
+        if ((it & 63u) == 0 && globaltimer() - t0 > kWaitTimeoutNs) {
+            record_status(B200_DEVSTATUS_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const ArArgs a) {
+    griddep_wait();  // this rank's partial is complete
+    griddep_launch_dependents();
+    const unsigned long long seq = a.st->step * (unsigned long long)a.per_step + (unsigned long long)a.idx + 1ull;
+    if (blockIdx.x == 0 && threadIdx.x < a.world) {
+        __threadfence_system();
+        st_release_sys_u64(a.peer_flag[threadIdx.x], seq);
+    }
+    bool ok = true;
+    for (int r = 0; r < a.world; ++r) ok = ok && wait_flag_geq(&a.flags[r], seq);
+    if (!ok) return;
+    const int n4 = a.n >> 2;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        float4 acc = ld_sys_f4(a.part[0] + 4 * i);
+        for (int r = 1; r < a.world; ++r) {
+            const float4 v = ld_sys_f4(a.part[r] + 4 * i);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        reinterpret_cast<float4*>(a.x)[i] = acc;
+    }
+}
+
+}  // namespace b200

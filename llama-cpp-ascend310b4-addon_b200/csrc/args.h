@@ -215,6 +215,20 @@ struct StepState {
     int next;                 // argmax token of this step
     int pad_;
     unsigned long long amax;  // packed (value, index) argmax of the logits
+    unsigned long long step;  // steps run so far (set by the embedding kernel; numbers the collectives)
+};
+
+// Tensor-parallel all-reduce over peer memory (one-shot): every rank sums
+// all ranks' partial vectors for collective `idx` of the current step.
+constexpr int kMaxRanks = 8;
+struct ArArgs {
+    int world, rank, n;        // ranks, this rank, floats per vector (multiple of 4)
+    int idx, per_step;         // collective index within the step, collectives per step
+    const StepState* st;
+    float* x;                  // result [n] on this rank
+    const float* part[kMaxRanks];                  // rank r's partial [n] (peer mapped)
+    unsigned long long* flags;                      // this rank's flags [kMaxRanks]: flags[r] = last seq rank r announced
+    unsigned long long* peer_flag[kMaxRanks];       // &flags of rank r [this rank]
 };
 
 }  // namespace b200

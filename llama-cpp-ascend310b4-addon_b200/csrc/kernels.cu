@@ -13,6 +13,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "allreduce.cuh"
 #include "common.cuh"
 #include "fa.cuh"
 #include "fa_mma.cuh"
@@ -368,6 +369,19 @@ int b200i_fa(const FaArgs& in, int D, cudaStream_t st, bool pdl) {
         }
         default: return B200_EUNSUPPORTED;
     }
+}
+
+int b200i_tp_allreduce(const ArArgs& a, cudaStream_t st, bool pdl) {
+    if (a.world < 1 || a.world > kMaxRanks || a.n <= 0 || (a.n & 3)) return B200_EINVAL;
+    const int grid = std::max(1, std::min(16, (a.n / 4 + kArThreads - 1) / kArThreads));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kArThreads, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute at = pdl_attr();
+    cfg.attrs = &at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cuda_status(cudaLaunchKernelEx(&cfg, tp_allreduce_kernel, a));
 }
 
 int b200i_sm_count() { return sm_count(current_device()); }

@@ -100,7 +100,7 @@ struct b200_model {
     uint8_t* tok_embd = nullptr;
     float* out_norm = nullptr;
     uint8_t* lm_head = nullptr;
-    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *part = nullptr, *logits = nullptr;
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
     StepState* st = nullptr;
     StepState* h_st = nullptr;
     int* h_next = nullptr;
@@ -119,6 +119,13 @@ struct b200_model {
     // B200_PDL=0): each GEMV starts streaming its weights while the previous
     // kernel drains.
     bool pdl = true;
+    // Tensor parallel: the O / down partials go to an IPC-shared region
+    // (two partial buffers, then the per-rank flags) summed by the
+    // peer-memory all-reduce; B200_TP_ALLREDUCE=nccl selects ncclAllReduce.
+    bool peer_ar = true;
+    uint8_t* comm_region = nullptr;
+    void* peer_region[kMaxRanks] = {};
+    size_t part_stride = 0, flags_off = 0;
 };
 
 namespace {
@@ -178,9 +185,31 @@ int gen_weight(b200_model* m, int layer, int which, uint8_t* dst, size_t cap, in
     return b200i_synth_q4_0(tensor_seed(m->seed, layer, which), m->sigma, r0, nr, c0, nc, kg, dst, m->stream);
 }
 
-int allreduce_sum(b200_model* m, const float* src, float* dst, size_t n, cudaStream_t s) {
-    NK(ncclAllReduce(src, dst, n, ncclFloat32, ncclSum, m->comm, s));
-    return B200_OK;
+float* part_buf(b200_model* m, int which) { return reinterpret_cast<float*>(m->comm_region + which * m->part_stride); }
+
+// x = sum over ranks of partial buffer `which` (0: O projection, 1: down),
+// collective `idx` of the step.
+int allreduce_sum(b200_model* m, int which, int idx, cudaStream_t s, bool pdl) {
+    if (!m->peer_ar) {
+        NK(ncclAllReduce(part_buf(m, which), m->x, m->c.d_model, ncclFloat32, ncclSum, m->comm, s));
+        return B200_OK;
+    }
+    ArArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.world = m->world;
+    a.rank = m->rank;
+    a.n = m->c.d_model;
+    a.idx = idx;
+    a.per_step = 2 * m->c.n_layer;
+    a.st = m->st;
+    a.x = m->x;
+    for (int r = 0; r < m->world; ++r) {
+        uint8_t* base = static_cast<uint8_t*>(m->peer_region[r]);
+        a.part[r] = reinterpret_cast<const float*>(base + which * m->part_stride);
+        a.peer_flag[r] = reinterpret_cast<unsigned long long*>(base + m->flags_off) + m->rank;
+    }
+    a.flags = reinterpret_cast<unsigned long long*>(m->comm_region + m->flags_off);
+    return b200i_tp_allreduce(a, s, pdl);
 }
 
 struct Dump {
@@ -268,14 +297,14 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
             a.y = m->x;
         } else {
             a.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
-            a.y = m->part;
+            a.y = part_buf(m, 0);
         }
         CR(B(3));
         CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
         CR(E());
         if (m->world > 1) {
             CR(B(7));
-            CR(allreduce_sum(m, m->part, m->x, c.d_model, s));
+            CR(allreduce_sum(m, 0, 2 * l, s, pdl));
             CR(E());
         }
 
@@ -305,14 +334,14 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
             a.y = m->x;
         } else {
             a.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
-            a.y = m->part;
+            a.y = part_buf(m, 1);
         }
         CR(B(5));
         CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
         CR(E());
         if (m->world > 1) {
             CR(B(7));
-            CR(allreduce_sum(m, m->part, m->x, c.d_model, s));
+            CR(allreduce_sum(m, 1, 2 * l + 1, s, pdl));
             CR(E());
         }
         if (dump)
@@ -341,6 +370,42 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         CR(E());
     }
     CR(b200i_finish(m->st, s));
+    return B200_OK;
+}
+
+// Partial buffers (and, for the peer all-reduce, the flags) of tensor
+// parallelism.  With the peer all-reduce the region is shared: every rank
+// maps every peer's region through CUDA IPC, the handles travelling through
+// one ncclAllGather.
+int setup_comm_region(b200_model* m) {
+    if (m->world == 1) return B200_OK;
+    m->part_stride = (size_t)align256((size_t)m->c.d_model * sizeof(float));
+    m->flags_off = 2 * m->part_stride;
+    const size_t bytes = m->flags_off + 256;
+    if (cudaMalloc(reinterpret_cast<void**>(&m->comm_region), bytes) != cudaSuccess) return B200_ENOMEM;
+    CK(cudaMemset(m->comm_region, 0, bytes));
+    if (!m->peer_ar) return B200_OK;
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, m->comm_region));
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    uint8_t* d = nullptr;
+    CK(cudaMalloc(reinterpret_cast<void**>(&d), 64 * (size_t)(m->world + 1)));
+    std::vector<cudaIpcMemHandle_t> all(m->world);
+    int rc = B200_OK;
+    if (cudaMemcpy(d, &mine, 64, cudaMemcpyHostToDevice) != cudaSuccess) rc = B200_ECUDA;
+    if (rc == B200_OK && ncclAllGather(d, d + 64, 64, ncclUint8, m->comm, m->stream) != ncclSuccess) rc = B200_ENCCL;
+    if (rc == B200_OK && cudaStreamSynchronize(m->stream) != cudaSuccess) rc = B200_ECUDA;
+    if (rc == B200_OK && cudaMemcpy(all.data(), d + 64, 64 * (size_t)m->world, cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = B200_ECUDA;
+    cudaFree(d);
+    if (rc) return rc;
+    for (int r = 0; r < m->world; ++r) {
+        if (r == m->rank) {
+            m->peer_region[r] = m->comm_region;
+            continue;
+        }
+        CK(cudaIpcOpenMemHandle(&m->peer_region[r], all[r], cudaIpcMemLazyEnablePeerAccess));
+    }
     return B200_OK;
 }
 
@@ -399,6 +464,9 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
         std::memcpy(&id, nccl_id128, sizeof(id));
         if (ncclCommInitRank(&m->comm, tp_world, id, tp_rank) != ncclSuccess) return fail(B200_ENCCL);
     }
+    if (const char* e = getenv("B200_TP_ALLREDUCE")) m->peer_ar = std::strcmp(e, "nccl") != 0;
+    if (tp_world > kMaxRanks) m->peer_ar = false;
+    if ((rc = setup_comm_region(m))) return fail(rc);
     const size_t p_qkv = b200_packed_size(B200_TYPE_Q4_0, m->qkv_rows, c.d_model);
     const size_t p_o = b200_packed_size(B200_TYPE_Q4_0, c.d_model, (int64_t)m->hq * D);
     const size_t p_gu = b200_packed_size(B200_TYPE_Q4_0, 2 * (int64_t)m->ff, c.d_model);
@@ -423,7 +491,7 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
     if ((rc = dalloc_t(m, &m->tok_embd, q4_bytes(c.vocab, c.d_model))) || (rc = dalloc_t(m, &m->lm_head, p_head)) ||
         (rc = dalloc_t(m, &m->out_norm, c.d_model * 4)) || (rc = dalloc_t(m, &m->x, c.d_model * 4)) ||
         (rc = dalloc_t(m, &m->q, (size_t)m->hq * D * 4)) || (rc = dalloc_t(m, &m->att, (size_t)m->hq * D * 4)) ||
-        (rc = dalloc_t(m, &m->h, (size_t)m->ff * 4)) || (rc = dalloc_t(m, &m->part, c.d_model * 4)) ||
+        (rc = dalloc_t(m, &m->h, (size_t)m->ff * 4)) ||
         (rc = dalloc_t(m, &m->logits, (size_t)m->voc * 4)) || (rc = dalloc_t(m, &m->st, sizeof(StepState))) ||
         (rc = dalloc(m, &m->fa_ws, m->fa_ws_bytes)) || (rc = dalloc_t(m, &m->staging, m->staging_bytes)))
         return fail(rc);
@@ -444,6 +512,14 @@ void b200_model_destroy(b200_model* m) {
     // Graphs that hold NCCL work are released before the communicator.
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
+    if (m->comm && m->comm_region && m->x) {
+        // no peer may still read this rank's region when it is unmapped and freed
+        ncclAllReduce(m->x, m->x, 1, ncclFloat32, ncclSum, m->comm, m->stream);
+        cudaStreamSynchronize(m->stream);
+    }
+    for (int r = 0; r < kMaxRanks; ++r)
+        if (m->peer_region[r] && r != m->rank) cudaIpcCloseMemHandle(m->peer_region[r]);
+    if (m->comm_region) cudaFree(m->comm_region);
     if (m->comm) ncclCommDestroy(m->comm);
     for (void* p : m->allocs) cudaFree(p);
     if (m->h_st) cudaFreeHost(m->h_st);

@@ -100,6 +100,7 @@ __global__ void embed_kernel(const uint8_t* table, int64_t d_model, int64_t voca
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         st->ctx = st->pos + 1;
         st->amax = 0ull;
+        st->step += 1;
     }
 }
 
