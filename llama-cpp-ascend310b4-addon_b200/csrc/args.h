@@ -3,6 +3,7 @@
 // No device code here, so any translation unit may include it.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (a plain 128-byte descriptor type)
 #include <stddef.h>
 #include <stdint.h>
 
@@ -179,6 +180,9 @@ struct FaArgs {
     float* part_o;          // [n_splits][Hq][D]
     float* part_ml;         // [n_splits][Hq][2]
     unsigned int* tickets;  // [Hkv][gchunks]
+    // TMA descriptors of K and V ([head_dim, Hkv, n_kv], 64 x 1 x 64 boxes,
+    // 128-byte swizzle), filled by the launcher of the tensor-core kernel.
+    CUtensorMap tmk, tmv;
 };
 
 struct FaLayout {

@@ -9,8 +9,10 @@
 //   P V       : A = P (the S accumulator layout re-used as the A operand),
 //               B = V tile via ldmatrix.trans.  P is split into an f16 high
 //               part and an f16 residual so the product keeps ~22 bits.
-// K/V chunks of 64 positions stream through 3-stage cp.async rings (rows
-// past the context are zero-filled).  The two warp groups walk alternate
+// K/V chunks of 64 positions arrive by TMA (a 3-D tensor map over
+// [head_dim, kv head, position]; boxes of 64 positions x 64 dims with the
+// 128-byte swizzle) into 3-stage rings counted on mbarriers; V rows past the
+// context are zeroed in shared memory.  The two warp groups walk alternate
 // chunks of the split, each with its own ring and named barrier, so two
 // independent load/mma/softmax chains run per SM.  Each warp owns 16
 // positions of its group's chunks and keeps its own online-softmax state
@@ -57,16 +59,15 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t r[4], uint32_t addr) {
                  : "r"(addr));
 }
 
-// 16-byte async copy; src_bytes == 0 zero-fills the destination.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+// 3-D tiled TMA load of one box into this CTA's shared memory; completion
+// is counted on `bar`.  x (the head_dim coordinate) is a multiple of 64
+// halves, so its byte offset is 16-byte aligned.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
@@ -80,18 +81,19 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 // floats plus 48 x kFaMaxG).
 constexpr int kFmMaxCluster = 16;
 B200_HD inline size_t fa_mma_smem_bytes(int D) {
-    const size_t ring = (size_t)kFmGroups * kFmStages * 2 * kFaChunk * D * 2;
+    const size_t ring = (size_t)kFmGroups * kFmStages * 2 * kFaChunk * D * 2 + 1024;  // + alignment of the TMA boxes
     const size_t merge = ((size_t)(4 * kFmGroups + 1) * kFaMaxG * D + 48 * kFaMaxG) * sizeof(float);
     return ring > merge ? ring : merge;
 }
 
 template <int D>
-__global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const FaArgs a) {
+__global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constant__ FaArgs a) {
     constexpr int KT = D / 16;       // k tiles of the QK^T product
     constexpr int NT = D / 8;        // n tiles of the PV product
     constexpr int GR = D / 8;        // 16-byte granules per K/V row
-    constexpr int ROWB = 2 * D;      // bytes per K/V row in shared memory
-    constexpr int TILE = kFaChunk * ROWB;
+    constexpr int BOXB = kFaChunk * 128;  // one TMA box: 64 positions x 64 halves
+    constexpr int NB = D / 64;            // boxes per K (or V) tile
+    constexpr int TILE = NB * BOXB;       // K (or V) tile of one chunk
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = 4 * kFmGroups;  // warps per CTA
     __shared__ float wm[NW][kFaMaxG], wl[NW][kFaMaxG];
@@ -114,7 +116,9 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const FaArgs a) {
     const int c_begin = split * a.chunks_per_split;
     const int c_end = min(c_begin + a.chunks_per_split, nchunks_ctx);
     const bool active = c_begin < c_end;
-    const uint32_t sbase = smem_u32(smem);
+    const uint32_t sbase = (smem_u32(smem) + 1023u) & ~1023u;  // TMA 128-byte swizzle: 1 KiB aligned boxes
+    __shared__ __align__(8) uint64_t fbar[kFmGroups][kFmStages];
+    __shared__ int fabort[kFmGroups];
 
     float m_run = -INFINITY, l_run = 0.f;  // head g of this warp's positions
     float o[NT][4];
@@ -125,32 +129,26 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const FaArgs a) {
     const int ncg = active ? (c_end - c_begin - grp + kFmGroups - 1) / kFmGroups : 0;
     if (ncg > 0) {
         const uint32_t gbase = sbase + (uint32_t)(grp * kFmStages * 2 * TILE);
-        // Each thread always copies granule cg = gtid % GR of rows
-        // gtid / GR + (128 / GR) i, so its source offsets and the swizzled
-        // destination column are fixed for the whole split.
-        constexpr int RPI = 128 / GR;  // rows covered per pass
-        const int cg = gtid % GR, r0 = gtid / GR;
-        const uint32_t swz = (uint32_t)((cg ^ (r0 & 7)) << 4);  // (r0 + RPI i) & 7 == r0 & 7
-        const uint8_t* kb = a.k + (int64_t)hk * a.k_nb2 + cg * 16;
-        const uint8_t* vb = a.v + (int64_t)hk * a.v_nb2 + cg * 16;
-        auto load_chunk = [&](int c, int stage) {
-            const uint32_t kst = gbase + (uint32_t)(stage * 2 * TILE) + (uint32_t)(r0 * ROWB) + swz;
-            const uint32_t vst = kst + TILE;
-            const int p0 = c * kFaChunk + r0;
-            const uint8_t* kp = kb + (int64_t)p0 * a.k_nb1;
-            const uint8_t* vp = vb + (int64_t)p0 * a.v_nb1;
+        uint64_t* bars = fbar[grp];
+        const int cfirst = c_begin + grp;
+        // chunk ci of this group -> stage ci % kFmStages; one thread issues
+        auto issue = [&](int ci) {
+            const int st = ci % kFmStages;
+            const int p0 = (cfirst + kFmGroups * ci) * kFaChunk;
+            const uint32_t kdst = gbase + (uint32_t)(st * 2 * TILE);
+            mbar_arrive_expect_tx(&bars[st], 2 * TILE);
 #pragma unroll
-            for (int i = 0; i < kFaChunk / RPI; ++i) {
-                const bool ok = p0 + RPI * i < ctx;
-                cp_async16(kst + (uint32_t)(RPI * i * ROWB), ok ? kp + (int64_t)RPI * i * a.k_nb1 : a.k, ok ? 16 : 0);
-                cp_async16(vst + (uint32_t)(RPI * i * ROWB), ok ? vp + (int64_t)RPI * i * a.v_nb1 : a.v, ok ? 16 : 0);
+            for (int b = 0; b < NB; ++b) {
+                tma_load_3d(kdst + b * BOXB, &a.tmk, 64 * b, hk, p0, &bars[st]);
+                tma_load_3d(kdst + TILE + b * BOXB, &a.tmv, 64 * b, hk, p0, &bars[st]);
             }
         };
-        const int cfirst = c_begin + grp;
-        load_chunk(cfirst, 0);
-        cp_async_commit();
-        if (ncg > 1) load_chunk(cfirst + kFmGroups, 1);
-        cp_async_commit();
+        if (gtid == 0) {
+            for (int st = 0; st < kFmStages; ++st) mbar_init(&bars[st], 1);
+            mbar_fence_init();
+            fabort[grp] = 0;
+            for (int ci = 0; ci < ncg && ci < kFmStages; ++ci) issue(ci);
+        }
 
         // Q fragments (A operand, rows = heads; rows 8..15 are zero), loaded
         // while the first K/V copies are in flight
@@ -166,14 +164,26 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const FaArgs a) {
                 qa[kt][1] = hv ? pack_half2(x1.x, x1.y) : 0u;
             }
         }
+        group_sync(grp);  // barrier init visible to the group
 
-        for (int ci = 0; ci < ncg; ++ci) {
+        int ci = 0;
+        for (; ci < ncg; ++ci) {
             const int c = cfirst + kFmGroups * ci;
             const int stage = ci % kFmStages;
-            if (ci + 2 < ncg) load_chunk(c + 2 * kFmGroups, (ci + 2) % kFmStages);
-            cp_async_commit();
-            cp_async_wait<2>();
+            if (!mbar_wait_bounded(&bars[stage], (uint32_t)((ci / kFmStages) & 1))) fabort[grp] = 1;
+            // V rows at or past the context hold no cache data: zero them
+            const int valid = ctx - c * kFaChunk;
+            if (valid < kFaChunk) {
+                const uint32_t vz = gbase + (uint32_t)(stage * 2 * TILE + TILE);
+                const int r0 = valid > 0 ? valid : 0;
+                for (int u = gtid; u < (kFaChunk - r0) * NB * 8; u += 128) {
+                    const int row = r0 + u / (NB * 8), rem = u - (u / (NB * 8)) * (NB * 8);
+                    const uint32_t addr = vz + (uint32_t)((rem >> 3) * BOXB + row * 128 + ((rem & 7) << 4));
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+                }
+            }
             group_sync(grp);  // chunk c is in shared memory for every warp of the group
+            if (fabort[grp]) break;
 
             const uint32_t kst = gbase + (uint32_t)(stage * 2 * TILE);
             const uint32_t vst = kst + TILE;
@@ -187,7 +197,8 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const FaArgs a) {
 #pragma unroll
                 for (int kt = 0; kt < KT; ++kt) {
                     uint32_t b[4];
-                    ldsm_x4(b, kst + (uint32_t)(r * ROWB + (((2 * kt + hh) ^ ri) << 4)));
+                    const int gk = 2 * kt + hh;  // 16-byte granule of the row
+                    ldsm_x4(b, kst + (uint32_t)((gk >> 3) * BOXB + r * 128 + (((gk & 7) ^ ri) << 4)));
                     const uint32_t af[4] = {qa[kt][0], 0u, qa[kt][1], 0u};
                     mma_16816(s[0], af, b[0], b[1]);
                     mma_16816(s[1], af, b[2], b[3]);
@@ -245,56 +256,82 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const FaArgs a) {
 #pragma unroll
                 for (int jj = 0; jj < NT / 2; ++jj) {
                     uint32_t b[4];
-                    ldsm_x4_trans(b, vst + (uint32_t)(r * ROWB + (((2 * jj + jn) ^ ri) << 4)));
+                    const int gv = 2 * jj + jn;
+                    ldsm_x4_trans(b, vst + (uint32_t)((gv >> 3) * BOXB + r * 128 + (((gv & 7) ^ ri) << 4)));
                     mma_16816(o[2 * jj], pa_hi, b[0], b[1]);
                     mma_16816(o[2 * jj], pa_lo, b[0], b[1]);
                     mma_16816(o[2 * jj + 1], pa_hi, b[2], b[3]);
                     mma_16816(o[2 * jj + 1], pa_lo, b[2], b[3]);
                 }
             }
-            group_sync(grp);  // stage may be refilled by the next iteration
+            group_sync(grp);  // every warp is done with this stage
+            if (gtid == 0 && ci + kFmStages < ncg) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue(ci + kFmStages);
+            }
         }
-        cp_async_wait<0>();
+        if (ci < ncg && gtid == 0) {
+            // a wait expired: let the copies still in flight land before the
+            // shared memory is reused or the CTA exits
+            for (int cj = ci; cj < ncg && cj < ci + kFmStages; ++cj)
+                mbar_wait_bounded(&bars[cj % kFmStages], (uint32_t)((cj / kFmStages) & 1));
+        }
     }
 
     // ---- combine the NW warps into this CTA's partial (shared memory re-used) ----
-    float* wo = reinterpret_cast<float*>(smem);             // [NW][kFaMaxG][D]
+    // Per (warp, head) weights exp(m_warp - M) are computed once; every warp
+    // scales its output by its weight and the scaled outputs are summed in
+    // warp order.
+    float* wo = reinterpret_cast<float*>(smem);             // [NW][kFaMaxG][D] scaled warp outputs
     float* co = wo + NW * kFaMaxG * D;                        // [kFaMaxG][D]  this CTA's partial
     float* wr = co + kFaMaxG * D;                             // [kFaMaxG][16] merge weights
     float* allm = wr + kFaMaxG * 16;                          // [16][kFaMaxG]
     float* alll = allm + 16 * kFaMaxG;                        // [16][kFaMaxG]
-    __shared__ float cm[kFaMaxG], cl[kFaMaxG];
-    __syncthreads();
+    __shared__ float cm[kFaMaxG], cl[kFaMaxG], ew[NW][kFaMaxG];
+    __syncthreads();  // the rings are no longer read
     if (t == 0) {
         wm[warp][g] = m_run;
         wl[warp][g] = l_run;
     }
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-        wo[((warp * kFaMaxG) + g) * D + 8 * n + 2 * t] = o[n][0];
-        wo[((warp * kFaMaxG) + g) * D + 8 * n + 2 * t + 1] = o[n][1];
-    }
     __syncthreads();
-    for (int idx = tid; idx < kFaMaxG * D; idx += kFmThreads) {
-        const int h = idx / D, d = idx - (idx / D) * D;
+    if (tid < kFaMaxG) {
+        const int h = tid;
         float M = -INFINITY;
         if (active && h < hn)
 #pragma unroll
             for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][h]);
-        float ov = 0.f, lv = 0.f;
-        if (M != -INFINITY) {
+        float L = 0.f;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) {
-                const float e = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
-                ov = fmaf(wo[((w * kFaMaxG) + h) * D + d], e, ov);
-                lv = fmaf(wl[w][h], e, lv);
-            }
+        for (int w = 0; w < NW; ++w) {
+            const float e = (M == -INFINITY || wm[w][h] == -INFINITY) ? 0.f : expf(wm[w][h] - M);
+            ew[w][h] = e;
+            L = fmaf(wl[w][h], e, L);
         }
-        co[h * D + d] = ov;
-        if (d == 0) {
-            cm[h] = M;
-            cl[h] = lv;
+        cm[h] = M;
+        cl[h] = L;
+    }
+    __syncthreads();
+    {
+        const float e = ew[warp][g];
+        float* dst = wo + ((warp * kFaMaxG) + g) * D + 2 * t;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            dst[8 * n] = o[n][0] * e;
+            dst[8 * n + 1] = o[n][1] * e;
         }
+    }
+    __syncthreads();
+    for (int i4 = tid; i4 < kFaMaxG * D / 4; i4 += kFmThreads) {
+        float4 acc = reinterpret_cast<const float4*>(wo)[i4];
+#pragma unroll
+        for (int w = 1; w < NW; ++w) {
+            const float4 v = reinterpret_cast<const float4*>(wo + w * kFaMaxG * D)[i4];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        reinterpret_cast<float4*>(co)[i4] = acc;
     }
 
     // ---- cluster merge over the splits (distributed shared memory) ----
@@ -323,16 +360,27 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const FaArgs a) {
         for (int r = 0; r < S; ++r) wr[h * 16 + r] *= inv;
     }
     __syncthreads();
-    const int tot = hn * D;
-    const int o0 = rank * tot / S, o1 = (rank + 1) * tot / S;
-    for (int idx = o0 + tid; idx < o1; idx += kFmThreads) {
-        const int h = idx / D, d = idx - (idx / D) * D;
-        float acc = 0.f;
-        for (int r = 0; r < S; ++r) {
-            const float w = wr[h * 16 + r];
-            if (w != 0.f) acc = fmaf(*cluster.map_shared_rank(co + h * D + d, r), w, acc);
-        }
-        a.out[(int64_t)(h0 + h) * D + d] = acc;
+    // this CTA's slice of the outputs, 4 floats per thread: all S peer loads
+    // are issued before the sums
+    const int tot4 = hn * D / 4;
+    const int o0 = rank * tot4 / S, o1 = (rank + 1) * tot4 / S;
+    for (int i4 = o0 + tid; i4 < o1; i4 += kFmThreads) {
+        const int h = (4 * i4) / D, d = 4 * i4 - h * D;
+        float4 v[kFmMaxCluster];
+#pragma unroll
+        for (int r = 0; r < kFmMaxCluster; ++r)
+            if (r < S) v[r] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(co + h * D + d, r));
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < kFmMaxCluster; ++r)
+            if (r < S) {
+                const float w = wr[h * 16 + r];
+                acc.x = fmaf(v[r].x, w, acc.x);
+                acc.y = fmaf(v[r].y, w, acc.y);
+                acc.z = fmaf(v[r].z, w, acc.z);
+                acc.w = fmaf(v[r].w, w, acc.w);
+            }
+        *reinterpret_cast<float4*>(a.out + (int64_t)(h0 + h) * D + d) = acc;
     }
     cluster.sync();  // peers finish reading this CTA's shared memory before it exits
 }

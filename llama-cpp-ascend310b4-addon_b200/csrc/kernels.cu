@@ -5,6 +5,7 @@
 // code.  Host-side code elsewhere (graph runner, backend, decode driver)
 // reaches the kernels through include/b200_decode.h and internal.h.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -331,9 +332,45 @@ int set_fa_attrs() {
     return fa_cluster_probe<128>(dev);
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// K or V cache view [D, Hkv, n_kv] (byte strides nb2 per head, nb1 per
+// position) as a TMA descriptor with 64 x 1 x 64 boxes and the 128-byte
+// swizzle that the tensor-core kernel's ldmatrix addressing expects.
+int encode_kv_map(CUtensorMap* m, const void* base, int D, int Hkv, int n_kv, int64_t nb1, int64_t nb2) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return B200_ECUDA;
+    const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)Hkv, (cuuint64_t)n_kv};
+    const cuuint64_t strides[2] = {(cuuint64_t)nb2, (cuuint64_t)nb1};
+    const cuuint32_t box[3] = {64, 1, (cuuint32_t)kFaChunk};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        fprintf(stderr, "b200_decode: cuTensorMapEncodeTiled failed (%d)\n", (int)r);
+        return B200_EUNSUPPORTED;
+    }
+    return B200_OK;
+}
+
 template <int D>
 int launch_fa_mma(FaArgs a, cudaStream_t st, bool pdl) {
     const int dev = current_device();
+    CR_(encode_kv_map(&a.tmk, a.k, D, a.Hkv, a.n_kv, a.k_nb1, a.k_nb2));
+    CR_(encode_kv_map(&a.tmv, a.v, D, a.Hkv, a.n_kv, a.v_nb1, a.v_nb2));
     CR_(set_fa_attrs());
     const int nchunks = (a.n_kv + kFaChunk - 1) / kFaChunk;
     const int S = fa_pick_cluster<D>(dev, a.Hkv * a.gchunks, nchunks);
