@@ -112,6 +112,7 @@ int b200_gemv_block_dots(int type, const void *w_packed, const float *x, int32_t
  *        only the first kv_len[0] positions are read when 0 < kv_len[0] < n_kv
  *        (attention_step_custom.cpp:110-113; src[5] of patch:2009-2023)
  *   out  f32 [n_head][head_dim]
+ * q must be 8-byte and out 16-byte aligned.
  * s = scale * (f16(q) . k) + mask; positions whose mask is -inf are skipped.
  * The workspace (b200_fa_workspace_size bytes) must be zero-filled before its
  * first use; every call leaves its counters zero again.  Calls that share a

@@ -17,10 +17,10 @@
 // independent load/mma/softmax chains run per SM.  Each warp owns 16
 // positions of its group's chunks and keeps its own online-softmax state
 // (max, sum, output); the eight warps are combined in shared memory.  The
-// splits of one (kv head, head chunk) form one thread-block cluster: after a
-// cluster barrier every CTA merges a slice of the outputs by reading its
-// peers' partial results through distributed shared memory, so partials never
-// leave the SMs.
+// splits of one (kv head, head chunk) form one thread-block cluster: every
+// CTA stores its partial of each slice of the outputs into the shared memory
+// of the CTA that owns the slice (distributed shared memory), and after one
+// cluster barrier the owners merge locally, so partials never leave the SMs.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -77,12 +77,12 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 
 // Shared memory of fa_mma_kernel<D>: per warp group kFmStages x (K tile + V
 // tile) of kFaChunk rows x D halves; reused after the loop for the warp
-// combine and the cluster merge (which need (4 kFmGroups + 1) x kFaMaxG x D
-// floats plus 48 x kFaMaxG).
+// combine (4 kFmGroups x kFaMaxG padded rows of D + 8 floats plus the CTA
+// partial, kFaMaxG x D floats).
 constexpr int kFmMaxCluster = 16;
 B200_HD inline size_t fa_mma_smem_bytes(int D) {
     const size_t ring = (size_t)kFmGroups * kFmStages * 2 * kFaChunk * D * 2 + 1024;  // + alignment of the TMA boxes
-    const size_t merge = ((size_t)(4 * kFmGroups + 1) * kFaMaxG * D + 48 * kFaMaxG) * sizeof(float);
+    const size_t merge = ((size_t)4 * kFmGroups * kFaMaxG * (D + 8) + (size_t)kFaMaxG * D) * sizeof(float);
     return ring > merge ? ring : merge;
 }
 
@@ -195,14 +195,23 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
                 const int j = mi >> 1, hh = mi & 1;
                 const int r = pw + 8 * j + ri;
 #pragma unroll
+                // two accumulator chains (even / odd k tiles) halve the
+                // dependent mma sequence
+                float s2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
                 for (int kt = 0; kt < KT; ++kt) {
                     uint32_t b[4];
                     const int gk = 2 * kt + hh;  // 16-byte granule of the row
                     ldsm_x4(b, kst + (uint32_t)((gk >> 3) * BOXB + r * 128 + (((gk & 7) ^ ri) << 4)));
                     const uint32_t af[4] = {qa[kt][0], 0u, qa[kt][1], 0u};
-                    mma_16816(s[0], af, b[0], b[1]);
-                    mma_16816(s[1], af, b[2], b[3]);
+                    float(*acc)[4] = (kt & 1) ? s2 : s;
+                    mma_16816(acc[0], af, b[0], b[1]);
+                    mma_16816(acc[1], af, b[2], b[3]);
                 }
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[j][e] += s2[j][e];
             }
             // ---- scale, mask, online softmax (rows = head g) ----
             const int pbase = c * kFaChunk + pw;
@@ -281,12 +290,11 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
     // ---- combine the NW warps into this CTA's partial (shared memory re-used) ----
     // Per (warp, head) weights exp(m_warp - M) are computed once; every warp
     // scales its output by its weight and the scaled outputs are summed in
-    // warp order.
-    float* wo = reinterpret_cast<float*>(smem);             // [NW][kFaMaxG][D] scaled warp outputs
-    float* co = wo + NW * kFaMaxG * D;                        // [kFaMaxG][D]  this CTA's partial
-    float* wr = co + kFaMaxG * D;                             // [kFaMaxG][16] merge weights
-    float* allm = wr + kFaMaxG * 16;                          // [16][kFaMaxG]
-    float* alll = allm + 16 * kFaMaxG;                        // [16][kFaMaxG]
+    // warp order.  Rows are padded by 8 floats so the float2 stores of a
+    // warp do not collide in shared-memory banks.
+    constexpr int WS = D + 8;                                 // padded row stride (floats)
+    float* wo = reinterpret_cast<float*>(smem);             // [NW][kFaMaxG][WS] scaled warp outputs
+    float* co = wo + NW * kFaMaxG * WS;                       // [kFaMaxG][D]  this CTA's partial
     __shared__ float cm[kFaMaxG], cl[kFaMaxG], ew[NW][kFaMaxG];
     __syncthreads();  // the rings are no longer read
     if (t == 0) {
@@ -313,19 +321,17 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
     __syncthreads();
     {
         const float e = ew[warp][g];
-        float* dst = wo + ((warp * kFaMaxG) + g) * D + 2 * t;
+        float2* dst = reinterpret_cast<float2*>(wo + ((warp * kFaMaxG) + g) * WS + 2 * t);
 #pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            dst[8 * n] = o[n][0] * e;
-            dst[8 * n + 1] = o[n][1] * e;
-        }
+        for (int n = 0; n < NT; ++n) dst[4 * n] = make_float2(o[n][0] * e, o[n][1] * e);
     }
     __syncthreads();
     for (int i4 = tid; i4 < kFaMaxG * D / 4; i4 += kFmThreads) {
-        float4 acc = reinterpret_cast<const float4*>(wo)[i4];
+        const int h = (4 * i4) / D, d = 4 * i4 - h * D;
+        float4 acc = *reinterpret_cast<const float4*>(wo + h * WS + d);
 #pragma unroll
         for (int w = 1; w < NW; ++w) {
-            const float4 v = reinterpret_cast<const float4*>(wo + w * kFaMaxG * D)[i4];
+            const float4 v = *reinterpret_cast<const float4*>(wo + (w * kFaMaxG + h) * WS + d);
             acc.x += v.x;
             acc.y += v.y;
             acc.z += v.z;
@@ -333,56 +339,66 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
         }
         reinterpret_cast<float4*>(co)[i4] = acc;
     }
+    __syncthreads();
 
-    // ---- cluster merge over the splits (distributed shared memory) ----
+    // ---- cluster merge over the splits (distributed shared memory, push) ----
+    // CTA k of the cluster owns outputs [k tot4 / S, (k+1) tot4 / S) (in
+    // float4 units).  Every CTA stores its partial of each owner's slice, and
+    // its (max, sum) per head, straight into the owner's shared memory; after
+    // one cluster barrier every owner merges from local shared memory, and no
+    // CTA touches a peer's shared memory again.
+    constexpr int kTot4Max = kFaMaxG * D / 4;
+    __shared__ __align__(16) float4 rcv[kTot4Max + kFmMaxCluster];  // [S][slice4]
+    __shared__ float rml[kFmMaxCluster][kFaMaxG][2];
+    __shared__ float wr[kFaMaxG][kFmMaxCluster];
     cgx::cluster_group cluster = cgx::this_cluster();
     const int S = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
-    cluster.sync();  // every CTA's partial is complete and visible
-    if (tid < S * kFaMaxG) {
-        const int r = tid / kFaMaxG, h = tid - (tid / kFaMaxG) * kFaMaxG;
-        allm[r * kFaMaxG + h] = *cluster.map_shared_rank(&cm[h], r);
-        alll[r * kFaMaxG + h] = *cluster.map_shared_rank(&cl[h], r);
+    const int tot4 = hn * D / 4;
+    const int slice4 = (tot4 + S - 1) / S;
+    for (int i4 = tid; i4 < tot4; i4 += kFmThreads) {
+        int k = (int)(((int64_t)i4 * S + S - 1) / tot4);  // owner: k tot4 / S <= i4 < (k+1) tot4 / S
+        while (k > 0 && k * tot4 / S > i4) --k;
+        while (k + 1 < S && (k + 1) * tot4 / S <= i4) ++k;
+        float4* dst = cluster.map_shared_rank(rcv, k);
+        dst[rank * slice4 + (i4 - k * tot4 / S)] = reinterpret_cast<const float4*>(co)[i4];
     }
-    __syncthreads();
+    if (tid < S * kFaMaxG) {
+        const int k = tid / kFaMaxG, h = tid - (tid / kFaMaxG) * kFaMaxG;
+        float* dst = &cluster.map_shared_rank(&rml[0][0][0], k)[(rank * kFaMaxG + h) * 2];
+        dst[0] = cm[h];
+        dst[1] = cl[h];
+    }
+    cluster.sync();  // every push has landed
     if (tid < hn) {
         const int h = tid;
         float M = -INFINITY;
-        for (int r = 0; r < S; ++r) M = fmaxf(M, allm[r * kFaMaxG + h]);
+        for (int r = 0; r < S; ++r) M = fmaxf(M, rml[r][h][0]);
         float L = 0.f;
         for (int r = 0; r < S; ++r) {
-            const float mr = allm[r * kFaMaxG + h];
+            const float mr = rml[r][h][0];
             const float e = (mr == -INFINITY) ? 0.f : expf(mr - M);
-            wr[h * 16 + r] = e;
-            L = fmaf(alll[r * kFaMaxG + h], e, L);
+            wr[h][r] = e;
+            L = fmaf(rml[r][h][1], e, L);
         }
         const float inv = L > 0.f ? 1.0f / L : 0.f;
-        for (int r = 0; r < S; ++r) wr[h * 16 + r] *= inv;
+        for (int r = 0; r < S; ++r) wr[h][r] *= inv;
     }
     __syncthreads();
-    // this CTA's slice of the outputs, 4 floats per thread: all S peer loads
-    // are issued before the sums
-    const int tot4 = hn * D / 4;
     const int o0 = rank * tot4 / S, o1 = (rank + 1) * tot4 / S;
     for (int i4 = o0 + tid; i4 < o1; i4 += kFmThreads) {
         const int h = (4 * i4) / D, d = 4 * i4 - h * D;
-        float4 v[kFmMaxCluster];
-#pragma unroll
-        for (int r = 0; r < kFmMaxCluster; ++r)
-            if (r < S) v[r] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(co + h * D + d, r));
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int r = 0; r < kFmMaxCluster; ++r)
-            if (r < S) {
-                const float w = wr[h * 16 + r];
-                acc.x = fmaf(v[r].x, w, acc.x);
-                acc.y = fmaf(v[r].y, w, acc.y);
-                acc.z = fmaf(v[r].z, w, acc.z);
-                acc.w = fmaf(v[r].w, w, acc.w);
-            }
+        for (int r = 0; r < S; ++r) {
+            const float w = wr[h][r];
+            const float4 v = rcv[r * slice4 + (i4 - o0)];
+            acc.x = fmaf(v.x, w, acc.x);
+            acc.y = fmaf(v.y, w, acc.y);
+            acc.z = fmaf(v.z, w, acc.z);
+            acc.w = fmaf(v.w, w, acc.w);
+        }
         *reinterpret_cast<float4*>(a.out + (int64_t)(h0 + h) * D + d) = acc;
     }
-    cluster.sync();  // peers finish reading this CTA's shared memory before it exits
 }
 
 }  // namespace b200

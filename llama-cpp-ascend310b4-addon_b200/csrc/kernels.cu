@@ -594,6 +594,7 @@ int b200_fa_decode(const float* q, const void* k, const void* v, const void* mas
                    int64_t v_nb1, int64_t v_nb2, float scale, void* workspace, size_t workspace_size,
                    b200_stream_t stream) {
     if (!q || !k || !v || !out || !workspace) return B200_EINVAL;
+    if (!aligned16(out) || (reinterpret_cast<uintptr_t>(q) & 7)) return B200_EINVAL;
     if (n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv || n_kv <= 0) return B200_EINVAL;
     if (head_dim != 64 && head_dim != 128 && head_dim != 256) return B200_EUNSUPPORTED;
     if (!aligned16(k) || !aligned16(v) || (k_nb1 & 15) || (k_nb2 & 15) || (v_nb1 & 15) || (v_nb2 & 15))
