@@ -448,26 +448,63 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     if (lane == 0) {
         for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
         mbar_fence_init();
-        for (int s = 0; s < S && s < nq; ++s) issue(s);
+        if (nq > 0) issue(0);
     }
-    // The weight stream above reads only constant data, so under a
+    // The first stage of every ring reads only constant data, so under a
     // programmatic launch it overlaps the previous kernel's tail; the
     // activation, residual and outputs are touched only after this wait.
     griddep_wait();
     griddep_launch_dependents();
 
     // ---- prologue: the activation, once per CTA, into shared memory ----
-    float nscale = 1.f;
+    // Fast path (Q8_0 activations, at most two 32-blocks per thread, one
+    // with RMSNorm): every thread loads its blocks of x (and of the norm
+    // weights) into registers BEFORE the rest of the weight ring is issued,
+    // so these latency-critical loads do not queue behind megabytes of
+    // weight copies; the blocks are then quantised from registers.
+    constexpr bool kQ8Act = FMT == FMT_Q4 || FMT == FMT_Q8;
     const bool norm = a.pro == PRO_RMSNORM;
+    const int nbt = (P.U + kGemvThreads - 1) / kGemvThreads;
+    const bool fast = kQ8Act && (norm ? nbt <= 1 : nbt <= 2);
+    // xv[0..7]: block tid of x; xv[8..15]: its norm weights (RMSNorm) or
+    // block tid + kGemvThreads of x (no norm)
+    float4 xv[16];
+    if (fast) {
+        if (tid < P.U) {
+            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)tid * 32);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xv[e] = src[e];
+        }
+        const float4* second = norm ? reinterpret_cast<const float4*>(a.norm_w + (int64_t)tid * 32)
+                                    : reinterpret_cast<const float4*>(a.x + (int64_t)(tid + kGemvThreads) * 32);
+        if (norm ? tid < P.U : tid + kGemvThreads < P.U)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xv[8 + e] = second[e];
+    }
+    if (lane == 0)
+        for (int s = 1; s < S && s < nq; ++s) issue(s);
+
+    float nscale = 1.f;
     if (norm) {
         float ss = 0.f;
-        const float4* x4 = reinterpret_cast<const float4*>(a.x);
-        for (int64_t i = tid; i < a.k / 4; i += kGemvThreads) {
-            const float4 v = x4[i];
-            ss = fmaf(v.x, v.x, ss);
-            ss = fmaf(v.y, v.y, ss);
-            ss = fmaf(v.z, v.z, ss);
-            ss = fmaf(v.w, v.w, ss);
+        if (fast) {
+            if (tid < P.U)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    ss = fmaf(xv[e].x, xv[e].x, ss);
+                    ss = fmaf(xv[e].y, xv[e].y, ss);
+                    ss = fmaf(xv[e].z, xv[e].z, ss);
+                    ss = fmaf(xv[e].w, xv[e].w, ss);
+                }
+        } else {
+            const float4* x4 = reinterpret_cast<const float4*>(a.x);
+            for (int64_t i = tid; i < a.k / 4; i += kGemvThreads) {
+                const float4 v = x4[i];
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+            }
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
@@ -478,10 +515,37 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         const float mean = __fdiv_rn(tot, (float)a.k);
         nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
     }
-    if constexpr (FMT == FMT_Q4 || FMT == FMT_Q8) {
+    if constexpr (kQ8Act) {
         int4* xq = reinterpret_cast<int4*>(xr);
         int2* xds = reinterpret_cast<int2*>(xr + 32 * (int64_t)P.U);
-        for (int b = tid; b < P.U; b += kGemvThreads) {
+        if (fast) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int b = tid + j * kGemvThreads;
+                if (j < nbt && b < P.U) {
+                    auto load = [&](int e) -> float4 {
+                        float4 v = xv[8 * j + e];
+                        if (norm) {
+                            v.x = __fmul_rn(__fmul_rn(v.x, nscale), xv[8 + e].x);
+                            v.y = __fmul_rn(__fmul_rn(v.y, nscale), xv[8 + e].y);
+                            v.z = __fmul_rn(__fmul_rn(v.z, nscale), xv[8 + e].z);
+                            v.w = __fmul_rn(__fmul_rn(v.w, nscale), xv[8 + e].w);
+                        }
+                        return v;
+                    };
+                    int q[8];
+                    float d;
+                    uint16_t dh;
+                    int qs;
+                    quantize_block32(load, q, d, dh, qs);
+                    xq[b] = make_int4(q[0], q[1], q[2], q[3]);
+                    xq[P.U + b] = make_int4(q[4], q[5], q[6], q[7]);
+                    xds[b] = make_int2(__float_as_int(d), qs);
+                    if (a.xq_out != nullptr && blockIdx.x == 0) store_block_q8_0(a.xq_out + (int64_t)b * 34, dh, q);
+                }
+            }
+        }
+        for (int b = fast ? P.U : tid; b < P.U; b += kGemvThreads) {
             const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)b * 32);
             const float4* wn = reinterpret_cast<const float4*>(a.norm_w + (int64_t)b * 32);
             auto load = [&](int e) -> float4 {
