@@ -53,7 +53,7 @@ struct GemvPlan {
     int tpr;            // lanes per row (32 / rpc)
     int tpr_log2;
     int upl;            // units per lane per chunk row
-    int full_upl;       // units per lane of a full chunk (rpc == 1 and kc % 64 == 0), else 0
+    int full_upl;       // units per lane of a full chunk (rpc == 1 and kc % 32 == 0), else 0
     int64_t stage_bytes;
 };
 
@@ -98,12 +98,13 @@ B200_HD inline bool make_plan(int type, int64_t n, int64_t k, GemvPlan* p) {
         p->rpc = 1;
         p->tpr = 32;
         p->tpr_log2 = 5;
-        // Chunk width: a multiple of 64 (every full chunk gives each lane the
-        // same even number of units and keeps the scale plane 16-byte
-        // aligned); prefer the widest one that divides the row, so that no
-        // row ends in a partial chunk.
+        // Chunk width: a multiple of 32 (every full chunk gives each lane the
+        // same number of units; the scale plane stays 16-byte aligned);
+        // prefer the widest one that divides the row, so that no row ends in
+        // a partial chunk.  Otherwise: the row in equal chunks, rounded up to
+        // a multiple of 64.
         int kc = 0;
-        for (int c = kc_max; c >= 64; c -= 64)
+        for (int c = kc_max; c >= 64; c -= 32)
             if (U % c == 0) {
                 kc = c;
                 break;
@@ -116,7 +117,7 @@ B200_HD inline bool make_plan(int type, int64_t n, int64_t k, GemvPlan* p) {
         p->kc = kc;
         p->nchunk = (U + kc - 1) / kc;
         p->upl = (kc + 31) / 32;
-        p->full_upl = (kc % 64 == 0) ? kc / 32 : 0;
+        p->full_upl = (kc % 32 == 0) ? kc / 32 : 0;
         p->stage_bytes = gemv_stage_bytes_rpc1(type, kc);
     } else {
         int rpc = 32;

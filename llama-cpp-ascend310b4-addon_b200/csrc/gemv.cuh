@@ -341,6 +341,122 @@ __device__ __forceinline__ float chunk_full_dot(const uint8_t* st, int kc, int l
     }
 }
 
+// ------------------------------------------------------------ activation
+
+// x -> Q8_0 activation planes in shared memory (optionally RMSNorm * w first),
+// quantize_row_q8_0_ref's rule on each 32-block.  Eight consecutive lanes
+// share a block, one float4 each, so every warp load is fully coalesced; the
+// block max and the sum of q are 8-lane shuffle reductions (order free, so the
+// bytes and scales equal a one-thread-per-block quantiser's).  `after_issue`
+// runs once the first loads are in flight (the caller issues its remaining
+// weight copies there).  Ends with __syncthreads.
+template <class AfterIssue>
+__device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan& P, uint8_t* xr, float* red, int tid,
+                                              int lane, int warp, AfterIssue after_issue) {
+    constexpr int R = 8;  // float4 units per thread held in registers at once
+    const bool norm = a.pro == PRO_RMSNORM;
+    const int nu = P.U * 8;  // float4 units of x
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
+    float4 xv[R], wv[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const int u = tid + i * kGemvThreads;
+        if (u < nu) {
+            xv[i] = x4[u];
+            if (norm) wv[i] = w4[u];
+        }
+    }
+    after_issue();
+    const bool resident = nu <= R * kGemvThreads;  // every unit of x is in registers
+    float nscale = 1.f;
+    if (norm) {
+        float ss = 0.f;
+        if (resident) {
+#pragma unroll
+            for (int i = 0; i < R; ++i)
+                if (tid + i * kGemvThreads < nu) {
+                    ss = fmaf(xv[i].x, xv[i].x, ss);
+                    ss = fmaf(xv[i].y, xv[i].y, ss);
+                    ss = fmaf(xv[i].z, xv[i].z, ss);
+                    ss = fmaf(xv[i].w, xv[i].w, ss);
+                }
+        } else {
+            for (int u = tid; u < nu; u += kGemvThreads) {
+                const float4 v = x4[u];
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) tot += red[w];
+        const float mean = __fdiv_rn(tot, (float)a.k);
+        nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+    }
+    int* xw = reinterpret_cast<int*>(xr);                       // plane 0: words 0..3 of block b at 4b
+    int2* xds = reinterpret_cast<int2*>(xr + 32 * (int64_t)P.U);  // {d, sum q}
+    const int wd = lane & 7;                                    // word of the block held by this lane
+    for (int base = 0; base < nu; base += R * kGemvThreads) {
+        if (base > 0) {  // next round: all of its loads in flight before any use
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                const int u = base + tid + i * kGemvThreads;
+                if (u < nu) {
+                    xv[i] = x4[u];
+                    if (norm) wv[i] = w4[u];
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int u = base + tid + i * kGemvThreads;
+            if (u >= nu) continue;  // whole 8-lane groups drop out together (nu is a multiple of 8)
+            float4 v = xv[i];
+            if (norm) {
+                const float4 w = wv[i];
+                v.x = __fmul_rn(__fmul_rn(v.x, nscale), w.x);
+                v.y = __fmul_rn(__fmul_rn(v.y, nscale), w.y);
+                v.z = __fmul_rn(__fmul_rn(v.z, nscale), w.z);
+                v.w = __fmul_rn(__fmul_rn(v.w, nscale), w.w);
+            }
+            float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+            const unsigned gm = 0xffu << (lane & 24);  // this 8-lane group
+            amax = fmaxf(amax, __shfl_xor_sync(gm, amax, 1, 8));
+            amax = fmaxf(amax, __shfl_xor_sync(gm, amax, 2, 8));
+            amax = fmaxf(amax, __shfl_xor_sync(gm, amax, 4, 8));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.f ? __frcp_rn(d) : 0.f;
+            const int q0 = round_half_away(__fmul_rn(v.x, id));
+            const int q1 = round_half_away(__fmul_rn(v.y, id));
+            const int q2 = round_half_away(__fmul_rn(v.z, id));
+            const int q3 = round_half_away(__fmul_rn(v.w, id));
+            int qs = q0 + q1 + q2 + q3;
+            qs += __shfl_xor_sync(gm, qs, 1, 8);
+            qs += __shfl_xor_sync(gm, qs, 2, 8);
+            qs += __shfl_xor_sync(gm, qs, 4, 8);
+            const int word = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) |
+                                   ((unsigned)(q2 & 0xff) << 16) | ((unsigned)(q3 & 0xff) << 24));
+            const int b = u >> 3;
+            xw[(wd < 4 ? 0 : 4 * P.U) + 4 * b + (wd & 3)] = word;
+            const uint16_t dh = f2h(d);
+            if (wd == 0) xds[b] = make_int2(__float_as_int(h2f(dh)), qs);
+            if (a.xq_out != nullptr && blockIdx.x == 0) {
+                uint16_t* o = reinterpret_cast<uint16_t*>(a.xq_out + (int64_t)b * 34);
+                if (wd == 0) o[0] = dh;
+                o[1 + 2 * wd] = (uint16_t)((unsigned)word & 0xffffu);
+                o[2 + 2 * wd] = (uint16_t)((unsigned)word >> 16);
+            }
+        }
+    }
+    __syncthreads();
+}
+
 // ------------------------------------------------------------ the kernel
 
 // UPL: units per lane of this plan's full chunks (P.full_upl), or 0 when the
@@ -457,46 +573,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     griddep_launch_dependents();
 
     // ---- prologue: the activation, once per CTA, into shared memory ----
-    // Fast path (Q8_0 activations, at most two 32-blocks per thread, one
-    // with RMSNorm): every thread loads its blocks of x (and of the norm
-    // weights) into registers BEFORE the rest of the weight ring is issued,
-    // so these latency-critical loads do not queue behind megabytes of
-    // weight copies; the blocks are then quantised from registers.
-    constexpr bool kQ8Act = FMT == FMT_Q4 || FMT == FMT_Q8;
+    // Q8_0 activations: every thread's first loads of x (and of the norm
+    // weights) are issued BEFORE the rest of the weight ring, so these
+    // latency-critical loads do not queue behind megabytes of weight copies.
     const bool norm = a.pro == PRO_RMSNORM;
-    const int nbt = (P.U + kGemvThreads - 1) / kGemvThreads;
-    const bool fast = kQ8Act && (norm ? nbt <= 1 : nbt <= 2);
-    // xv[0..7]: block tid of x; xv[8..15]: its norm weights (RMSNorm) or
-    // block tid + kGemvThreads of x (no norm)
-    float4 xv[16];
-    if (fast) {
-        if (tid < P.U) {
-            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)tid * 32);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) xv[e] = src[e];
-        }
-        const float4* second = norm ? reinterpret_cast<const float4*>(a.norm_w + (int64_t)tid * 32)
-                                    : reinterpret_cast<const float4*>(a.x + (int64_t)(tid + kGemvThreads) * 32);
-        if (norm ? tid < P.U : tid + kGemvThreads < P.U)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) xv[8 + e] = second[e];
-    }
-    if (lane == 0)
-        for (int s = 1; s < S && s < nq; ++s) issue(s);
-
-    float nscale = 1.f;
-    if (norm) {
-        float ss = 0.f;
-        if (fast) {
-            if (tid < P.U)
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    ss = fmaf(xv[e].x, xv[e].x, ss);
-                    ss = fmaf(xv[e].y, xv[e].y, ss);
-                    ss = fmaf(xv[e].z, xv[e].z, ss);
-                    ss = fmaf(xv[e].w, xv[e].w, ss);
-                }
-        } else {
+    if constexpr (FMT == FMT_Q4 || FMT == FMT_Q8) {
+        activation_q8(a, P, xr, red, tid, lane, warp, [&] {
+            if (lane == 0)
+                for (int s = 1; s < S && s < nq; ++s) issue(s);
+        });
+    } else {
+        if (lane == 0)
+            for (int s = 1; s < S && s < nq; ++s) issue(s);
+        float nscale = 1.f;
+        if (norm) {
+            float ss = 0.f;
             const float4* x4 = reinterpret_cast<const float4*>(a.x);
             for (int64_t i = tid; i < a.k / 4; i += kGemvThreads) {
                 const float4 v = x4[i];
@@ -505,71 +596,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
                 ss = fmaf(v.z, v.z, ss);
                 ss = fmaf(v.w, v.w, ss);
             }
-        }
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        float tot = 0.f;
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+            __syncthreads();
+            float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w) tot += red[w];
-        const float mean = __fdiv_rn(tot, (float)a.k);
-        nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-    }
-    if constexpr (kQ8Act) {
-        int4* xq = reinterpret_cast<int4*>(xr);
-        int2* xds = reinterpret_cast<int2*>(xr + 32 * (int64_t)P.U);
-        if (fast) {
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int b = tid + j * kGemvThreads;
-                if (j < nbt && b < P.U) {
-                    auto load = [&](int e) -> float4 {
-                        float4 v = xv[8 * j + e];
-                        if (norm) {
-                            v.x = __fmul_rn(__fmul_rn(v.x, nscale), xv[8 + e].x);
-                            v.y = __fmul_rn(__fmul_rn(v.y, nscale), xv[8 + e].y);
-                            v.z = __fmul_rn(__fmul_rn(v.z, nscale), xv[8 + e].z);
-                            v.w = __fmul_rn(__fmul_rn(v.w, nscale), xv[8 + e].w);
-                        }
-                        return v;
-                    };
-                    int q[8];
-                    float d;
-                    uint16_t dh;
-                    int qs;
-                    quantize_block32(load, q, d, dh, qs);
-                    xq[b] = make_int4(q[0], q[1], q[2], q[3]);
-                    xq[P.U + b] = make_int4(q[4], q[5], q[6], q[7]);
-                    xds[b] = make_int2(__float_as_int(d), qs);
-                    if (a.xq_out != nullptr && blockIdx.x == 0) store_block_q8_0(a.xq_out + (int64_t)b * 34, dh, q);
-                }
-            }
+            for (int w = 0; w < kGemvWarps; ++w) tot += red[w];
+            const float mean = __fdiv_rn(tot, (float)a.k);
+            nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
         }
-        for (int b = fast ? P.U : tid; b < P.U; b += kGemvThreads) {
-            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)b * 32);
-            const float4* wn = reinterpret_cast<const float4*>(a.norm_w + (int64_t)b * 32);
-            auto load = [&](int e) -> float4 {
-                float4 v = src[e];
-                if (norm) {
-                    const float4 w4 = wn[e];
-                    v.x = __fmul_rn(__fmul_rn(v.x, nscale), w4.x);
-                    v.y = __fmul_rn(__fmul_rn(v.y, nscale), w4.y);
-                    v.z = __fmul_rn(__fmul_rn(v.z, nscale), w4.z);
-                    v.w = __fmul_rn(__fmul_rn(v.w, nscale), w4.w);
-                }
-                return v;
-            };
-            int q[8];
-            float d;
-            uint16_t dh;
-            int qs;
-            quantize_block32(load, q, d, dh, qs);
-            xq[b] = make_int4(q[0], q[1], q[2], q[3]);
-            xq[P.U + b] = make_int4(q[4], q[5], q[6], q[7]);
-            xds[b] = make_int2(__float_as_int(d), qs);
-            if (a.xq_out != nullptr && blockIdx.x == 0) store_block_q8_0(a.xq_out + (int64_t)b * 34, dh, q);
-        }
-    } else {
         uint4* xh = reinterpret_cast<uint4*>(xr);
         for (int64_t i = tid; i < a.k / 8; i += kGemvThreads) {
             const float4* src = reinterpret_cast<const float4*>(a.x + i * 8);
@@ -685,5 +720,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         if (lane == 0 && best != 0ull) atomicMax(a.amax, best);
     }
 }
+
 
 }  // namespace b200

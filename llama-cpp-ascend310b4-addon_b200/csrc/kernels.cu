@@ -31,7 +31,7 @@ constexpr size_t kSmemBudget = 200 * 1024;
 
 int g_sms[kMaxDevices];
 std::mutex g_attr_mu;
-bool g_attr_done[kMaxDevices][4][2][5];
+bool g_attr_done[kMaxDevices][4][2][9];
 
 int current_device() {
     int d = 0;
@@ -79,7 +79,7 @@ int cuda_status(cudaError_t e) {
 template <int FMT, bool DEBUG, int UPL>
 int set_gemv_attr(int dev) {
     std::lock_guard<std::mutex> lk(g_attr_mu);
-    const int slot = UPL / 2;  // 0, 2, 4, 6, 8 -> 0..4
+    const int slot = UPL;
     if (dev < 0 || dev >= kMaxDevices || g_attr_done[dev][FMT][DEBUG ? 1 : 0][slot]) return B200_OK;
     cudaError_t e = cudaFuncSetAttribute(gemv_kernel<FMT, DEBUG, UPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
@@ -93,8 +93,11 @@ int set_gemv_attrs(int dev) {
     CR_((set_gemv_attr<FMT, DEBUG, 0>(dev)));
     CR_((set_gemv_attr<FMT, DEBUG, 2>(dev)));
     CR_((set_gemv_attr<FMT, DEBUG, 4>(dev)));
+    CR_((set_gemv_attr<FMT, DEBUG, 3>(dev)));
     if constexpr (FMT != FMT_Q8) {
+        CR_((set_gemv_attr<FMT, DEBUG, 5>(dev)));
         CR_((set_gemv_attr<FMT, DEBUG, 6>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 7>(dev)));
         CR_((set_gemv_attr<FMT, DEBUG, 8>(dev)));
     }
     return B200_OK;
@@ -157,9 +160,16 @@ template <int FMT, bool DEBUG>
 int launch_gemv_t(GemvArgs a, const GemvPlan& p, cudaStream_t st, bool pdl) {
     switch (p.full_upl) {
         case 2: return launch_gemv_u<FMT, DEBUG, 2>(a, p, st, pdl);
+        case 3: return launch_gemv_u<FMT, DEBUG, 3>(a, p, st, pdl);
         case 4: return launch_gemv_u<FMT, DEBUG, 4>(a, p, st, pdl);
+        case 5:
+            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 5>(a, p, st, pdl);
+            break;
         case 6:
             if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 6>(a, p, st, pdl);
+            break;
+        case 7:
+            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 7>(a, p, st, pdl);
             break;
         case 8:
             if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 8>(a, p, st, pdl);

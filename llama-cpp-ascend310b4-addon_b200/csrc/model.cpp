@@ -218,136 +218,103 @@ struct Dump {
     float* att = nullptr;  // device [n_layer * hq * D]
 };
 
-int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = nullptr) {
+// Argument blocks of the step's kernels (layer l).
+GemvArgs qkv_args(const b200_model* m, int l) {
     const b200_llama_config& c = m->c;
     const int D = c.head_dim;
-    const float theta_scale = powf(c.rope_theta, -2.0f / (float)D);
-    auto B = [&](int cls) { return prof ? prof->begin(s, cls) : B200_OK; };
-    auto E = [&]() { return prof ? prof->end(s) : B200_OK; };
-    // events and dump copies between the kernels would serialise them anyway
-    const bool pdl = m->pdl && !prof && !dump;
+    const Layer& Ly = m->L[l];
+    GemvArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.w = Ly.wqkv;
+    a.n = m->qkv_rows;
+    a.k = c.d_model;
+    a.x = m->x;
+    a.norm_w = Ly.attn_norm;
+    a.eps = c.rms_eps;
+    a.pro = PRO_RMSNORM;
+    a.epi = EPI_QKV;
+    a.y = m->q;
+    a.nq = m->hq * D;
+    a.nkv = m->hkv * D;
+    a.head_dim = D;
+    a.pos = &m->st->pos;
+    a.theta_scale = powf(c.rope_theta, -2.0f / (float)D);
+    a.kc = Ly.kc;
+    a.vc = Ly.vc;
+    return a;
+}
 
-    CR(B(0));
-    CR(b200i_embed(m->tok_embd, c.d_model, c.vocab, m->st, m->x, s));
-    CR(E());
-    const size_t qbytes = (size_t)m->hq * D * sizeof(float);
-    if (dump) CK(cudaMemcpyAsync(dump->x, m->x, c.d_model * sizeof(float), cudaMemcpyDeviceToDevice, s));
-    for (int l = 0; l < c.n_layer; ++l) {
-        const Layer& Ly = m->L[l];
-        GemvArgs a;
-        std::memset(&a, 0, sizeof(a));
-        a.w = Ly.wqkv;
-        a.n = m->qkv_rows;
-        a.k = c.d_model;
-        a.x = m->x;
-        a.norm_w = Ly.attn_norm;
-        a.eps = c.rms_eps;
-        a.pro = PRO_RMSNORM;
-        a.epi = EPI_QKV;
-        a.y = m->q;
-        a.nq = m->hq * D;
-        a.nkv = m->hkv * D;
-        a.head_dim = D;
-        a.pos = &m->st->pos;
-        a.theta_scale = theta_scale;
-        a.kc = Ly.kc;
-        a.vc = Ly.vc;
-        CR(B(1));
-        CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
-        CR(E());
+FaArgs fa_args(const b200_model* m, int l) {
+    const b200_llama_config& c = m->c;
+    const int D = c.head_dim;
+    const Layer& Ly = m->L[l];
+    FaArgs f;
+    std::memset(&f, 0, sizeof(f));
+    f.q = m->q;
+    f.k = reinterpret_cast<const uint8_t*>(Ly.kc);
+    f.v = reinterpret_cast<const uint8_t*>(Ly.vc);
+    f.mask = nullptr;
+    f.kv_len = &m->st->ctx;
+    f.out = m->att;
+    f.Hq = m->hq;
+    f.Hkv = m->hkv;
+    f.G = m->hq / m->hkv;
+    f.gchunks = m->fa.gchunks;
+    f.n_kv = c.kv_size;
+    f.n_splits = m->fa.n_splits;
+    f.chunks_per_split = m->fa.chunks_per_split;
+    f.k_nb1 = f.v_nb1 = (int64_t)m->hkv * D * 2;
+    f.k_nb2 = f.v_nb2 = (int64_t)D * 2;
+    f.scale = 1.0f / sqrtf((float)D);
+    uint8_t* ws = static_cast<uint8_t*>(m->fa_ws);
+    f.part_o = reinterpret_cast<float*>(ws + m->fa.off_o);
+    f.part_ml = reinterpret_cast<float*>(ws + m->fa.off_ml);
+    f.tickets = reinterpret_cast<unsigned int*>(ws + m->fa.off_tickets);
+    return f;
+}
 
-        FaArgs f;
-        std::memset(&f, 0, sizeof(f));
-        f.q = m->q;
-        f.k = reinterpret_cast<const uint8_t*>(Ly.kc);
-        f.v = reinterpret_cast<const uint8_t*>(Ly.vc);
-        f.mask = nullptr;
-        f.kv_len = &m->st->ctx;
-        f.out = m->att;
-        f.Hq = m->hq;
-        f.Hkv = m->hkv;
-        f.G = m->hq / m->hkv;
-        f.gchunks = m->fa.gchunks;
-        f.n_kv = c.kv_size;
-        f.n_splits = m->fa.n_splits;
-        f.chunks_per_split = m->fa.chunks_per_split;
-        f.k_nb1 = f.v_nb1 = (int64_t)m->hkv * D * 2;
-        f.k_nb2 = f.v_nb2 = (int64_t)D * 2;
-        f.scale = 1.0f / sqrtf((float)D);
-        uint8_t* ws = static_cast<uint8_t*>(m->fa_ws);
-        f.part_o = reinterpret_cast<float*>(ws + m->fa.off_o);
-        f.part_ml = reinterpret_cast<float*>(ws + m->fa.off_ml);
-        f.tickets = reinterpret_cast<unsigned int*>(ws + m->fa.off_tickets);
-        if (dump) CK(cudaMemcpyAsync(dump->q + (size_t)l * m->hq * D, m->q, qbytes, cudaMemcpyDeviceToDevice, s));
-        CR(B(2));
-        CR(b200i_fa(f, D, s, pdl));
-        CR(E());
-        if (dump)
-            CK(cudaMemcpyAsync(dump->att + (size_t)l * m->hq * D, m->att, qbytes, cudaMemcpyDeviceToDevice, s));
-
-        std::memset(&a, 0, sizeof(a));
-        a.w = Ly.wo;
-        a.n = c.d_model;
-        a.k = (int64_t)m->hq * D;
-        a.x = m->att;
-        a.pro = PRO_PLAIN;
-        a.res = m->x;
-        if (m->world == 1) {
-            a.epi = EPI_ADD;
-            a.y = m->x;
-        } else {
-            a.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
-            a.y = part_buf(m, 0);
-        }
-        CR(B(3));
-        CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
-        CR(E());
-        if (m->world > 1) {
-            CR(B(7));
-            CR(allreduce_sum(m, 0, 2 * l, s, pdl));
-            CR(E());
-        }
-
-        std::memset(&a, 0, sizeof(a));
-        a.w = Ly.wgu;
-        a.n = 2 * (int64_t)m->ff;
-        a.k = c.d_model;
-        a.x = m->x;
-        a.norm_w = Ly.ffn_norm;
-        a.eps = c.rms_eps;
-        a.pro = PRO_RMSNORM;
-        a.epi = EPI_SWIGLU;
-        a.y = m->h;
-        CR(B(4));
-        CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
-        CR(E());
-
-        std::memset(&a, 0, sizeof(a));
-        a.w = Ly.wdown;
-        a.n = c.d_model;
-        a.k = m->ff;
-        a.x = m->h;
-        a.pro = PRO_PLAIN;
-        a.res = m->x;
-        if (m->world == 1) {
-            a.epi = EPI_ADD;
-            a.y = m->x;
-        } else {
-            a.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
-            a.y = part_buf(m, 1);
-        }
-        CR(B(5));
-        CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
-        CR(E());
-        if (m->world > 1) {
-            CR(B(7));
-            CR(allreduce_sum(m, 1, 2 * l + 1, s, pdl));
-            CR(E());
-        }
-        if (dump)
-            CK(cudaMemcpyAsync(dump->x + (size_t)(l + 1) * c.d_model, m->x, c.d_model * sizeof(float),
-                               cudaMemcpyDeviceToDevice, s));
+// Row-split projection (O: which 0, down: which 1) adding into the residual
+// stream; with tensor parallelism rank 0 adds the residual into its partial
+// and the others store theirs, for the all-reduce.
+GemvArgs proj_args(b200_model* m, int l, int which) {
+    const b200_llama_config& c = m->c;
+    const Layer& Ly = m->L[l];
+    GemvArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.w = which == 0 ? Ly.wo : Ly.wdown;
+    a.n = c.d_model;
+    a.k = which == 0 ? (int64_t)m->hq * c.head_dim : m->ff;
+    a.x = which == 0 ? m->att : m->h;
+    a.pro = PRO_PLAIN;
+    a.res = m->x;
+    if (m->world == 1) {
+        a.epi = EPI_ADD;
+        a.y = m->x;
+    } else {
+        a.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
+        a.y = part_buf(m, which);
     }
+    return a;
+}
+
+GemvArgs gate_up_args(const b200_model* m, int l) {
+    const b200_llama_config& c = m->c;
+    GemvArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.w = m->L[l].wgu;
+    a.n = 2 * (int64_t)m->ff;
+    a.k = c.d_model;
+    a.x = m->x;
+    a.norm_w = m->L[l].ffn_norm;
+    a.eps = c.rms_eps;
+    a.pro = PRO_RMSNORM;
+    a.epi = EPI_SWIGLU;
+    a.y = m->h;
+    return a;
+}
+
+GemvArgs head_args(const b200_model* m) {
+    const b200_llama_config& c = m->c;
     GemvArgs a;
     std::memset(&a, 0, sizeof(a));
     a.w = m->lm_head;
@@ -361,8 +328,58 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
     a.y = m->logits;
     a.amax = &m->st->amax;
     a.row_offset = (int64_t)m->rank * m->voc;
+    return a;
+}
+
+int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = nullptr) {
+    const b200_llama_config& c = m->c;
+    const int D = c.head_dim;
+    auto B = [&](int cls) { return prof ? prof->begin(s, cls) : B200_OK; };
+    auto E = [&]() { return prof ? prof->end(s) : B200_OK; };
+    // events and dump copies between the kernels would serialise them anyway
+    const bool pdl = m->pdl && !prof && !dump;
+
+    CR(B(0));
+    CR(b200i_embed(m->tok_embd, c.d_model, c.vocab, m->st, m->x, s));
+    CR(E());
+
+    const size_t qbytes = (size_t)m->hq * D * sizeof(float);
+    if (dump) CK(cudaMemcpyAsync(dump->x, m->x, c.d_model * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    for (int l = 0; l < c.n_layer; ++l) {
+        CR(B(1));
+        CR(b200i_gemv(FMT_Q4, qkv_args(m, l), false, s, pdl));
+        CR(E());
+        if (dump) CK(cudaMemcpyAsync(dump->q + (size_t)l * m->hq * D, m->q, qbytes, cudaMemcpyDeviceToDevice, s));
+        CR(B(2));
+        CR(b200i_fa(fa_args(m, l), D, s, pdl));
+        CR(E());
+        if (dump)
+            CK(cudaMemcpyAsync(dump->att + (size_t)l * m->hq * D, m->att, qbytes, cudaMemcpyDeviceToDevice, s));
+        CR(B(3));
+        CR(b200i_gemv(FMT_Q4, proj_args(m, l, 0), false, s, pdl));
+        CR(E());
+        if (m->world > 1) {
+            CR(B(7));
+            CR(allreduce_sum(m, 0, 2 * l, s, pdl));
+            CR(E());
+        }
+        CR(B(4));
+        CR(b200i_gemv(FMT_Q4, gate_up_args(m, l), false, s, pdl));
+        CR(E());
+        CR(B(5));
+        CR(b200i_gemv(FMT_Q4, proj_args(m, l, 1), false, s, pdl));
+        CR(E());
+        if (m->world > 1) {
+            CR(B(7));
+            CR(allreduce_sum(m, 1, 2 * l + 1, s, pdl));
+            CR(E());
+        }
+        if (dump)
+            CK(cudaMemcpyAsync(dump->x + (size_t)(l + 1) * c.d_model, m->x, c.d_model * sizeof(float),
+                               cudaMemcpyDeviceToDevice, s));
+    }
     CR(B(6));
-    CR(b200i_gemv(FMT_Q4, a, false, s, pdl));
+    CR(b200i_gemv(FMT_Q4, head_args(m), false, s, pdl));
     CR(E());
     if (m->world > 1) {
         CR(B(7));
