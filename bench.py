@@ -88,9 +88,22 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def mark(self):
+        """Start of the timed region: later readings are the region's."""
+        self.first = len(self.lines)
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.lines = self.lines[getattr(self, "first", 0):]
+        if not self.lines:
+            # region shorter than the sampling period: one reading right at its end
+            try:
+                r = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                    "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=10)
+                self.lines.extend(x.strip() for x in r.stdout.splitlines() if x.strip())
+            except Exception:
+                pass
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -240,13 +253,14 @@ def run_ours(args):
 
     # ---- device-resident steps (graph replay, token fed back on the GPU)
     m.set_state(128000, N_PREFILL, advance=True)
+    clocks = ClockSampler(local)
+    clocks.start()  # running (under load) before the timed region starts
     for _ in range(args.warmup):
         m.launch()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
+    clocks.mark()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
