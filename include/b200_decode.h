@@ -151,6 +151,34 @@ int b200_fa_decode_static_scratch(const float *q, const void *k, const void *v, 
                                   int n_kv, int64_t k_nb1, int64_t k_nb2, int64_t v_nb1, int64_t v_nb2, float scale,
                                   b200_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Neighbour ops of the decode step, for a backend that runs the graph op by
+ * op (the whole-model driver fuses them into the GEMVs).  The reference
+ * patches these for the 310B: RMS_NORM decomposed into mul/mean/add/sqrt/div
+ * (patch:1133-1170) and enabled in supports_op (patch:1942-1951), SET_ROWS
+ * through IndexPut (patch:1179-1184), ROPE through its fallback
+ * (patch:1360-1363).  Out-of-range row indices are skipped and set
+ * B200_DEVSTATUS_BOUNDS.
+ *   rms_norm : rows x n f32; y = x / sqrt(mean(x^2) + eps) (sum in double), then
+ *              * w when w != NULL (RMS_NORM followed by MUL)
+ *   rope_norm: x, y f32 [n_tokens][n_heads][head_dim]; pos int32 [n_tokens]
+ *              (ggml ROPE, mode 0: adjacent pairs)
+ *   set_rows : src f32 [nrows][n] -> f16 rows idx[r] of dst (byte stride)
+ *   get_rows : Q4_0 table [vocab][n] -> dst f32 [nidx][n]
+ *   swiglu   : y = g / (1 + exp(-g)) * u;  add: y = a + b
+ *   argmax   : out[0] = index of the first maximum of x[n] */
+int b200_rms_norm_f32(const float *x, const float *w, float *y, int64_t n, int64_t rows, float eps,
+                      b200_stream_t stream);
+int b200_rope_norm_f32(const float *x, float *y, const int32_t *pos, int64_t n_tokens, int n_heads, int head_dim,
+                       float freq_base, b200_stream_t stream);
+int b200_set_rows_f16(const float *src, const int64_t *rows_idx, void *dst, int64_t n, int64_t nrows,
+                      int64_t dst_row_stride, int64_t dst_rows, b200_stream_t stream);
+int b200_get_rows_q4_0(const void *table, const int32_t *idx, float *dst, int64_t n, int64_t nidx, int64_t vocab,
+                       b200_stream_t stream);
+int b200_swiglu_f32(const float *g, const float *u, float *y, int64_t n, b200_stream_t stream);
+int b200_add_f32(const float *a, const float *b, float *y, int64_t n, b200_stream_t stream);
+int b200_argmax_f32(const float *x, int64_t n, int32_t *out, b200_stream_t stream);
+
 /* Host helper mirroring llama-graph.cpp set_input_kv_lengths_impl
  * (patch:2900-2916): out[r] = 1 + index of the last finite entry of mask row
  * r (at least 1).  mask f16 host array [n_rows][n_kv]. */

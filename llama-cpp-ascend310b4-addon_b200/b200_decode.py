@@ -93,6 +93,13 @@ def _declare(L):
             [P, P, P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, I64, I64, I64, I64, C.c_float, P],
         ),
         "b200_kv_lengths_from_mask_f16": (C.c_int, [P, I64, I64, P]),
+        "b200_rms_norm_f32": (C.c_int, [P, P, P, I64, I64, C.c_float, P]),
+        "b200_rope_norm_f32": (C.c_int, [P, P, P, I64, C.c_int, C.c_int, C.c_float, P]),
+        "b200_set_rows_f16": (C.c_int, [P, P, P, I64, I64, I64, I64, P]),
+        "b200_get_rows_q4_0": (C.c_int, [P, P, P, I64, I64, I64, P]),
+        "b200_swiglu_f32": (C.c_int, [P, P, P, I64, P]),
+        "b200_add_f32": (C.c_int, [P, P, P, I64, P]),
+        "b200_argmax_f32": (C.c_int, [P, I64, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -280,6 +287,71 @@ def flash_attn_ext_static_scratch(q, k, v, mask=None, scale: float = 1.0, kv_len
         k.stride(0) * es, k.stride(1) * es, v.stride(0) * es, v.stride(1) * es, float(scale), _stream(q.device),
     )
     _check(rc, "flash_attn_ext_static_scratch")
+    return out
+
+
+# ------------------------------------------------------------ neighbour ops
+# ggml's RMS_NORM (+ MUL), ROPE (NORM mode), SET_ROWS, GET_ROWS, SWIGLU, ADD
+# and ARGMAX for a backend that runs the decode graph op by op.
+
+
+def rms_norm(x, eps: float, w=None, out=None):
+    """x f32 [rows, n] (or [n]); y = x / sqrt(mean(x^2) + eps) * w."""
+    torch = _torch()
+    x = x.contiguous()
+    n = x.shape[-1]
+    rows = x.numel() // n
+    out = torch.empty_like(x) if out is None else out
+    _check(lib().b200_rms_norm_f32(_ptr(x), _ptr(w), _ptr(out), n, rows, float(eps), _stream(x.device)), "rms_norm")
+    return out
+
+
+def rope_norm(x, pos, freq_base: float, out=None):
+    """x f32 [n_tokens, n_heads, head_dim]; pos int32 [n_tokens] on the device."""
+    torch = _torch()
+    x = x.contiguous()
+    n_tokens, n_heads, head_dim = x.shape
+    out = torch.empty_like(x) if out is None else out
+    _check(lib().b200_rope_norm_f32(_ptr(x), _ptr(out), _ptr(pos), n_tokens, n_heads, head_dim, float(freq_base),
+                                    _stream(x.device)), "rope_norm")
+    return out
+
+
+def set_rows_f16(src, idx, dst):
+    """dst[idx[r], :n] = f16(src[r]); dst f16 [rows, >= n] (row-strided view), idx int64."""
+    nrows, n = src.shape
+    _check(lib().b200_set_rows_f16(_ptr(src.contiguous()), _ptr(idx), _ptr(dst), n, nrows, dst.stride(0) * 2,
+                                   dst.shape[0], _stream(src.device)), "set_rows_f16")
+    return dst
+
+
+def get_rows_q4_0(table, idx, vocab: int, n: int, out=None):
+    """table: Q4_0 blocks [vocab, n/32 * 18] (ggml layout); idx int32 [nidx] -> f32 [nidx, n]."""
+    torch = _torch()
+    out = torch.empty((idx.numel(), n), dtype=torch.float32, device=idx.device) if out is None else out
+    _check(lib().b200_get_rows_q4_0(_ptr(table), _ptr(idx), _ptr(out), n, idx.numel(), vocab, _stream(idx.device)),
+           "get_rows_q4_0")
+    return out
+
+
+def swiglu(g, u, out=None):
+    torch = _torch()
+    out = torch.empty_like(g) if out is None else out
+    _check(lib().b200_swiglu_f32(_ptr(g), _ptr(u), _ptr(out), g.numel(), _stream(g.device)), "swiglu")
+    return out
+
+
+def add(a, b, out=None):
+    torch = _torch()
+    out = torch.empty_like(a) if out is None else out
+    _check(lib().b200_add_f32(_ptr(a), _ptr(b), _ptr(out), a.numel(), _stream(a.device)), "add")
+    return out
+
+
+def argmax(x):
+    torch = _torch()
+    out = torch.empty(1, dtype=torch.int32, device=x.device)
+    _check(lib().b200_argmax_f32(_ptr(x), x.numel(), _ptr(out), _stream(x.device)), "argmax")
     return out
 
 

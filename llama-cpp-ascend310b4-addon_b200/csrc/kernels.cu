@@ -21,6 +21,7 @@
 #include "gemv.cuh"
 #include "internal.h"
 #include "model_ops.cuh"
+#include "ops.cuh"
 
 using namespace b200;
 
@@ -592,6 +593,63 @@ int b200_gemv_block_dots(int type, const void* w, const float* x, int32_t* dots,
     a.k = k;
     if (!w || !x || !aligned16(w) || !aligned16(x)) return B200_EINVAL;
     return b200i_gemv(type == B200_TYPE_Q4_0 ? FMT_Q4 : FMT_Q8, a, true, (cudaStream_t)stream);
+}
+
+// ---- neighbour ops (ops.cuh) ----
+
+int b200_rms_norm_f32(const float* x, const float* w, float* y, int64_t n, int64_t rows, float eps,
+                      b200_stream_t stream) {
+    if (!x || !y || n <= 0 || rows <= 0 || rows > INT32_MAX) return B200_EINVAL;
+    rms_norm_kernel<<<(unsigned)rows, kOpThreads, 0, (cudaStream_t)stream>>>(x, w, y, n, eps);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_rope_norm_f32(const float* x, float* y, const int32_t* pos, int64_t n_tokens, int n_heads, int head_dim,
+                       float freq_base, b200_stream_t stream) {
+    if (!x || !y || !pos || n_tokens <= 0 || n_heads <= 0 || head_dim <= 0 || (head_dim & 1)) return B200_EINVAL;
+    const int64_t total = n_tokens * n_heads * (head_dim / 2);
+    const float theta_scale = powf(freq_base, -2.0f / (float)head_dim);
+    rope_norm_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, y, pos, n_tokens, n_heads,
+                                                                                       head_dim, theta_scale);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_set_rows_f16(const float* src, const int64_t* rows_idx, void* dst, int64_t n, int64_t nrows,
+                      int64_t dst_row_stride, int64_t dst_rows, b200_stream_t stream) {
+    if (!src || !rows_idx || !dst || n <= 0 || nrows <= 0 || dst_rows <= 0 || dst_row_stride < 2 * n ||
+        (dst_row_stride & 1) || (reinterpret_cast<uintptr_t>(dst) & 1))
+        return B200_EINVAL;
+    const int64_t total = n * nrows;
+    set_rows_f16_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        src, rows_idx, static_cast<uint8_t*>(dst), n, nrows, dst_row_stride, dst_rows);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_get_rows_q4_0(const void* table, const int32_t* idx, float* dst, int64_t n, int64_t nidx, int64_t vocab,
+                       b200_stream_t stream) {
+    if (!table || !idx || !dst || n <= 0 || (n % 32) || nidx <= 0 || vocab <= 0) return B200_EINVAL;
+    const int64_t total = n * nidx;
+    get_rows_q4_0_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        static_cast<const uint8_t*>(table), idx, dst, n, nidx, vocab);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_swiglu_f32(const float* g, const float* u, float* y, int64_t n, b200_stream_t stream) {
+    if (!g || !u || !y || n <= 0) return B200_EINVAL;
+    swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(g, u, y, n);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_add_f32(const float* a, const float* b, float* y, int64_t n, b200_stream_t stream) {
+    if (!a || !b || !y || n <= 0) return B200_EINVAL;
+    add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a, b, y, n);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_argmax_f32(const float* x, int64_t n, int32_t* out, b200_stream_t stream) {
+    if (!x || !out || n <= 0 || n > INT32_MAX) return B200_EINVAL;
+    argmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, out);
+    return cuda_status(cudaGetLastError());
 }
 
 size_t b200_fa_workspace_size(int head_dim, int n_head, int n_head_kv, int n_kv) {

@@ -75,6 +75,14 @@ def test_argument_validation_without_device():
     assert L.b200_quantize_q8_0(None, None, 32, None) == B.EINVAL
     v = C.c_uint(0)
     assert L.b200_device_status(None, 0) == B.EINVAL
+    # neighbour ops: null pointers and bad shapes are refused before any launch
+    assert L.b200_rms_norm_f32(None, None, None, 8, 1, 1e-5, None) == B.EINVAL
+    assert L.b200_rope_norm_f32(None, None, None, 1, 8, 127, 1e4, None) == B.EINVAL
+    assert L.b200_set_rows_f16(None, None, None, 8, 1, 16, 4, None) == B.EINVAL
+    assert L.b200_get_rows_q4_0(None, None, None, 48, 1, 4, None) == B.EINVAL
+    assert L.b200_swiglu_f32(None, None, None, 8, None) == B.EINVAL
+    assert L.b200_add_f32(None, None, None, 8, None) == B.EINVAL
+    assert L.b200_argmax_f32(None, 8, None, None) == B.EINVAL
 
 
 def test_kv_lengths_host_helper_matches_oracle():
