@@ -175,9 +175,34 @@ int b200_set_rows_f16(const float *src, const int64_t *rows_idx, void *dst, int6
                       int64_t dst_row_stride, int64_t dst_rows, b200_stream_t stream);
 int b200_get_rows_q4_0(const void *table, const int32_t *idx, float *dst, int64_t n, int64_t nidx, int64_t vocab,
                        b200_stream_t stream);
+/* GET_ROWS from the packed Q4_0 copy (b200_repack output): a tied token
+ * embedding / output matrix then needs one device copy, where the reference
+ * keeps an ND and an NZ copy (patch:1451-1468). */
+int b200_get_rows_q4_0_packed(const void *table_packed, const int32_t *idx, float *dst, int64_t n, int64_t nidx,
+                              int64_t vocab, b200_stream_t stream);
 int b200_swiglu_f32(const float *g, const float *u, float *y, int64_t n, b200_stream_t stream);
 int b200_add_f32(const float *a, const float *b, float *y, int64_t n, b200_stream_t stream);
 int b200_argmax_f32(const float *x, int64_t n, int32_t *out, b200_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Weight upload in chunks.  Replaces the reference's TensorSetTracker and the
+ * NZ branch of set_tensor (patch:1745-1807): the model loader may call
+ * set_tensor for a tensor in pieces and from several threads, and the layout
+ * transform can only run once every byte has arrived.
+ *   begin: one ggml weight (type, n rows of k) whose packed copy is dst_packed
+ *          (b200_packed_size bytes, device); allocates a device staging buffer
+ *          of the ggml size on the current device.
+ *   write: bytes [offset, offset + size) of the ggml-layout tensor from host
+ *          memory; returns once the host memory has been read.  Thread safe.
+ *          Covered ranges are tracked exactly (repeats and overlaps count
+ *          once); the write that completes the tensor repacks it into
+ *          dst_packed and returns with *complete = 1 once that is done.
+ *   end:   releases the staging buffer; B200_ESTATE if the tensor never
+ *          became complete. */
+typedef struct b200_upload b200_upload;
+int b200_upload_begin(int type, int64_t n, int64_t k, void *dst_packed, b200_upload **out);
+int b200_upload_write(b200_upload *u, size_t offset, const void *host, size_t size, int *complete);
+int b200_upload_end(b200_upload *u);
 
 /* Host helper mirroring llama-graph.cpp set_input_kv_lengths_impl
  * (patch:2900-2916): out[r] = 1 + index of the last finite entry of mask row

@@ -97,6 +97,10 @@ def _declare(L):
         "b200_rope_norm_f32": (C.c_int, [P, P, P, I64, C.c_int, C.c_int, C.c_float, P]),
         "b200_set_rows_f16": (C.c_int, [P, P, P, I64, I64, I64, I64, P]),
         "b200_get_rows_q4_0": (C.c_int, [P, P, P, I64, I64, I64, P]),
+        "b200_get_rows_q4_0_packed": (C.c_int, [P, P, P, I64, I64, I64, P]),
+        "b200_upload_begin": (C.c_int, [C.c_int, I64, I64, P, C.POINTER(P)]),
+        "b200_upload_write": (C.c_int, [P, C.c_size_t, P, C.c_size_t, C.POINTER(C.c_int)]),
+        "b200_upload_end": (C.c_int, [P]),
         "b200_swiglu_f32": (C.c_int, [P, P, P, I64, P]),
         "b200_add_f32": (C.c_int, [P, P, P, I64, P]),
         "b200_argmax_f32": (C.c_int, [P, I64, P, P]),
@@ -332,6 +336,44 @@ def get_rows_q4_0(table, idx, vocab: int, n: int, out=None):
     _check(lib().b200_get_rows_q4_0(_ptr(table), _ptr(idx), _ptr(out), n, idx.numel(), vocab, _stream(idx.device)),
            "get_rows_q4_0")
     return out
+
+
+def get_rows_q4_0_packed(w: "PackedWeight", idx, out=None):
+    """GET_ROWS from a packed Q4_0 weight (rows of w.k elements) -> f32 [nidx, w.k]."""
+    torch = _torch()
+    out = torch.empty((idx.numel(), w.k), dtype=torch.float32, device=idx.device) if out is None else out
+    _check(lib().b200_get_rows_q4_0_packed(_ptr(w.data), _ptr(idx), _ptr(out), w.k, idx.numel(), w.n,
+                                           _stream(idx.device)), "get_rows_q4_0_packed")
+    return out
+
+
+class Upload:
+    """set_tensor-style upload of one ggml weight into a packed copy:
+    write(offset, host_bytes) in any order, from any thread; complete once
+    every byte has arrived (the repack then has run)."""
+
+    def __init__(self, wtype: int, n: int, k: int, device=None):
+        torch = _torch()
+        self.w = PackedWeight(wtype, n, k, torch.empty(packed_size(wtype, n, k), dtype=torch.uint8,
+                                                       device=device or "cuda"))
+        self.h = C.c_void_p()
+        _check(lib().b200_upload_begin(wtype, n, k, _ptr(self.w.data), C.byref(self.h)), "b200_upload_begin")
+        self.complete = False
+
+    def write(self, offset: int, data: np.ndarray) -> bool:
+        data = np.ascontiguousarray(data).view(np.uint8)
+        done = C.c_int(0)
+        _check(lib().b200_upload_write(self.h, offset, data.ctypes.data_as(C.c_void_p), data.nbytes, C.byref(done)),
+               "b200_upload_write")
+        self.complete = bool(done.value)
+        return self.complete
+
+    def close(self) -> int:
+        if self.h:
+            rc = lib().b200_upload_end(self.h)
+            self.h = None
+            return rc
+        return OK
 
 
 def swiglu(g, u, out=None):

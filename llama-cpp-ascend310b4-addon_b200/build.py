@@ -25,6 +25,7 @@ SOURCES = [
     "kernels.cu",
     "host.cpp",
     "model.cpp",
+    "upload.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

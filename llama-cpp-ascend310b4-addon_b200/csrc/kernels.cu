@@ -634,6 +634,17 @@ int b200_get_rows_q4_0(const void* table, const int32_t* idx, float* dst, int64_
     return cuda_status(cudaGetLastError());
 }
 
+int b200_get_rows_q4_0_packed(const void* table_packed, const int32_t* idx, float* dst, int64_t n, int64_t nidx,
+                              int64_t vocab, b200_stream_t stream) {
+    if (!table_packed || !idx || !dst || n <= 0 || (n % 32) || nidx <= 0 || vocab <= 0) return B200_EINVAL;
+    const int64_t rs = b200_packed_row_stride(B200_TYPE_Q4_0, vocab, n);
+    if (rs <= 0) return B200_EUNSUPPORTED;
+    const int64_t total = n * nidx;
+    get_rows_q4_0_packed_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        static_cast<const uint8_t*>(table_packed), idx, dst, n, nidx, vocab, rs);
+    return cuda_status(cudaGetLastError());
+}
+
 int b200_swiglu_f32(const float* g, const float* u, float* y, int64_t n, b200_stream_t stream) {
     if (!g || !u || !y || n <= 0) return B200_EINVAL;
     swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(g, u, y, n);

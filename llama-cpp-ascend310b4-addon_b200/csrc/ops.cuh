@@ -101,6 +101,28 @@ __global__ void get_rows_q4_0_kernel(const uint8_t* table, const int32_t* idx, f
     dst[i] = __fmul_rn((float)(q - 8), d);
 }
 
+// GET_ROWS from the packed Q4_0 layout (the table is also the lm_head's
+// GEMV operand, so a tied embedding needs one copy): row r at r * rs,
+// nibbles qs[U][16] then the scales d[U].
+__global__ void get_rows_q4_0_packed_kernel(const uint8_t* table, const int32_t* idx, float* dst, int64_t n,
+                                            int64_t nidx, int64_t vocab, int64_t rs) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * nidx) return;
+    const int64_t r = i / n, c = i - r * n;
+    const int64_t row = idx[r];
+    if (row < 0 || row >= vocab) {
+        if (c == 0) record_status(B200_DEVSTATUS_BOUNDS);
+        dst[i] = 0.f;
+        return;
+    }
+    const int64_t U = n / 32, b = c / 32;
+    const uint8_t* base = table + row * rs;
+    const float d = h2f((uint16_t)(base[16 * U + 2 * b] | (base[16 * U + 2 * b + 1] << 8)));
+    const int j = (int)(c & 31);
+    const int q = j < 16 ? (base[16 * b + j] & 0x0f) : (base[16 * b + j - 16] >> 4);
+    dst[i] = __fmul_rn((float)(q - 8), d);
+}
+
 __global__ void swiglu_kernel(const float* g, const float* u, float* y, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;

@@ -83,6 +83,11 @@ def test_argument_validation_without_device():
     assert L.b200_swiglu_f32(None, None, None, 8, None) == B.EINVAL
     assert L.b200_add_f32(None, None, None, 8, None) == B.EINVAL
     assert L.b200_argmax_f32(None, 8, None, None) == B.EINVAL
+    assert L.b200_get_rows_q4_0_packed(None, None, None, 64, 1, 4, None) == B.EINVAL
+    h = C.c_void_p()
+    assert L.b200_upload_begin(2, 4, 64, None, C.byref(h)) == B.EINVAL
+    assert L.b200_upload_write(None, 0, None, 16, None) == B.EINVAL
+    assert L.b200_upload_end(None) == B.EINVAL
 
 
 def test_kv_lengths_host_helper_matches_oracle():
