@@ -41,6 +41,9 @@ typedef struct CUstream_st *b200_stream_t;
 #define B200_TYPE_F16 1
 #define B200_TYPE_Q4_0 2
 #define B200_TYPE_Q8_0 8
+/* This library's int8 layout for the reference's A8W8 scheme (per-row weight
+ * scale, per-token activation scale); not a ggml type id. */
+#define B200_TYPE_A8W8 100
 
 /* Q4_0 GEMV arithmetic. */
 #define B200_Q4_MODE_GGML 0  /* ggml-cpu semantics: x -> Q8_0 blocks, integer block dots */
@@ -89,6 +92,20 @@ int b200_gemv_q4_0(const void *w_packed, const float *x, float *y, int64_t n, in
                    b200_stream_t stream);
 int b200_gemv_q8_0_q8_0(const void *w_packed, const float *x, float *y, int64_t n, int64_t k,
                         b200_stream_t stream);
+
+/* The reference add-on's own A8W8 scheme (per-output-column int8 weights,
+ * per-token int8 activation, int32 accumulation), as opposed to ggml's
+ * Q8_0 x Q8_0 above.
+ * b200_a8w8_transform replaces ggml_backend_cann_transform_f16_a8w8
+ * (patch:1674-1695): w_f16 holds the ggml F16 weight (n rows of k) on the
+ * device; dst (b200_packed_size(B200_TYPE_A8W8, n, k) bytes) receives per
+ * row s = max(amax / 127, 1e-8) as f16 and q = clamp(roundf(w / s), +-127).
+ * b200_gemv_a8w8 replaces the dispatch chain cast -> W8a8QuantizeCustom ->
+ * MatmulW8a8I32Custom -> W8a8DequantCustom -> cast (patch:1223-1282) with one
+ * launch: x f32 [k] -> f16 -> int8 with one scale amax / 127 (round half to
+ * even), exact int32 dot per row, y[r] = f16(acc * s_x * s_w[r]) as f32. */
+int b200_a8w8_transform(const void *w_f16, void *dst, int64_t n, int64_t k, b200_stream_t stream);
+int b200_gemv_a8w8(const void *w_packed, const float *x, float *y, int64_t n, int64_t k, b200_stream_t stream);
 
 /* Exactness exports.  b200_quantize_q8_0 runs the activation quantiser that
  * the Q4_0/Q8_0 GEMVs fuse (replaces W8a8QuantizeCustom,

@@ -27,6 +27,7 @@ TYPE_F32 = 0
 TYPE_F16 = 1
 TYPE_Q4_0 = 2
 TYPE_Q8_0 = 8
+TYPE_A8W8 = 100  # this library's int8 layout for the reference's A8W8 scheme
 Q4_MODE_GGML = 0
 Q4_MODE_W4A16 = 1
 
@@ -81,6 +82,8 @@ def _declare(L):
         "b200_gemv_f16": (C.c_int, [P, P, P, I64, I64, P]),
         "b200_gemv_q4_0": (C.c_int, [P, P, P, I64, I64, C.c_int, P]),
         "b200_gemv_q8_0_q8_0": (C.c_int, [P, P, P, I64, I64, P]),
+        "b200_a8w8_transform": (C.c_int, [P, P, I64, I64, P]),
+        "b200_gemv_a8w8": (C.c_int, [P, P, P, I64, I64, P]),
         "b200_quantize_q8_0": (C.c_int, [P, P, I64, P]),
         "b200_gemv_block_dots": (C.c_int, [C.c_int, P, P, P, P, I64, I64, P]),
         "b200_fa_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
@@ -167,6 +170,16 @@ def repack(wtype: int, src, n: int, k: int) -> PackedWeight:
     return PackedWeight(wtype, n, k, dst)
 
 
+def a8w8_transform(w_f16, n: int, k: int) -> PackedWeight:
+    """The reference's F16 -> A8W8 weight transform (per-row int8 + f16 scale)
+    of a ggml F16 weight [n, k] on the device."""
+    torch = _torch()
+    dst = torch.empty(packed_size(TYPE_A8W8, n, k), dtype=torch.uint8, device=w_f16.device)
+    _check(lib().b200_a8w8_transform(_ptr(w_f16.contiguous()), _ptr(dst), n, k, _stream(w_f16.device)),
+           "b200_a8w8_transform")
+    return PackedWeight(TYPE_A8W8, n, k, dst)
+
+
 def repack_interleave2(wtype: int, src_even, src_odd, n_each: int, k: int) -> PackedWeight:
     torch = _torch()
     size = packed_size(wtype, 2 * n_each, k)
@@ -194,6 +207,8 @@ def mul_mat(w: PackedWeight, x, y=None, q4_mode: int = Q4_MODE_GGML):
         rc = lib().b200_gemv_q4_0(_ptr(w.data), _ptr(x), _ptr(y), w.n, w.k, q4_mode, s)
     elif w.wtype == TYPE_Q8_0:
         rc = lib().b200_gemv_q8_0_q8_0(_ptr(w.data), _ptr(x), _ptr(y), w.n, w.k, s)
+    elif w.wtype == TYPE_A8W8:
+        rc = lib().b200_gemv_a8w8(_ptr(w.data), _ptr(x), _ptr(y), w.n, w.k, s)
     else:
         raise B200Unsupported(EUNSUPPORTED, f"mul_mat weight type {w.wtype}")
     _check(rc, "mul_mat")

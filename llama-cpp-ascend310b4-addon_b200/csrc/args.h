@@ -17,7 +17,7 @@
 
 namespace b200 {
 
-enum GemvFmt { FMT_F16 = 0, FMT_Q4 = 1, FMT_Q4W = 2, FMT_Q8 = 3 };
+enum GemvFmt { FMT_F16 = 0, FMT_Q4 = 1, FMT_Q4W = 2, FMT_Q8 = 3, FMT_A8 = 4 };
 enum GemvPro { PRO_PLAIN = 0, PRO_RMSNORM = 1 };
 enum GemvEpi { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_ARGMAX = 4 };
 
@@ -31,6 +31,8 @@ constexpr int64_t kGemvSmemBudget = 200 * 1024;
 //   Q4_0: qs[U][16 bytes], then d[U] f16 padded to 16     rs = 16U + pad16(2U)
 //   Q8_0: qs bytes 0..15 [U][16], bytes 16..31 [U][16],
 //         then d[U] f16 padded to 16                      rs = 32U + pad16(2U)
+//   A8W8: int8 bytes 0..15 [U][16], bytes 16..31 [U][16]  rs = 32U, then one f16
+//         scale per row after all n rows (padded to 16)
 // (U = K/8 units of 8 halves for F16, K/32 blocks for Q4_0/Q8_0.)  Planes
 // are split so that 32 lanes reading consecutive units issue conflict-free
 // 16-byte shared-memory loads, and every plane start is 16-byte aligned for
@@ -61,6 +63,7 @@ B200_HD inline int64_t pad16(int64_t v) { return (v + 15) & ~int64_t(15); }
 
 B200_HD inline int64_t gemv_stage_bytes_rpc1(int type, int kc) {
     if (type == B200_TYPE_F16) return 16 * (int64_t)kc;
+    if (type == B200_TYPE_A8W8) return 32 * (int64_t)kc;
     if (type == B200_TYPE_Q4_0) return 16 * (int64_t)kc + pad16(2 * (int64_t)kc);
     return 32 * (int64_t)kc + pad16(2 * (int64_t)kc);
 }
@@ -88,6 +91,12 @@ B200_HD inline bool make_plan(int type, int64_t n, int64_t k, GemvPlan* p) {
         p->U = (int)(k / 32);
         p->ub = 34;
         p->rs = 32 * (int64_t)p->U + pad16(2 * (int64_t)p->U);
+        kc_max = 128;
+    } else if (type == B200_TYPE_A8W8) {
+        if (k % 32 || k > 131072) return false;  // |int32 row sum| <= k * 127^2
+        p->U = (int)(k / 32);
+        p->ub = 32;
+        p->rs = 32 * (int64_t)p->U;  // int8 bytes 0..15 [U][16], bytes 16..31 [U][16]; row scales after all rows
         kc_max = 128;
     } else {
         return false;
@@ -135,7 +144,9 @@ B200_HD inline bool make_plan(int type, int64_t n, int64_t k, GemvPlan* p) {
     return true;
 }
 
-B200_HD inline int64_t gemv_packed_bytes(const GemvPlan& p) { return p.n * p.rs; }
+B200_HD inline int64_t gemv_packed_bytes(const GemvPlan& p) {
+    return p.n * p.rs + (p.type == B200_TYPE_A8W8 ? pad16(2 * p.n) : 0);
+}
 
 struct GemvArgs {
     const uint8_t* w;

@@ -20,6 +20,8 @@
 // dequantised nibbles and f16-rounded x.
 #pragma once
 
+#include <type_traits>
+
 #include "args.h"
 #include "common.cuh"
 
@@ -87,7 +89,8 @@ __device__ __forceinline__ float small_int_to_float(int v) {
 
 // Bytes of the activation region at the start of shared memory.
 B200_HD inline int64_t gemv_x_bytes(int fmt, const GemvPlan& p) {
-    if (fmt == FMT_Q4 || fmt == FMT_Q8) return pad16(40 * (int64_t)p.U);  // xq planes 2 x [U][16] + {d, sum}[U]
+    if (fmt == FMT_Q4 || fmt == FMT_Q8 || fmt == FMT_A8)
+        return pad16(40 * (int64_t)p.U);  // xq planes 2 x [U][16] + {d, sum}[U] (A8W8: the token scale)
     return pad16(2 * p.k);                                                // f16 x[K]
 }
 
@@ -145,17 +148,50 @@ __device__ __forceinline__ void epi_pair(const GemvArgs& a, int64_t n, float v0,
 
 template <int FMT>
 struct GemvTraits {
-    // units per lane per chunk row, upper bound (plan: kc <= 128 for Q8_0, 256 otherwise)
-    static constexpr int kMaxUpl = FMT == FMT_Q8 ? 4 : 8;
+    // units per lane per chunk row, upper bound (plan: kc <= 128 for Q8_0 / A8W8, 256 otherwise)
+    static constexpr int kMaxUpl = (FMT == FMT_Q8 || FMT == FMT_A8) ? 4 : 8;
+    // A8W8 rows are exact int32 sums (one scale per row and token); the
+    // other formats scale every block and accumulate in fp32
+    using Acc = std::conditional_t<FMT == FMT_A8, int, float>;
 };
+
+// Sum over the lanes of a warp, in the accumulator type.
+__device__ __forceinline__ float warp_sum_acc(float v) { return warp_sum(v); }
+__device__ __forceinline__ int warp_sum_acc(int v) { return __reduce_add_sync(0xffffffffu, v); }
+__device__ __forceinline__ int group_sum(int v, int width) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        if (o < width) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// A8W8 output: y = f16(f32(acc) * s_x * s_w) as an f32 (the reference's
+// W8a8DequantCustom writes f16, then the op casts back to f32).
+__device__ __forceinline__ float a8w8_dequant(int acc, float xs, uint16_t ws) {
+    return round_f16(__fmul_rn(__fmul_rn(__int2float_rn(acc), xs), h2f(ws)));
+}
 
 // Sum of one staged chunk row for this lane: units i = i0 + step*j (j < upl,
 // i < nu) of a row whose planes are `pw` units wide; `u0` is the row offset of
 // unit 0 of the chunk.  All loads of the row are issued before the math.
 template <int FMT, bool DEBUG>
-__device__ __forceinline__ float unit_dot(const uint8_t* row, int pw, int i, int u, const uint8_t* xr, int U,
-                                          int32_t* dots, int64_t nrow) {
-    if constexpr (FMT == FMT_F16) {
+__device__ __forceinline__ typename GemvTraits<FMT>::Acc unit_dot(const uint8_t* row, int pw, int i, int u,
+                                                                  const uint8_t* xr, int U, int32_t* dots,
+                                                                  int64_t nrow) {
+    if constexpr (FMT == FMT_A8) {
+        const int4 xa = reinterpret_cast<const int4*>(xr)[u];
+        const int4 xb = reinterpret_cast<const int4*>(xr + 16 * (int64_t)U)[u];
+        const uint4 lo = *reinterpret_cast<const uint4*>(row + 16 * i);
+        const uint4 hi = *reinterpret_cast<const uint4*>(row + 16 * pw + 16 * i);
+        int s0 = dp4a((int)lo.x, xa.x, 0), s1 = dp4a((int)hi.x, xb.x, 0);
+        s0 = dp4a((int)lo.y, xa.y, s0);
+        s1 = dp4a((int)hi.y, xb.y, s1);
+        s0 = dp4a((int)lo.z, xa.z, s0);
+        s1 = dp4a((int)hi.z, xb.z, s1);
+        s0 = dp4a((int)lo.w, xa.w, s0);
+        s1 = dp4a((int)hi.w, xb.w, s1);
+        return s0 + s1;
+    } else if constexpr (FMT == FMT_F16) {
         const uint4 wv = *reinterpret_cast<const uint4*>(row + 16 * i);
         const uint4 xv = *reinterpret_cast<const uint4*>(xr + 16 * u);
         const __half2* wh = reinterpret_cast<const __half2*>(&wv);
@@ -236,9 +272,10 @@ __device__ __forceinline__ float unit_dot(const uint8_t* row, int pw, int i, int
 
 // Generic chunk row (tails, short rows): units i = i0 + step*j, j < upl, i < nu.
 template <int FMT, bool DEBUG>
-__device__ __forceinline__ float chunk_row_dot(const uint8_t* row, int pw, int i0, int step, int upl, int nu, int u0,
-                                               const uint8_t* xr, int U, int32_t* dots, int64_t nrow) {
-    float acc = 0.f;
+__device__ __forceinline__ typename GemvTraits<FMT>::Acc chunk_row_dot(const uint8_t* row, int pw, int i0, int step,
+                                                                       int upl, int nu, int u0, const uint8_t* xr,
+                                                                       int U, int32_t* dots, int64_t nrow) {
+    typename GemvTraits<FMT>::Acc acc = 0;
     for (int j = 0; j < upl; ++j) {
         const int i = i0 + step * j;
         if (i < nu) acc += unit_dot<FMT, DEBUG>(row, pw, i, u0 + i, xr, U, dots, nrow);
@@ -249,8 +286,31 @@ __device__ __forceinline__ float chunk_row_dot(const uint8_t* row, int pw, int i
 // Full chunk on the one-row path: exactly UPL units per lane at compile-time
 // offsets (unit j of this lane is chunk unit lane + 32 j), no predicates.
 template <int FMT, bool DEBUG, int UPL>
-__device__ __forceinline__ float chunk_full_dot(const uint8_t* st, int kc, int lane, int u0, const uint8_t* xr, int U,
-                                                int32_t* dots, int64_t nrow) {
+__device__ __forceinline__ typename GemvTraits<FMT>::Acc chunk_full_dot(const uint8_t* st, int kc, int lane, int u0,
+                                                                        const uint8_t* xr, int U, int32_t* dots,
+                                                                        int64_t nrow) {
+    if constexpr (FMT == FMT_A8) {
+        const uint8_t* wl = st + 16 * lane;
+        const uint8_t* wh = st + 16 * kc + 16 * lane;
+        const int4* xpa = reinterpret_cast<const int4*>(xr) + u0 + lane;
+        const int4* xpb = reinterpret_cast<const int4*>(xr + 16 * (int64_t)U) + u0 + lane;
+        int s0 = 0, s1 = 0;
+#pragma unroll
+        for (int j = 0; j < UPL; ++j) {
+            const uint4 lo = *reinterpret_cast<const uint4*>(wl + 512 * j);
+            const uint4 hi = *reinterpret_cast<const uint4*>(wh + 512 * j);
+            const int4 xa = xpa[32 * j], xb = xpb[32 * j];
+            s0 = dp4a((int)lo.x, xa.x, s0);
+            s1 = dp4a((int)hi.x, xb.x, s1);
+            s0 = dp4a((int)lo.y, xa.y, s0);
+            s1 = dp4a((int)hi.y, xb.y, s1);
+            s0 = dp4a((int)lo.z, xa.z, s0);
+            s1 = dp4a((int)hi.z, xb.z, s1);
+            s0 = dp4a((int)lo.w, xa.w, s0);
+            s1 = dp4a((int)hi.w, xb.w, s1);
+        }
+        return s0 + s1;
+    }
     float acc = 0.f;
     if constexpr (FMT == FMT_Q4 || FMT == FMT_Q8) {
         const uint8_t* wq = st + 16 * lane;
@@ -457,6 +517,65 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
     __syncthreads();
 }
 
+// x -> the reference's per-token int8 activation (W8a8QuantizeCustom,
+// w8a8_quantize_custom_vector.cpp:35-64): x cast to f16, one scale
+// amax / 127 (amax at least 1.27e-6) kept as f16, q = rint(x * 127 / amax)
+// (round half to even).  Same planes as activation_q8; the token scale (the
+// f16 value as f32) goes where the per-block scales would be.  Ends with
+// __syncthreads.
+template <class AfterIssue>
+__device__ __forceinline__ void activation_a8(const GemvArgs& a, const GemvPlan& P, uint8_t* xr, float* red, int tid,
+                                              int lane, int warp, AfterIssue after_issue) {
+    constexpr int R = 8;
+    const int nu = P.U * 8;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    float4 xv[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const int u = tid + i * kGemvThreads;
+        if (u < nu) xv[i] = x4[u];
+    }
+    after_issue();
+    float amax = 0.f;
+    for (int base = 0; base < nu; base += R * kGemvThreads) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int u = base + tid + i * kGemvThreads;
+            if (u >= nu) continue;
+            const float4 v = base == 0 ? xv[i] : x4[u];
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(round_f16(v.x)), fabsf(round_f16(v.y))),
+                                     fmaxf(fabsf(round_f16(v.z)), fabsf(round_f16(v.w)))));
+        }
+    }
+    amax = warp_max(amax);
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+    amax = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGemvWarps; ++w) amax = fmaxf(amax, red[w]);
+    amax = fmaxf(amax, 0.00000127f);
+    const float inv = __fdiv_rn(127.0f, amax);
+    if (tid == 0) *reinterpret_cast<float*>(xr + 32 * (int64_t)P.U) = round_f16(__fdiv_rn(amax, 127.0f));
+    int* xw = reinterpret_cast<int*>(xr);
+    const int wd = lane & 7;
+    for (int base = 0; base < nu; base += R * kGemvThreads) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int u = base + tid + i * kGemvThreads;
+            if (u >= nu) continue;
+            const float4 v = base == 0 ? xv[i] : x4[u];
+            const int q0 = __float2int_rn(__fmul_rn(round_f16(v.x), inv));
+            const int q1 = __float2int_rn(__fmul_rn(round_f16(v.y), inv));
+            const int q2 = __float2int_rn(__fmul_rn(round_f16(v.z), inv));
+            const int q3 = __float2int_rn(__fmul_rn(round_f16(v.w), inv));
+            const int word = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) |
+                                   ((unsigned)(q2 & 0xff) << 16) | ((unsigned)(q3 & 0xff) << 24));
+            xw[(wd < 4 ? 0 : 4 * P.U) + 4 * (u >> 3) + (wd & 3)] = word;
+        }
+    }
+    __syncthreads();
+}
+
 // ------------------------------------------------------------ the kernel
 
 // UPL: units per lane of this plan's full chunks (P.full_upl), or 0 when the
@@ -548,6 +667,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
                 bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
                 bulk_g2s(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 16 * (int64_t)u0, b0, bar);
                 bulk_g2s(dst + 32 * P.kc, base + 32 * (int64_t)P.U + 2 * (int64_t)u0, b1, bar);
+            } else if constexpr (FMT == FMT_A8) {
+                mbar_arrive_expect_tx(bar, 2 * b0);
+                bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
+                bulk_g2s(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 16 * (int64_t)u0, b0, bar);
             } else {
                 const uint32_t b1 = (uint32_t)pad16(2 * nu);
                 mbar_arrive_expect_tx(bar, b0 + b1);
@@ -579,6 +702,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     const bool norm = a.pro == PRO_RMSNORM;
     if constexpr (FMT == FMT_Q4 || FMT == FMT_Q8) {
         activation_q8(a, P, xr, red, tid, lane, warp, [&] {
+            if (lane == 0)
+                for (int s = 1; s < S && s < nq; ++s) issue(s);
+        });
+    } else if constexpr (FMT == FMT_A8) {
+        activation_a8(a, P, xr, red, tid, lane, warp, [&] {
             if (lane == 0)
                 for (int s = 1; s < S && s < nq; ++s) issue(s);
         });
@@ -629,8 +757,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         for (int64_t r = tid; r < 2 * (cr1 - cr0); r += kGemvThreads) part0[r] = 0.f;
         __syncthreads();
     }
-    float acc = 0.f;
+    using Acc = typename GemvTraits<FMT>::Acc;
+    Acc acc = 0;
     unsigned long long best = 0ull;
+    // A8W8: the token scale (activation_a8) and the per-row weight scales
+    const float a8_xs = FMT == FMT_A8 ? *reinterpret_cast<const float*>(xr + 32 * (int64_t)P.U) : 0.f;
+    const uint16_t* a8_ws = reinterpret_cast<const uint16_t*>(a.w + P.n * P.rs);
+    Acc* pacc0 = reinterpret_cast<Acc*>(part0);
+    Acc* pacc1 = reinterpret_cast<Acc*>(part1);
     int s = 0;
     uint32_t parity = 0;
     int64_t crow = 0;                                             // rows consumed (offset from row_begin)
@@ -657,14 +791,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         if (P.rpc > 1) {
             const int64_t r0 = row_begin + crow;
             const int nr = (int)min((int64_t)P.rpc, P.n - r0);
-            float v = 0.f;
+            Acc v = 0;
             if (rr < nr)
                 v = chunk_row_dot<FMT, DEBUG>(st + (int64_t)rr * P.rs, P.U, li, P.tpr, P.upl, P.U, 0, xr, P.U,
                                               a.dots, r0 + rr);
             v = group_sum(v, P.tpr);
-            const float vn = __shfl_down_sync(0xffffffffu, v, P.tpr < 32 ? P.tpr : 0);
+            const Acc vn = __shfl_down_sync(0xffffffffu, v, P.tpr < 32 ? P.tpr : 0);
             if (li == 0 && rr < nr) {
-                if (pair) {
+                if constexpr (FMT == FMT_A8) {
+                    a.y[r0 + rr] = a8w8_dequant(v, a8_xs, a8_ws[r0 + rr]);
+                } else if (pair) {
                     if ((rr & 1) == 0) epi_pair(a, r0 + rr, v, vn);
                 } else {
                     epi_row(a, r0 + rr, v, best);
@@ -681,9 +817,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
                 acc += chunk_row_dot<FMT, DEBUG>(st, P.kc, lane, 32, P.upl, nu, u0, xr, P.U, a.dots, row);
             const bool row_done = ++cc == P.nchunk;
             if (row_done || q == nq - 1) {
-                const float v = warp_sum(acc);
-                acc = 0.f;
-                if (lane == 0) (first_part ? part0 : part1)[row - cr0] = v;
+                const Acc v = warp_sum_acc(acc);
+                acc = 0;
+                if (lane == 0) (first_part ? pacc0 : pacc1)[row - cr0] = v;
                 if (row_done) {
                     cc = 0;
                     ++crow;
@@ -704,7 +840,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     if (P.rpc == 1) {
         __syncthreads();  // all row partials of the CTA are in shared memory
         const int64_t nrows = cr1 - cr0;
-        if (pair) {
+        if constexpr (FMT == FMT_A8) {
+            for (int64_t r = tid; r < nrows; r += kGemvThreads)
+                a.y[cr0 + r] = a8w8_dequant(pacc0[r] + pacc1[r], a8_xs, a8_ws[cr0 + r]);
+        } else if (pair) {
             for (int64_t r = 2 * (int64_t)tid; r < nrows; r += 2 * kGemvThreads)
                 epi_pair(a, cr0 + r, part0[r] + part1[r], part0[r + 1] + part1[r + 1]);
         } else {

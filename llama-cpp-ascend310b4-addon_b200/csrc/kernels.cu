@@ -32,7 +32,7 @@ constexpr size_t kSmemBudget = 200 * 1024;
 
 int g_sms[kMaxDevices];
 std::mutex g_attr_mu;
-bool g_attr_done[kMaxDevices][4][2][9];
+bool g_attr_done[kMaxDevices][5][2][9];
 
 int current_device() {
     int d = 0;
@@ -95,7 +95,7 @@ int set_gemv_attrs(int dev) {
     CR_((set_gemv_attr<FMT, DEBUG, 2>(dev)));
     CR_((set_gemv_attr<FMT, DEBUG, 4>(dev)));
     CR_((set_gemv_attr<FMT, DEBUG, 3>(dev)));
-    if constexpr (FMT != FMT_Q8) {
+    if constexpr (FMT != FMT_Q8 && FMT != FMT_A8) {
         CR_((set_gemv_attr<FMT, DEBUG, 5>(dev)));
         CR_((set_gemv_attr<FMT, DEBUG, 6>(dev)));
         CR_((set_gemv_attr<FMT, DEBUG, 7>(dev)));
@@ -164,16 +164,16 @@ int launch_gemv_t(GemvArgs a, const GemvPlan& p, cudaStream_t st, bool pdl) {
         case 3: return launch_gemv_u<FMT, DEBUG, 3>(a, p, st, pdl);
         case 4: return launch_gemv_u<FMT, DEBUG, 4>(a, p, st, pdl);
         case 5:
-            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 5>(a, p, st, pdl);
+            if constexpr (FMT != FMT_Q8 && FMT != FMT_A8) return launch_gemv_u<FMT, DEBUG, 5>(a, p, st, pdl);
             break;
         case 6:
-            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 6>(a, p, st, pdl);
+            if constexpr (FMT != FMT_Q8 && FMT != FMT_A8) return launch_gemv_u<FMT, DEBUG, 6>(a, p, st, pdl);
             break;
         case 7:
-            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 7>(a, p, st, pdl);
+            if constexpr (FMT != FMT_Q8 && FMT != FMT_A8) return launch_gemv_u<FMT, DEBUG, 7>(a, p, st, pdl);
             break;
         case 8:
-            if constexpr (FMT != FMT_Q8) return launch_gemv_u<FMT, DEBUG, 8>(a, p, st, pdl);
+            if constexpr (FMT != FMT_Q8 && FMT != FMT_A8) return launch_gemv_u<FMT, DEBUG, 8>(a, p, st, pdl);
             break;
         default: break;
     }
@@ -236,7 +236,10 @@ __global__ void quantize_q8_0_kernel(const float* x, uint8_t* out, int64_t nb) {
 
 int gemv_common(int fmt, const void* w, const float* x, float* y, int64_t n, int64_t k, int32_t* dots,
                 cudaStream_t st) {
-    const int type = fmt == FMT_F16 ? B200_TYPE_F16 : (fmt == FMT_Q8 ? B200_TYPE_Q8_0 : B200_TYPE_Q4_0);
+    const int type = fmt == FMT_F16  ? B200_TYPE_F16
+                     : fmt == FMT_Q8 ? B200_TYPE_Q8_0
+                     : fmt == FMT_A8 ? B200_TYPE_A8W8
+                                     : B200_TYPE_Q4_0;
     GemvPlan p;
     if (!make_plan(type, n, k, &p)) return B200_EUNSUPPORTED;
     if (!w || !x || !y || !aligned16(w) || !aligned16(x)) return B200_EINVAL;
@@ -258,7 +261,10 @@ int gemv_common(int fmt, const void* w, const float* x, float* y, int64_t n, int
 // ------------------------------------------------------------------ internal
 
 int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st, bool pdl) {
-    const int type = fmt == FMT_F16 ? B200_TYPE_F16 : (fmt == FMT_Q8 ? B200_TYPE_Q8_0 : B200_TYPE_Q4_0);
+    const int type = fmt == FMT_F16  ? B200_TYPE_F16
+                     : fmt == FMT_Q8 ? B200_TYPE_Q8_0
+                     : fmt == FMT_A8 ? B200_TYPE_A8W8
+                                     : B200_TYPE_Q4_0;
     GemvPlan p;
     if (!make_plan(type, a.n, a.k, &p)) return B200_EUNSUPPORTED;
     if (debug) {
@@ -271,6 +277,7 @@ int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st, bool pdl) {
         case FMT_Q4: return launch_gemv_t<FMT_Q4, false>(a, p, st, pdl);
         case FMT_Q4W: return launch_gemv_t<FMT_Q4W, false>(a, p, st, pdl);
         case FMT_Q8: return launch_gemv_t<FMT_Q8, false>(a, p, st, pdl);
+        case FMT_A8: return launch_gemv_t<FMT_A8, false>(a, p, st, pdl);
         default: return B200_EINVAL;
     }
 }
@@ -443,6 +450,7 @@ int b200i_prepare_device() {
     CR_((set_gemv_attrs<FMT_Q4, false>(dev)));
     CR_((set_gemv_attrs<FMT_Q4W, false>(dev)));
     CR_((set_gemv_attrs<FMT_Q8, false>(dev)));
+    CR_((set_gemv_attrs<FMT_A8, false>(dev)));
     CR_((set_gemv_attrs<FMT_Q4, true>(dev)));
     CR_((set_gemv_attrs<FMT_Q8, true>(dev)));
     CR_(set_fa_attrs());
@@ -526,6 +534,35 @@ size_t b200_packed_size(int type, int64_t n, int64_t k) {
     return make_plan(type, n, k, &p) ? (size_t)gemv_packed_bytes(p) : 0;
 }
 
+// The reference's host transform ggml_backend_cann_transform_f16_a8w8
+// (patch:1674-1695) on the device: per weight row (an output column of the
+// ggml matmul) s = max(amax / 127, 1e-8) kept as f16, q = clamp(roundf(w / s),
+// +-127) with the f32 s.  One CTA per row; q into the two int8 planes of the
+// A8W8 layout, s after all rows.
+__global__ void __launch_bounds__(256) a8w8_transform_kernel(const uint16_t* w, uint8_t* dst, int64_t n, int64_t k) {
+    const int64_t r = blockIdx.x;
+    const uint16_t* wr = w + r * k;
+    float amax = 0.f;
+    for (int64_t i = threadIdx.x; i < k; i += 256) amax = fmaxf(amax, fabsf(h2f(wr[i])));
+    amax = warp_max(amax);
+    __shared__ float wm[8];
+    if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = 0.f;
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, wm[i]);
+    float scale = __fdiv_rn(amax, 127.0f);
+    if (scale < 1.0e-8f) scale = 1.0e-8f;
+    const int64_t U = k / 32;
+    uint8_t* row = dst + r * 32 * U;
+    for (int64_t i = threadIdx.x; i < k; i += 256) {
+        float q = roundf(__fdiv_rn(h2f(wr[i]), scale));
+        q = fminf(fmaxf(q, -127.0f), 127.0f);
+        const int64_t b = i / 32, j = i - b * 32;
+        row[(j < 16 ? 0 : 16 * U) + 16 * b + (j & 15)] = (uint8_t)(int8_t)q;
+    }
+    if (threadIdx.x == 0) reinterpret_cast<uint16_t*>(dst + n * 32 * U)[r] = f2h(scale);
+}
+
 static int repack_impl(int type, const void* s0, const void* s1, int interleave, void* dst, int64_t n,
                        int64_t k, cudaStream_t st) {
     GemvPlan p;
@@ -593,6 +630,22 @@ int b200_gemv_block_dots(int type, const void* w, const float* x, int32_t* dots,
     a.k = k;
     if (!w || !x || !aligned16(w) || !aligned16(x)) return B200_EINVAL;
     return b200i_gemv(type == B200_TYPE_Q4_0 ? FMT_Q4 : FMT_Q8, a, true, (cudaStream_t)stream);
+}
+
+int b200_a8w8_transform(const void* w_f16, void* dst, int64_t n, int64_t k, b200_stream_t stream) {
+    GemvPlan p;
+    if (!w_f16 || !dst || !aligned16(dst)) return B200_EINVAL;
+    if (!make_plan(B200_TYPE_A8W8, n, k, &p) || n > INT32_MAX) return B200_EUNSUPPORTED;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t tail = pad16(2 * n) - 2 * n;  // zero the scale plane's padding
+    if (tail) CR_(cuda_status(cudaMemsetAsync(static_cast<uint8_t*>(dst) + n * p.rs + 2 * n, 0, tail, st)));
+    a8w8_transform_kernel<<<(unsigned)n, 256, 0, st>>>(static_cast<const uint16_t*>(w_f16), static_cast<uint8_t*>(dst),
+                                                      n, k);
+    return cuda_status(cudaGetLastError());
+}
+
+int b200_gemv_a8w8(const void* w_packed, const float* x, float* y, int64_t n, int64_t k, b200_stream_t stream) {
+    return gemv_common(FMT_A8, w_packed, x, y, n, k, nullptr, (cudaStream_t)stream);
 }
 
 // ---- neighbour ops (ops.cuh) ----

@@ -35,7 +35,7 @@ def _torch():
 
 def _blocks(wtype, n, k):
     torch = _torch()
-    if wtype == B.TYPE_F16:
+    if wtype in (B.TYPE_F16, B.TYPE_A8W8):
         return (torch.randn(n, k, device="cuda") * 0.02).half()
     bb = B.BLOCK_BYTES[wtype]
     src = torch.randint(0, 255, (n, k // 32 * bb), dtype=torch.uint8, device="cuda")
@@ -53,6 +53,7 @@ GEMV = {
     "config3_q4_0": (B.TYPE_Q4_0, 1536, 8960, B.Q4_MODE_GGML),
     "config3_w4a16": (B.TYPE_Q4_0, 1536, 8960, B.Q4_MODE_W4A16),
     "config4_q8_0": (B.TYPE_Q8_0, 151936, 1536, 0),
+    "config4_a8w8": (B.TYPE_A8W8, 151936, 1536, 0),  # the reference's per-token / per-column int8 scheme
     "gateup": (B.TYPE_Q4_0, 57344, 8192, B.Q4_MODE_GGML),  # Llama-3-70B gate+up rows
     "down": (B.TYPE_Q4_0, 8192, 28672, B.Q4_MODE_GGML),
     "qkv": (B.TYPE_Q4_0, 10240, 8192, B.Q4_MODE_GGML),
@@ -69,6 +70,8 @@ ATTN = {
 
 
 def _row_bytes(wtype, k):
+    if wtype == B.TYPE_A8W8:
+        return k + 2  # int8 row + its f16 scale
     return 2 * k if wtype == B.TYPE_F16 else k // 32 * B.BLOCK_BYTES[wtype]
 
 
@@ -78,7 +81,10 @@ def gemv_case(name, reps_copies=None):
     nbytes = n * _row_bytes(wtype, k) + 4 * k + 4 * n
     copies = reps_copies or _copies(nbytes)
     src = _blocks(wtype, n, k)
-    ws = [B.repack(wtype, src, n, k) for _ in range(copies)]
+    if wtype == B.TYPE_A8W8:
+        ws = [B.a8w8_transform(src, n, k) for _ in range(copies)]
+    else:
+        ws = [B.repack(wtype, src, n, k) for _ in range(copies)]
     del src
     x = torch.randn(k, device="cuda")
     y = torch.empty(n, device="cuda")
