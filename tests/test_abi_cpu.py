@@ -53,6 +53,16 @@ def test_packed_size_layout(wtype, n, k):
     assert rs % 16 == 0
 
 
+@pytest.mark.parametrize("n,k", [(151936, 1536), (8960, 1536), (3, 32), (5, 96)])
+def test_packed_size_a8w8(n, k):
+    import b200_decode as B
+
+    # int8 rows of k bytes, then the n f16 row scales padded to 16 bytes
+    pad16 = lambda v: (v + 15) // 16 * 16
+    assert B.row_stride(B.TYPE_A8W8, n, k) == k
+    assert B.packed_size(B.TYPE_A8W8, n, k) == n * k + pad16(2 * n)
+
+
 def test_unsupported_shapes_report_zero():
     import b200_decode as B
 
@@ -88,6 +98,8 @@ def test_argument_validation_without_device():
     assert L.b200_upload_begin(2, 4, 64, None, C.byref(h)) == B.EINVAL
     assert L.b200_upload_write(None, 0, None, 16, None) == B.EINVAL
     assert L.b200_upload_end(None) == B.EINVAL
+    assert L.b200_a8w8_transform(None, None, 4, 64, None) == B.EINVAL
+    assert L.b200_gemv_a8w8(None, None, None, 4, 64, None) == B.EINVAL
 
 
 def test_kv_lengths_host_helper_matches_oracle():
