@@ -403,52 +403,106 @@ __device__ __forceinline__ typename GemvTraits<FMT>::Acc chunk_full_dot(const ui
 
 // ------------------------------------------------------------ activation
 
-// x -> Q8_0 activation planes in shared memory (optionally RMSNorm * w first),
-// quantize_row_q8_0_ref's rule on each 32-block.  Eight consecutive lanes
-// share a block, one float4 each, so every warp load is fully coalesced; the
-// block max and the sum of q are 8-lane shuffle reductions (order free, so the
-// bytes and scales equal a one-thread-per-block quantiser's).  `after_issue`
-// runs once the first loads are in flight (the caller issues its remaining
-// weight copies there).  Ends with __syncthreads.
+// R float4 units per lane, each an eighth of a 32-block: the 8 units of a
+// block sit in 8 consecutive lanes (lane & 7 = the unit's index in the
+// block), quantised with quantize_row_q8_0_ref's rule: d = amax / 127,
+// q = roundf(x / d) (x times the reciprocal, as ggml does).  The block max
+// and the sum of q are 8-lane shuffle reductions (order free).  The R units
+// are independent chains written phase by phase, so they interleave; all 32
+// lanes must execute this (full-warp shuffles).  Out: this lane's 4 bytes of
+// q packed in a word, and the block's f16 scale and sum of q (every lane of
+// the group).
+template <int R>
+__device__ __forceinline__ void q8_units(const float4 (&v)[R], int (&word)[R], uint16_t (&dh)[R], int (&qs)[R]) {
+    float amax[R], id[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i)
+        amax[i] = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < R; ++i) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o, 8));
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const float d = __fdiv_rn(amax[i], 127.0f);
+        id[i] = d != 0.f ? __frcp_rn(d) : 0.f;
+        dh[i] = f2h(d);
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const int q0 = round_half_away(__fmul_rn(v[i].x, id[i]));
+        const int q1 = round_half_away(__fmul_rn(v[i].y, id[i]));
+        const int q2 = round_half_away(__fmul_rn(v[i].z, id[i]));
+        const int q3 = round_half_away(__fmul_rn(v[i].w, id[i]));
+        qs[i] = q0 + q1 + q2 + q3;
+        word[i] = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) | ((unsigned)(q2 & 0xff) << 16) |
+                        ((unsigned)(q3 & 0xff) << 24));
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < R; ++i) qs[i] += __shfl_xor_sync(0xffffffffu, qs[i], o, 8);
+}
+
+__device__ __forceinline__ float4 norm_unit(float4 v, float4 w, float nscale) {
+    v.x = __fmul_rn(__fmul_rn(v.x, nscale), w.x);
+    v.y = __fmul_rn(__fmul_rn(v.y, nscale), w.y);
+    v.z = __fmul_rn(__fmul_rn(v.z, nscale), w.z);
+    v.w = __fmul_rn(__fmul_rn(v.w, nscale), w.w);
+    return v;
+}
+
+// x -> Q8_0 activation planes in shared memory (optionally RMSNorm * w first).
+// Eight consecutive lanes share a block, one float4 each, so every warp load
+// is fully coalesced.  A thread handles units tid + i T (T threads) in rounds
+// of R: the next round's loads are in flight while the current round is
+// quantised, every lane of every warp runs every round (loads clamped to the
+// last unit, stores only for real units).  The sum of squares runs over each
+// thread's units in increasing order.  `after_issue` runs once the first
+// loads are in flight (the caller issues its remaining weight copies there).
+// Ends with __syncthreads.
 template <class AfterIssue>
 __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan& P, uint8_t* xr, float* red, int tid,
                                               int lane, int warp, AfterIssue after_issue) {
-    constexpr int R = 8;  // float4 units per thread held in registers at once
+    constexpr int R = 4;
+    constexpr int RT = R * kGemvThreads;
     const bool norm = a.pro == PRO_RMSNORM;
     const int nu = P.U * 8;  // float4 units of x
+    const int rounds = (nu + RT - 1) / RT;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
     const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
     float4 xv[R], wv[R];
+    auto load = [&](int base) {
 #pragma unroll
-    for (int i = 0; i < R; ++i) {
-        const int u = tid + i * kGemvThreads;
-        if (u < nu) {
+        for (int i = 0; i < R; ++i) {
+            const int u = min(base + tid + i * kGemvThreads, nu - 1);
             xv[i] = x4[u];
             if (norm) wv[i] = w4[u];
         }
-    }
+    };
+    load(0);
     after_issue();
-    const bool resident = nu <= R * kGemvThreads;  // every unit of x is in registers
     float nscale = 1.f;
     if (norm) {
         float ss = 0.f;
-        if (resident) {
+        for (int r = 0; r < rounds; ++r) {
+            const int base = r * RT;
+            float4 t[R];
+            if (r == 0) {
+#pragma unroll
+                for (int i = 0; i < R; ++i) t[i] = xv[i];
+            } else {
+#pragma unroll
+                for (int i = 0; i < R; ++i) t[i] = x4[min(base + tid + i * kGemvThreads, nu - 1)];
+            }
 #pragma unroll
             for (int i = 0; i < R; ++i)
-                if (tid + i * kGemvThreads < nu) {
-                    ss = fmaf(xv[i].x, xv[i].x, ss);
-                    ss = fmaf(xv[i].y, xv[i].y, ss);
-                    ss = fmaf(xv[i].z, xv[i].z, ss);
-                    ss = fmaf(xv[i].w, xv[i].w, ss);
+                if (base + tid + i * kGemvThreads < nu) {
+                    ss = fmaf(t[i].x, t[i].x, ss);
+                    ss = fmaf(t[i].y, t[i].y, ss);
+                    ss = fmaf(t[i].z, t[i].z, ss);
+                    ss = fmaf(t[i].w, t[i].w, ss);
                 }
-        } else {
-            for (int u = tid; u < nu; u += kGemvThreads) {
-                const float4 v = x4[u];
-                ss = fmaf(v.x, v.x, ss);
-                ss = fmaf(v.y, v.y, ss);
-                ss = fmaf(v.z, v.z, ss);
-                ss = fmaf(v.w, v.w, ss);
-            }
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
@@ -462,55 +516,28 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
     int* xw = reinterpret_cast<int*>(xr);                       // plane 0: words 0..3 of block b at 4b
     int2* xds = reinterpret_cast<int2*>(xr + 32 * (int64_t)P.U);  // {d, sum q}
     const int wd = lane & 7;                                    // word of the block held by this lane
-    for (int base = 0; base < nu; base += R * kGemvThreads) {
-        if (base > 0) {  // next round: all of its loads in flight before any use
+    uint8_t* xq_out = blockIdx.x == 0 ? a.xq_out : nullptr;
+    for (int r = 0; r < rounds; ++r) {
+        const int base = r * RT;
+        float4 v[R];
 #pragma unroll
-            for (int i = 0; i < R; ++i) {
-                const int u = base + tid + i * kGemvThreads;
-                if (u < nu) {
-                    xv[i] = x4[u];
-                    if (norm) wv[i] = w4[u];
-                }
-            }
-        }
+        for (int i = 0; i < R; ++i) v[i] = norm ? norm_unit(xv[i], wv[i], nscale) : xv[i];
+        if (r + 1 < rounds) load(base + RT);
+        int word[R], qs[R];
+        uint16_t dh[R];
+        q8_units<R>(v, word, dh, qs);
 #pragma unroll
         for (int i = 0; i < R; ++i) {
             const int u = base + tid + i * kGemvThreads;
-            if (u >= nu) continue;  // whole 8-lane groups drop out together (nu is a multiple of 8)
-            float4 v = xv[i];
-            if (norm) {
-                const float4 w = wv[i];
-                v.x = __fmul_rn(__fmul_rn(v.x, nscale), w.x);
-                v.y = __fmul_rn(__fmul_rn(v.y, nscale), w.y);
-                v.z = __fmul_rn(__fmul_rn(v.z, nscale), w.z);
-                v.w = __fmul_rn(__fmul_rn(v.w, nscale), w.w);
-            }
-            float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-            const unsigned gm = 0xffu << (lane & 24);  // this 8-lane group
-            amax = fmaxf(amax, __shfl_xor_sync(gm, amax, 1, 8));
-            amax = fmaxf(amax, __shfl_xor_sync(gm, amax, 2, 8));
-            amax = fmaxf(amax, __shfl_xor_sync(gm, amax, 4, 8));
-            const float d = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.f ? __frcp_rn(d) : 0.f;
-            const int q0 = round_half_away(__fmul_rn(v.x, id));
-            const int q1 = round_half_away(__fmul_rn(v.y, id));
-            const int q2 = round_half_away(__fmul_rn(v.z, id));
-            const int q3 = round_half_away(__fmul_rn(v.w, id));
-            int qs = q0 + q1 + q2 + q3;
-            qs += __shfl_xor_sync(gm, qs, 1, 8);
-            qs += __shfl_xor_sync(gm, qs, 2, 8);
-            qs += __shfl_xor_sync(gm, qs, 4, 8);
-            const int word = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) |
-                                   ((unsigned)(q2 & 0xff) << 16) | ((unsigned)(q3 & 0xff) << 24));
+            if (u >= nu) continue;
             const int b = u >> 3;
-            xw[(wd < 4 ? 0 : 4 * P.U) + 4 * b + (wd & 3)] = word;
-            const uint16_t dh = f2h(d);
-            if (wd == 0) xds[b] = make_int2(__float_as_int(h2f(dh)), qs);
-            if (a.xq_out != nullptr && blockIdx.x == 0) {
-                uint16_t* o = reinterpret_cast<uint16_t*>(a.xq_out + (int64_t)b * 34);
-                if (wd == 0) o[0] = dh;
-                o[1 + 2 * wd] = (uint16_t)((unsigned)word & 0xffffu);
-                o[2 + 2 * wd] = (uint16_t)((unsigned)word >> 16);
+            xw[(wd < 4 ? 0 : 4 * P.U) + 4 * b + (wd & 3)] = word[i];
+            if (wd == 0) xds[b] = make_int2(__float_as_int(h2f(dh[i])), qs[i]);
+            if (xq_out != nullptr) {
+                uint16_t* o = reinterpret_cast<uint16_t*>(xq_out + (int64_t)b * 34);
+                if (wd == 0) o[0] = dh[i];
+                o[1 + 2 * wd] = (uint16_t)((unsigned)word[i] & 0xffffu);
+                o[2 + 2 * wd] = (uint16_t)((unsigned)word[i] >> 16);
             }
         }
     }
