@@ -172,6 +172,13 @@ struct GemvArgs {
     // exactness exports
     int32_t* dots;                // [n][U] int32 block dots (Q formats, DEBUG kernels)
     uint8_t* xq_out;              // Q8_0 blocks of the quantised activation (CTA 0)
+    // Quantised-activation images (Q4_0 / Q8_0 weights).  An image holds the
+    // Q8_0 activation in the prologue's shared-memory layout, 40 U bytes:
+    // words [U][4] of q bytes 0..15, words [U][4] of bytes 16..31, then
+    // {d as f32, sum of q}[U].
+    const uint8_t* xq_in;         // set: the prologue copies this image instead of quantising x
+    uint8_t* xq_img;              // EPI_SWIGLU (rpc == 1): also quantise the output into this image
+    unsigned int* xq_tickets;     // one counter per 32-block of the output, zero between launches
 };
 
 constexpr int kFaThreads = 128;
@@ -192,6 +199,11 @@ struct FaArgs {
     float* part_o;          // [n_splits][Hq][D]
     float* part_ml;         // [n_splits][Hq][2]
     unsigned int* tickets;  // [Hkv][gchunks]
+    // Tensor-core kernel: when set, the output is also quantised (Q8_0 over
+    // blocks of 32 of the flat [Hq][D] vector) into this activation image of
+    // xq_U = Hq D / 32 blocks, the layout of GemvArgs::xq_in.
+    uint8_t* xq_img;
+    int xq_U;
     // TMA descriptors of K and V ([head_dim, Hkv, n_kv], 64 x 1 x 64 boxes,
     // 128-byte swizzle), filled by the launcher of the tensor-core kernel.
     CUtensorMap tmk, tmv;

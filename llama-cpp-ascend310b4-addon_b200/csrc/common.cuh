@@ -129,4 +129,56 @@ __device__ __forceinline__ int round_half_away(float x) {
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// R float4 units per lane, each an eighth of a 32-block: the 8 units of a
+// block sit in 8 consecutive lanes (lane & 7 = the unit's index in the
+// block), quantised with quantize_row_q8_0_ref's rule: d = amax / 127,
+// q = roundf(x / d) (x times the reciprocal, as ggml does).  The block max
+// and the sum of q are 8-lane shuffle reductions (order free).  The R units
+// are independent chains written phase by phase, so they interleave; all 32
+// lanes must execute this (full-warp shuffles).  Out: this lane's 4 bytes of
+// q packed in a word, and the block's f16 scale and sum of q (every lane of
+// the group).
+template <int R>
+__device__ __forceinline__ void q8_units(const float4 (&v)[R], int (&word)[R], uint16_t (&dh)[R], int (&qs)[R]) {
+    float amax[R], id[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i)
+        amax[i] = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < R; ++i) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o, 8));
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const float d = __fdiv_rn(amax[i], 127.0f);
+        id[i] = d != 0.f ? __frcp_rn(d) : 0.f;
+        dh[i] = f2h(d);
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const int q0 = round_half_away(__fmul_rn(v[i].x, id[i]));
+        const int q1 = round_half_away(__fmul_rn(v[i].y, id[i]));
+        const int q2 = round_half_away(__fmul_rn(v[i].z, id[i]));
+        const int q3 = round_half_away(__fmul_rn(v[i].w, id[i]));
+        qs[i] = q0 + q1 + q2 + q3;
+        word[i] = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) | ((unsigned)(q2 & 0xff) << 16) |
+                        ((unsigned)(q3 & 0xff) << 24));
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < R; ++i) qs[i] += __shfl_xor_sync(0xffffffffu, qs[i], o, 8);
+}
+
+// Unit `unit` of the flat activation (4 values; block unit / 8, word
+// unit % 8 of the block) into a quantised-activation image of U blocks
+// (words [U][4] of q bytes 0..15, words [U][4] of bytes 16..31, then
+// {d as f32, sum of q}[U]); the block's {d, sum} from its word-0 lane.
+__device__ __forceinline__ void q8_image_store(uint8_t* img, int64_t U, int64_t unit, int word, uint16_t dh, int qs) {
+    const int64_t b = unit >> 3;
+    const int wd = (int)(unit & 7);
+    reinterpret_cast<int*>(img)[(wd < 4 ? 0 : 4 * U) + 4 * b + (wd & 3)] = word;
+    if (wd == 0) reinterpret_cast<int2*>(img + 32 * U)[b] = make_int2(__float_as_int(h2f(dh)), qs);
+}
+
 }  // namespace b200

@@ -342,26 +342,30 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
     __syncthreads();
 
     // ---- cluster merge over the splits (distributed shared memory, push) ----
-    // CTA k of the cluster owns outputs [k tot4 / S, (k+1) tot4 / S) (in
-    // float4 units).  Every CTA stores its partial of each owner's slice, and
-    // its (max, sum) per head, straight into the owner's shared memory; after
-    // one cluster barrier every owner merges from local shared memory, and no
-    // CTA touches a peer's shared memory again.
+    // The outputs (float4 units) form tb blocks of 8 units (32 values); CTA k
+    // of the cluster owns units [8 (k tb / S), 8 ((k+1) tb / S)), whole
+    // blocks, so that it can also quantise them.  Every CTA stores its
+    // partial of each owner's slice, and its (max, sum) per head, straight
+    // into the owner's shared memory; after one cluster barrier every owner
+    // merges from local shared memory, and no CTA touches a peer's shared
+    // memory again.
     constexpr int kTot4Max = kFaMaxG * D / 4;
-    __shared__ __align__(16) float4 rcv[kTot4Max + kFmMaxCluster];  // [S][slice4]
+    __shared__ __align__(16) float4 rcv[kTot4Max + 8 * kFmMaxCluster];  // [S][slice4]
     __shared__ float rml[kFmMaxCluster][kFaMaxG][2];
     __shared__ float wr[kFaMaxG][kFmMaxCluster];
     cgx::cluster_group cluster = cgx::this_cluster();
     const int S = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
     const int tot4 = hn * D / 4;
-    const int slice4 = (tot4 + S - 1) / S;
+    const int tb = tot4 / 8;                       // D is a multiple of 32
+    const int slice4 = 8 * ((tb + S - 1) / S);
     for (int i4 = tid; i4 < tot4; i4 += kFmThreads) {
-        int k = (int)(((int64_t)i4 * S + S - 1) / tot4);  // owner: k tot4 / S <= i4 < (k+1) tot4 / S
-        while (k > 0 && k * tot4 / S > i4) --k;
-        while (k + 1 < S && (k + 1) * tot4 / S <= i4) ++k;
+        const int bi = i4 >> 3;
+        int k = (int)(((int64_t)bi * S + S - 1) / tb);  // owner: k tb / S <= bi < (k+1) tb / S
+        while (k > 0 && k * tb / S > bi) --k;
+        while (k + 1 < S && (k + 1) * tb / S <= bi) ++k;
         float4* dst = cluster.map_shared_rank(rcv, k);
-        dst[rank * slice4 + (i4 - k * tot4 / S)] = reinterpret_cast<const float4*>(co)[i4];
+        dst[rank * slice4 + (i4 - 8 * (k * tb / S))] = reinterpret_cast<const float4*>(co)[i4];
     }
     if (tid < S * kFaMaxG) {
         const int k = tid / kFaMaxG, h = tid - (tid / kFaMaxG) * kFaMaxG;
@@ -385,19 +389,33 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
         for (int r = 0; r < S; ++r) wr[h][r] *= inv;
     }
     __syncthreads();
-    const int o0 = rank * tot4 / S, o1 = (rank + 1) * tot4 / S;
-    for (int i4 = o0 + tid; i4 < o1; i4 += kFmThreads) {
-        const int h = (4 * i4) / D, d = 4 * i4 - h * D;
+    const int o0 = 8 * (rank * tb / S), o1 = 8 * ((rank + 1) * tb / S);
+    // Whole warps walk the slice together (o0 and o1 are multiples of 8, so
+    // each 8-lane group is one block, all in or all out of the slice).
+    for (int base = o0; base < o1; base += kFmThreads) {
+        const int i4 = base + tid;
+        const bool valid = i4 < o1;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < S; ++r) {
-            const float w = wr[h][r];
-            const float4 v = rcv[r * slice4 + (i4 - o0)];
-            acc.x = fmaf(v.x, w, acc.x);
-            acc.y = fmaf(v.y, w, acc.y);
-            acc.z = fmaf(v.z, w, acc.z);
-            acc.w = fmaf(v.w, w, acc.w);
+        if (valid) {
+            const int h = (4 * i4) / D, d = 4 * i4 - h * D;
+            for (int r = 0; r < S; ++r) {
+                const float w = wr[h][r];
+                const float4 v = rcv[r * slice4 + (i4 - o0)];
+                acc.x = fmaf(v.x, w, acc.x);
+                acc.y = fmaf(v.y, w, acc.y);
+                acc.z = fmaf(v.z, w, acc.z);
+                acc.w = fmaf(v.w, w, acc.w);
+            }
+            *reinterpret_cast<float4*>(a.out + (int64_t)(h0 + h) * D + d) = acc;
         }
-        *reinterpret_cast<float4*>(a.out + (int64_t)(h0 + h) * D + d) = acc;
+        if (a.xq_img != nullptr && base + (tid & ~31) < o1) {
+            // the o projection's Q8_0 activation, quantised here once
+            float4 v[1] = {acc};
+            int word[1], qs[1];
+            uint16_t dh[1];
+            q8_units<1>(v, word, dh, qs);
+            if (valid) q8_image_store(a.xq_img, a.xq_U, (int64_t)h0 * D / 4 + i4, word[0], dh[0], qs[0]);
+        }
     }
 }
 

@@ -403,47 +403,6 @@ __device__ __forceinline__ typename GemvTraits<FMT>::Acc chunk_full_dot(const ui
 
 // ------------------------------------------------------------ activation
 
-// R float4 units per lane, each an eighth of a 32-block: the 8 units of a
-// block sit in 8 consecutive lanes (lane & 7 = the unit's index in the
-// block), quantised with quantize_row_q8_0_ref's rule: d = amax / 127,
-// q = roundf(x / d) (x times the reciprocal, as ggml does).  The block max
-// and the sum of q are 8-lane shuffle reductions (order free).  The R units
-// are independent chains written phase by phase, so they interleave; all 32
-// lanes must execute this (full-warp shuffles).  Out: this lane's 4 bytes of
-// q packed in a word, and the block's f16 scale and sum of q (every lane of
-// the group).
-template <int R>
-__device__ __forceinline__ void q8_units(const float4 (&v)[R], int (&word)[R], uint16_t (&dh)[R], int (&qs)[R]) {
-    float amax[R], id[R];
-#pragma unroll
-    for (int i = 0; i < R; ++i)
-        amax[i] = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1)
-#pragma unroll
-        for (int i = 0; i < R; ++i) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o, 8));
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-        const float d = __fdiv_rn(amax[i], 127.0f);
-        id[i] = d != 0.f ? __frcp_rn(d) : 0.f;
-        dh[i] = f2h(d);
-    }
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-        const int q0 = round_half_away(__fmul_rn(v[i].x, id[i]));
-        const int q1 = round_half_away(__fmul_rn(v[i].y, id[i]));
-        const int q2 = round_half_away(__fmul_rn(v[i].z, id[i]));
-        const int q3 = round_half_away(__fmul_rn(v[i].w, id[i]));
-        qs[i] = q0 + q1 + q2 + q3;
-        word[i] = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) | ((unsigned)(q2 & 0xff) << 16) |
-                        ((unsigned)(q3 & 0xff) << 24));
-    }
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1)
-#pragma unroll
-        for (int i = 0; i < R; ++i) qs[i] += __shfl_xor_sync(0xffffffffu, qs[i], o, 8);
-}
-
 __device__ __forceinline__ float4 norm_unit(float4 v, float4 w, float nscale) {
     v.x = __fmul_rn(__fmul_rn(v.x, nscale), w.x);
     v.y = __fmul_rn(__fmul_rn(v.y, nscale), w.y);
@@ -607,6 +566,51 @@ __device__ __forceinline__ void activation_a8(const GemvArgs& a, const GemvPlan&
 
 // UPL: units per lane of this plan's full chunks (P.full_upl), or 0 when the
 // plan has none; fixed at compile time so those chunks run fully unrolled.
+// SwiGLU outputs [j0, j1) of this CTA (already stored to a.y) into the
+// Q8_0 image a.xq_img that the down projection reads.  A 32-block may span
+// two CTAs: each CTA adds the number of the block's outputs it owns to the
+// block's ticket, and the CTA that completes the count quantises the block
+// (reading the other CTA's outputs from L2) and resets the ticket.  Blocks
+// this CTA owns whole are quantised without a ticket.  The output count is
+// a multiple of 32.  `scratch` holds at least 2 + (j1 - j0) / 32 + 2 ints.
+__device__ __forceinline__ void swiglu_quantise(const GemvArgs& a, int64_t j0, int64_t j1, int tid, float* scratch) {
+    if (j1 <= j0) return;
+    const int64_t nout = a.n / 2;
+    int* list = reinterpret_cast<int*>(scratch);  // [0] = count, then block indices
+    __threadfence();   // this CTA's outputs are visible before any ticket moves
+    __syncthreads();   // ... and the row partials (which `scratch` overlaps) are read
+    if (tid == 0) list[0] = 0;
+    __syncthreads();
+    const int64_t bf = j0 / 32, bl = (j1 - 1) / 32;
+    for (int64_t b = bf + tid; b <= bl; b += kGemvThreads) {
+        const int64_t lo = max(j0, 32 * b), hi = min(j1, 32 * b + 32);
+        const unsigned own = (unsigned)(hi - lo);
+        bool mine = own == 32u;
+        if (!mine) {
+            const unsigned old = atomicAdd(&a.xq_tickets[b], own);
+            mine = old + own == 32u;
+            if (mine) a.xq_tickets[b] = 0u;
+        }
+        if (mine) list[1 + atomicAdd(&list[0], 1)] = (int)b;
+    }
+    __syncthreads();
+    const int nb = list[0];
+    __threadfence();  // the other CTAs' outputs of the completed blocks
+    const int lane = tid & 31;
+    // 8 lanes per block, one float4 each; whole warps run q8_units
+    for (int g0 = (tid >> 5) * 4; g0 < nb; g0 += kGemvThreads / 8) {
+        const int gi = g0 + (lane >> 3);
+        const bool valid = gi < nb;
+        const int64_t b = list[1 + (valid ? gi : 0)];
+        const int64_t unit = 8 * b + (lane & 7);
+        float4 v[1] = {__ldcg(reinterpret_cast<const float4*>(a.y) + unit)};
+        int word[1], qs[1];
+        uint16_t dh[1];
+        q8_units<1>(v, word, dh, qs);
+        if (valid) q8_image_store(a.xq_img, nout / 32, unit, word[0], dh[0], qs[0]);
+    }
+}
+
 template <int FMT, bool DEBUG, int UPL>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -728,10 +732,32 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     // latency-critical loads do not queue behind megabytes of weight copies.
     const bool norm = a.pro == PRO_RMSNORM;
     if constexpr (FMT == FMT_Q4 || FMT == FMT_Q8) {
-        activation_q8(a, P, xr, red, tid, lane, warp, [&] {
-            if (lane == 0)
-                for (int s = 1; s < S && s < nq; ++s) issue(s);
-        });
+        if (a.xq_in != nullptr) {
+            // the producer already quantised the activation: copy its image
+            // (loads first, then the rest of the weight ring)
+            const int64_t n16 = 40 * (int64_t)P.U / 16;
+            const int4* src = reinterpret_cast<const int4*>(a.xq_in);
+            int4* dst = reinterpret_cast<int4*>(xr);
+            constexpr int RC = 8;
+            int4 t[RC];
+            for (int64_t base = 0; base < n16; base += RC * kGemvThreads) {
+#pragma unroll
+                for (int i = 0; i < RC; ++i)
+                    if (base + tid + i * kGemvThreads < n16) t[i] = src[base + tid + i * kGemvThreads];
+                if (base == 0 && lane == 0)
+                    for (int s = 1; s < S && s < nq; ++s) issue(s);
+#pragma unroll
+                for (int i = 0; i < RC; ++i)
+                    if (base + tid + i * kGemvThreads < n16) dst[base + tid + i * kGemvThreads] = t[i];
+            }
+            if (tid == 0 && (P.U & 1))  // 40 U is a multiple of 8 only: the last 8 bytes
+                reinterpret_cast<int2*>(xr)[5 * (int64_t)P.U - 1] = reinterpret_cast<const int2*>(a.xq_in)[5 * (int64_t)P.U - 1];
+        } else {
+            activation_q8(a, P, xr, red, tid, lane, warp, [&] {
+                if (lane == 0)
+                    for (int s = 1; s < S && s < nq; ++s) issue(s);
+            });
+        }
     } else if constexpr (FMT == FMT_A8) {
         activation_a8(a, P, xr, red, tid, lane, warp, [&] {
             if (lane == 0)
@@ -873,6 +899,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         } else if (pair) {
             for (int64_t r = 2 * (int64_t)tid; r < nrows; r += 2 * kGemvThreads)
                 epi_pair(a, cr0 + r, part0[r] + part1[r], part0[r + 1] + part1[r + 1]);
+            if (a.epi == EPI_SWIGLU && a.xq_img != nullptr) swiglu_quantise(a, cr0 / 2, cr1 / 2, tid, red);
         } else {
             for (int64_t r = tid; r < nrows; r += kGemvThreads) epi_row(a, cr0 + r, part0[r] + part1[r], best);
         }

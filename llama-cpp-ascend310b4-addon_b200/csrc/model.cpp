@@ -119,6 +119,15 @@ struct b200_model {
     // B200_PDL=0): each GEMV starts streaming its weights while the previous
     // kernel drains.
     bool pdl = true;
+    // Producers quantise the next GEMV's activation (on unless
+    // B200_XQ_FUSED=0): the gate/up epilogue writes the down projection's
+    // Q8_0 image (img_h, with per-block tickets), the attention merge writes
+    // the o projection's (img_att); those GEMVs copy the image instead of
+    // quantising in every CTA.
+    bool xq_fused = true;
+    uint8_t* img_h = nullptr;
+    uint8_t* img_att = nullptr;
+    unsigned int* img_tickets = nullptr;
     // Tensor parallel: the O / down partials go to an IPC-shared region
     // (two partial buffers, then the per-rank flags) summed by the
     // peer-memory all-reduce; B200_TP_ALLREDUCE=nccl selects ncclAllReduce.
@@ -218,6 +227,12 @@ struct Dump {
     float* att = nullptr;  // device [n_layer * hq * D]
 };
 
+// Producer-side quantisation (see b200_model::xq_fused): the SwiGLU
+// epilogue writes the image only on the split-row path (d_model >= 2048),
+// the attention merge only in the tensor-core kernel (head dim 64 / 128).
+bool fused_down(const b200_model* m) { return m->xq_fused && m->c.d_model / 32 >= 64 && m->ff % 32 == 0; }
+bool fused_o(const b200_model* m) { return m->xq_fused && (m->c.head_dim == 64 || m->c.head_dim == 128); }
+
 // Argument blocks of the step's kernels (layer l).
 GemvArgs qkv_args(const b200_model* m, int l) {
     const b200_llama_config& c = m->c;
@@ -270,6 +285,10 @@ FaArgs fa_args(const b200_model* m, int l) {
     f.part_o = reinterpret_cast<float*>(ws + m->fa.off_o);
     f.part_ml = reinterpret_cast<float*>(ws + m->fa.off_ml);
     f.tickets = reinterpret_cast<unsigned int*>(ws + m->fa.off_tickets);
+    if (fused_o(m)) {
+        f.xq_img = m->img_att;
+        f.xq_U = m->hq * D / 32;
+    }
     return f;
 }
 
@@ -285,6 +304,8 @@ GemvArgs proj_args(b200_model* m, int l, int which) {
     a.n = c.d_model;
     a.k = which == 0 ? (int64_t)m->hq * c.head_dim : m->ff;
     a.x = which == 0 ? m->att : m->h;
+    if (which == 0 && fused_o(m)) a.xq_in = m->img_att;
+    if (which == 1 && fused_down(m)) a.xq_in = m->img_h;
     a.pro = PRO_PLAIN;
     a.res = m->x;
     if (m->world == 1) {
@@ -310,6 +331,10 @@ GemvArgs gate_up_args(const b200_model* m, int l) {
     a.pro = PRO_RMSNORM;
     a.epi = EPI_SWIGLU;
     a.y = m->h;
+    if (fused_down(m)) {
+        a.xq_img = m->img_h;
+        a.xq_tickets = m->img_tickets;
+    }
     return a;
 }
 
@@ -461,6 +486,7 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
     m->c = *cfg;
     m->device = device;
     if (const char* e = getenv("B200_PDL")) m->pdl = atoi(e) != 0;
+    if (const char* e = getenv("B200_XQ_FUSED")) m->xq_fused = atoi(e) != 0;
     m->rank = tp_rank;
     m->world = tp_world;
     const b200_llama_config& c = m->c;
@@ -512,6 +538,12 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
         (rc = dalloc_t(m, &m->logits, (size_t)m->voc * 4)) || (rc = dalloc_t(m, &m->st, sizeof(StepState))) ||
         (rc = dalloc(m, &m->fa_ws, m->fa_ws_bytes)) || (rc = dalloc_t(m, &m->staging, m->staging_bytes)))
         return fail(rc);
+    if ((rc = dalloc_t(m, &m->img_h, (size_t)(40 * (m->ff / 32)))) ||
+        (rc = dalloc_t(m, &m->img_att, (size_t)(40 * ((int64_t)m->hq * D / 32)))) ||
+        (rc = dalloc_t(m, &m->img_tickets, (size_t)(m->ff / 32) * sizeof(unsigned int))))
+        return fail(rc);
+    if (cudaMemset(m->img_tickets, 0, (size_t)(m->ff / 32) * sizeof(unsigned int)) != cudaSuccess)
+        return fail(B200_ECUDA);
     if (cudaMemset(m->fa_ws, 0, m->fa_ws_bytes) != cudaSuccess) return fail(B200_ECUDA);
     if (cudaMallocHost(reinterpret_cast<void**>(&m->h_st), sizeof(StepState)) != cudaSuccess) return fail(B200_ENOMEM);
     if (cudaMallocHost(reinterpret_cast<void**>(&m->h_next), sizeof(int)) != cudaSuccess) return fail(B200_ENOMEM);

@@ -132,6 +132,48 @@ def test_graph_replay_greedy_matches_decode():
     b.close()
 
 
+FUSED_SHAPES = {
+    # Llama-3-70B widths, two layers
+    "llama70b_widths": dict(n_layer=2, d_model=8192, n_head=64, n_head_kv=8, head_dim=128, d_ff=28672,
+                            vocab=128256, kv_size=4224),
+    # 5632 / 148 CTAs: ~38 SwiGLU outputs per CTA, most 32-blocks shared by two CTAs
+    "ff5632_d128": dict(n_layer=2, d_model=2048, n_head=16, n_head_kv=4, head_dim=128, d_ff=5632, vocab=4096,
+                        kv_size=320),
+    # head dim 64: attention slices of 16 blocks per kv head
+    "d64": dict(n_layer=2, d_model=2048, n_head=32, n_head_kv=8, head_dim=64, d_ff=4096, vocab=4096,
+                kv_size=320),
+}
+
+
+@pytest.mark.parametrize("shape", list(FUSED_SHAPES))
+def test_producer_quantised_activation_bit_identical(monkeypatch, shape):
+    """The gate/up epilogue and the attention merge write the Q8_0 activation
+    image that the down and o projections copy (B200_XQ_FUSED=1); with
+    B200_XQ_FUSED=0 those GEMVs quantise f32 x in every CTA.  Same bytes, so
+    every logit of every step is bit-identical."""
+    import b200_decode as B
+    import decode_model as M
+
+    kw = FUSED_SHAPES[shape]
+    n_pre = kw["kv_size"] - 128
+    out = {}
+    for fused in ("1", "0"):
+        monkeypatch.setenv("B200_XQ_FUSED", fused)
+        m = M.DecodeModel(M.LlamaConfig(**kw))
+        m.init_synthetic(seed=21, sigma=0.02)
+        m.fill_kv_synthetic(seed=22, n_pos=n_pre)
+        t, steps = 7, []
+        for i in range(3):
+            t, logits = m.decode(t, n_pre + i, want_logits=True)
+            steps.append((t, logits))
+        out[fused] = steps
+        m.close()
+    for (t1, l1), (t0, l0) in zip(out["1"], out["0"]):
+        assert t1 == t0
+        np.testing.assert_array_equal(l1, l0)
+    assert B.device_status() == 0
+
+
 def test_model_rejects_bad_config():
     import b200_decode as B
     import decode_model as M
