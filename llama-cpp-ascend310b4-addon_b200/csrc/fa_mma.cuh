@@ -105,8 +105,11 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
     const int h0 = hk * a.G + gc * kFaMaxG;
     const int hn = min(kFaMaxG, a.G - gc * kFaMaxG);
 
-    griddep_wait();  // q, the new K/V row and kv_len come from earlier kernels
-    griddep_launch_dependents();
+    // The context length and every K/V row but the newest (position
+    // ctx - 1, written by this step's QKV projection) come from earlier
+    // steps, so under a programmatic launch the first copies of chunks
+    // before the newest row start ahead of griddep_wait; q, the newest row
+    // and the mask are read after it.
     int ctx = a.n_kv;
     if (a.kv_len != nullptr) {
         const int kl = a.kv_len[0];
@@ -127,6 +130,10 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
 
     // this group's chunks: c_begin + grp + kFmGroups * i, i < ncg
     const int ncg = active ? (c_end - c_begin - grp + kFmGroups - 1) / kFmGroups : 0;
+    if (ncg <= 0) {
+        griddep_wait();
+        griddep_launch_dependents();
+    }
     if (ncg > 0) {
         const uint32_t gbase = sbase + (uint32_t)(grp * kFmStages * 2 * TILE);
         uint64_t* bars = fbar[grp];
@@ -143,12 +150,18 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
                 tma_load_3d(kdst + TILE + b * BOXB, &a.tmv, 64 * b, hk, p0, &bars[st]);
             }
         };
+        const int c_new = (ctx - 1) / kFaChunk;  // the chunk holding the newest row
         if (gtid == 0) {
             for (int st = 0; st < kFmStages; ++st) mbar_init(&bars[st], 1);
             mbar_fence_init();
             fabort[grp] = 0;
-            for (int ci = 0; ci < ncg && ci < kFmStages; ++ci) issue(ci);
+            int ci = 0;
+            for (; ci < ncg && ci < kFmStages && cfirst + kFmGroups * ci < c_new; ++ci) issue(ci);
+            griddep_wait();
+            for (; ci < ncg && ci < kFmStages; ++ci) issue(ci);
         }
+        griddep_wait();
+        griddep_launch_dependents();
 
         // Q fragments (A operand, rows = heads; rows 8..15 are zero), loaded
         // while the first K/V copies are in flight
@@ -302,21 +315,24 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
         wl[warp][g] = l_run;
     }
     __syncthreads();
-    if (tid < kFaMaxG) {
-        const int h = tid;
-        float M = -INFINITY;
-        if (active && h < hn)
+    static_assert(NW == 8, "the warp combine reduces over groups of 8 lanes");
+    if (tid < NW * kFaMaxG) {
+        // thread (h, w) = (tid / 8, tid % 8): max and weighted sum over the
+        // 8 lanes of head h, a fixed shuffle tree
+        const int h = tid >> 3, w = tid & 7;
+        const float mw = (active && h < hn) ? wm[w][h] : -INFINITY;
+        float M = mw;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][h]);
-        float L = 0.f;
+        for (int o = 1; o < 8; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o, 8));
+        const float e = (M == -INFINITY || mw == -INFINITY) ? 0.f : expf(mw - M);
+        ew[w][h] = e;
+        float L = (active && h < hn) ? wl[w][h] * e : 0.f;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            const float e = (M == -INFINITY || wm[w][h] == -INFINITY) ? 0.f : expf(wm[w][h] - M);
-            ew[w][h] = e;
-            L = fmaf(wl[w][h], e, L);
+        for (int o = 1; o < 8; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o, 8);
+        if (w == 0) {
+            cm[h] = M;
+            cl[h] = L;
         }
-        cm[h] = M;
-        cl[h] = L;
     }
     __syncthreads();
     {
@@ -374,19 +390,22 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
         dst[1] = cl[h];
     }
     cluster.sync();  // every push has landed
-    if (tid < hn) {
-        const int h = tid;
-        float M = -INFINITY;
-        for (int r = 0; r < S; ++r) M = fmaxf(M, rml[r][h][0]);
-        float L = 0.f;
-        for (int r = 0; r < S; ++r) {
-            const float mr = rml[r][h][0];
-            const float e = (mr == -INFINITY) ? 0.f : expf(mr - M);
-            wr[h][r] = e;
-            L = fmaf(rml[r][h][1], e, L);
-        }
+    static_assert(kFmMaxCluster == 16 && kFaMaxG * kFmMaxCluster <= kFmThreads, "merge lanes");
+    {
+        // thread (h, r) = (tid / 16, tid % 16): max, weighted sum and
+        // weights over the 16 lanes of head h (ranks r >= S hold nothing)
+        const int h = tid >> 4, r = tid & 15;
+        const bool live = h < hn && r < S;
+        const float mr = live ? rml[r][h][0] : -INFINITY;
+        float M = mr;
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o, 16));
+        const float e = (mr == -INFINITY) ? 0.f : expf(mr - M);
+        float L = live ? rml[r][h][1] * e : 0.f;
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o, 16);
         const float inv = L > 0.f ? 1.0f / L : 0.f;
-        for (int r = 0; r < S; ++r) wr[h][r] *= inv;
+        if (live) wr[h][r] = e * inv;
     }
     __syncthreads();
     const int o0 = 8 * (rank * tb / S), o1 = 8 * ((rank + 1) * tb / S);
