@@ -170,6 +170,61 @@ __device__ __forceinline__ void q8_units(const float4 (&v)[R], int (&word)[R], u
         for (int i = 0; i < R; ++i) qs[i] += __shfl_xor_sync(0xffffffffu, qs[i], o, 8);
 }
 
+// R half-blocks per lane: lanes 2k and 2k + 1 hold values 0..15 and 16..31
+// of one 32-block, four float4 each, quantised with quantize_row_q8_0_ref's
+// rule (d = amax / 127, q = roundf(x / d) as x times the reciprocal).  The
+// block max and the sum of q meet over the lane pair (order free).  Out: this
+// lane's 16 q bytes as four words, the block's f16 scale and sum of q (both
+// lanes).  Every lane of the warp must run it (full-warp shuffles).
+template <int R>
+__device__ __forceinline__ void q8_halves(const float4 (&v)[R][4], int4 (&w)[R], uint16_t (&dh)[R], int (&qs)[R]) {
+    float amax[R], id[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        float m[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m[j] = fmaxf(fmaxf(fabsf(v[i][j].x), fabsf(v[i][j].y)), fmaxf(fabsf(v[i][j].z), fabsf(v[i][j].w)));
+        amax[i] = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], 1));
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const float d = __fdiv_rn(amax[i], 127.0f);
+        id[i] = d != 0.f ? __frcp_rn(d) : 0.f;
+        dh[i] = f2h(d);
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        int wd[4], s = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q0 = round_half_away(__fmul_rn(v[i][j].x, id[i]));
+            const int q1 = round_half_away(__fmul_rn(v[i][j].y, id[i]));
+            const int q2 = round_half_away(__fmul_rn(v[i][j].z, id[i]));
+            const int q3 = round_half_away(__fmul_rn(v[i][j].w, id[i]));
+            s += (q0 + q1) + (q2 + q3);
+            wd[j] = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) | ((unsigned)(q2 & 0xff) << 16) |
+                          ((unsigned)(q3 & 0xff) << 24));
+        }
+        w[i] = make_int4(wd[0], wd[1], wd[2], wd[3]);
+        qs[i] = s;
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) qs[i] += __shfl_xor_sync(0xffffffffu, qs[i], 1);
+}
+
+// Half-block `half` (block half / 2; values 0..15 or 16..31) into a
+// quantised-activation image of U blocks: its 16 q bytes are words 0..3 of
+// the block in plane 0 or plane 1; the first half also stores {d, sum}.
+__device__ __forceinline__ void q8_image_store_half(uint8_t* img, int64_t U, int64_t half, int4 w, uint16_t dh,
+                                                    int qs) {
+    const int64_t b = half >> 1;
+    const int p = (int)(half & 1);
+    reinterpret_cast<int4*>(img)[(p ? U : 0) + b] = w;
+    if (p == 0) reinterpret_cast<int2*>(img + 32 * U)[b] = make_int2(__float_as_int(h2f(dh)), qs);
+}
+
 // Unit `unit` of the flat activation (4 values; block unit / 8, word
 // unit % 8 of the block) into a quantised-activation image of U blocks
 // (words [U][4] of q bytes 0..15, words [U][4] of bytes 16..31, then

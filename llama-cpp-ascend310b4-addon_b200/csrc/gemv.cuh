@@ -412,31 +412,28 @@ __device__ __forceinline__ float4 norm_unit(float4 v, float4 w, float nscale) {
 }
 
 // x -> Q8_0 activation planes in shared memory (optionally RMSNorm * w first).
-// Eight consecutive lanes share a block, one float4 each, so every warp load
-// is fully coalesced.  A thread handles units tid + i T (T threads) in rounds
-// of R: the next round's loads are in flight while the current round is
-// quantised, every lane of every warp runs every round (loads clamped to the
-// last unit, stores only for real units).  The sum of squares runs over each
-// thread's units in increasing order.  `after_issue` runs once the first
-// loads are in flight (the caller issues its remaining weight copies there).
-// Ends with __syncthreads.
+// Two lanes per 32-block (q8_halves): thread t takes half-blocks t, t + T, ...
+// (T threads), four float4 each, with the next half-block's loads in flight
+// while the current one is quantised; every lane runs every round (loads
+// clamped to the last half-block, stores only for real ones).  The sum of
+// squares runs over each thread's values in order.  `after_issue` runs once
+// the first loads are in flight (the caller issues its remaining weight
+// copies there).  Ends with __syncthreads.
 template <class AfterIssue>
 __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan& P, uint8_t* xr, float* red, int tid,
                                               int lane, int warp, AfterIssue after_issue) {
-    constexpr int R = 4;
-    constexpr int RT = R * kGemvThreads;
     const bool norm = a.pro == PRO_RMSNORM;
-    const int nu = P.U * 8;  // float4 units of x
-    const int rounds = (nu + RT - 1) / RT;
+    const int nh = 2 * P.U;  // half-blocks of x
+    const int rounds = (nh + kGemvThreads - 1) / kGemvThreads;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
     const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
-    float4 xv[R], wv[R];
-    auto load = [&](int base) {
+    float4 xv[4], wv[4];
+    auto load = [&](int r) {
+        const int h = min(r * kGemvThreads + tid, nh - 1);
 #pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const int u = min(base + tid + i * kGemvThreads, nu - 1);
-            xv[i] = x4[u];
-            if (norm) wv[i] = w4[u];
+        for (int j = 0; j < 4; ++j) {
+            xv[j] = x4[4 * h + j];
+            if (norm) wv[j] = w4[4 * h + j];
         }
     };
     load(0);
@@ -445,23 +442,19 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
     if (norm) {
         float ss = 0.f;
         for (int r = 0; r < rounds; ++r) {
-            const int base = r * RT;
-            float4 t[R];
-            if (r == 0) {
+            float4 t[4];
+            const int h = r * kGemvThreads + tid;
 #pragma unroll
-                for (int i = 0; i < R; ++i) t[i] = xv[i];
-            } else {
+            for (int j = 0; j < 4; ++j) t[j] = r == 0 ? xv[j] : x4[4 * min(h, nh - 1) + j];
+            if (h < nh) {
 #pragma unroll
-                for (int i = 0; i < R; ++i) t[i] = x4[min(base + tid + i * kGemvThreads, nu - 1)];
-            }
-#pragma unroll
-            for (int i = 0; i < R; ++i)
-                if (base + tid + i * kGemvThreads < nu) {
-                    ss = fmaf(t[i].x, t[i].x, ss);
-                    ss = fmaf(t[i].y, t[i].y, ss);
-                    ss = fmaf(t[i].z, t[i].z, ss);
-                    ss = fmaf(t[i].w, t[i].w, ss);
+                for (int j = 0; j < 4; ++j) {
+                    ss = fmaf(t[j].x, t[j].x, ss);
+                    ss = fmaf(t[j].y, t[j].y, ss);
+                    ss = fmaf(t[j].z, t[j].z, ss);
+                    ss = fmaf(t[j].w, t[j].w, ss);
                 }
+            }
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
@@ -472,31 +465,30 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
         const float mean = __fdiv_rn(tot, (float)a.k);
         nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
     }
-    int* xw = reinterpret_cast<int*>(xr);                       // plane 0: words 0..3 of block b at 4b
-    int2* xds = reinterpret_cast<int2*>(xr + 32 * (int64_t)P.U);  // {d, sum q}
-    const int wd = lane & 7;                                    // word of the block held by this lane
     uint8_t* xq_out = blockIdx.x == 0 ? a.xq_out : nullptr;
     for (int r = 0; r < rounds; ++r) {
-        const int base = r * RT;
-        float4 v[R];
+        const int h = r * kGemvThreads + tid;
+        float4 v[1][4];
 #pragma unroll
-        for (int i = 0; i < R; ++i) v[i] = norm ? norm_unit(xv[i], wv[i], nscale) : xv[i];
-        if (r + 1 < rounds) load(base + RT);
-        int word[R], qs[R];
-        uint16_t dh[R];
-        q8_units<R>(v, word, dh, qs);
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const int u = base + tid + i * kGemvThreads;
-            if (u >= nu) continue;
-            const int b = u >> 3;
-            xw[(wd < 4 ? 0 : 4 * P.U) + 4 * b + (wd & 3)] = word[i];
-            if (wd == 0) xds[b] = make_int2(__float_as_int(h2f(dh[i])), qs[i]);
+        for (int j = 0; j < 4; ++j) v[0][j] = norm ? norm_unit(xv[j], wv[j], nscale) : xv[j];
+        if (r + 1 < rounds) load(r + 1);
+        int4 w[1];
+        uint16_t dh[1];
+        int qs[1];
+        q8_halves<1>(v, w, dh, qs);
+        if (h < nh) {  // both lanes of a pair together (nh and T are even)
+            q8_image_store_half(xr, P.U, h, w[0], dh[0], qs[0]);
             if (xq_out != nullptr) {
-                uint16_t* o = reinterpret_cast<uint16_t*>(xq_out + (int64_t)b * 34);
-                if (wd == 0) o[0] = dh[i];
-                o[1 + 2 * wd] = (uint16_t)((unsigned)word[i] & 0xffffu);
-                o[2 + 2 * wd] = (uint16_t)((unsigned)word[i] >> 16);
+                // ggml block_q8_0: f16 d, then 32 int8 (2-byte aligned)
+                uint16_t* o = reinterpret_cast<uint16_t*>(xq_out + (int64_t)(h >> 1) * 34);
+                const int p = h & 1;
+                if (p == 0) o[0] = dh[0];
+                const int wds[4] = {w[0].x, w[0].y, w[0].z, w[0].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    o[1 + 8 * p + 2 * k] = (uint16_t)((unsigned)wds[k] & 0xffffu);
+                    o[2 + 8 * p + 2 * k] = (uint16_t)((unsigned)wds[k] >> 16);
+                }
             }
         }
     }
