@@ -569,7 +569,8 @@ __device__ __forceinline__ void swiglu_quantise(const GemvArgs& a, int64_t j0, i
     if (j1 <= j0) return;
     const int64_t nout = a.n / 2;
     int* list = reinterpret_cast<int*>(scratch);  // [0] = count, then block indices
-    __threadfence();   // this CTA's outputs are visible before any ticket moves
+    const bool whole = (j0 & 31) == 0 && (j1 & 31) == 0;  // no block shared with another CTA
+    if (!whole) __threadfence();  // this CTA's outputs are visible before any ticket moves
     __syncthreads();   // ... and the row partials (which `scratch` overlaps) are read
     if (tid == 0) list[0] = 0;
     __syncthreads();
@@ -587,19 +588,22 @@ __device__ __forceinline__ void swiglu_quantise(const GemvArgs& a, int64_t j0, i
     }
     __syncthreads();
     const int nb = list[0];
-    __threadfence();  // the other CTAs' outputs of the completed blocks
+    if (!whole) __threadfence();  // the other CTAs' outputs of the completed blocks
     const int lane = tid & 31;
-    // 8 lanes per block, one float4 each; whole warps run q8_units
-    for (int g0 = (tid >> 5) * 4; g0 < nb; g0 += kGemvThreads / 8) {
-        const int gi = g0 + (lane >> 3);
+    // 2 lanes per block, 16 values each; whole warps run q8_halves
+    for (int g0 = (tid >> 5) * 16; g0 < nb; g0 += kGemvThreads / 2) {
+        const int gi = g0 + (lane >> 1);
         const bool valid = gi < nb;
-        const int64_t b = list[1 + (valid ? gi : 0)];
-        const int64_t unit = 8 * b + (lane & 7);
-        float4 v[1] = {__ldcg(reinterpret_cast<const float4*>(a.y) + unit)};
-        int word[1], qs[1];
+        const int64_t half = 2 * (int64_t)list[1 + (valid ? gi : 0)] + (lane & 1);
+        const float4* src = reinterpret_cast<const float4*>(a.y) + 4 * half;
+        float4 v[1][4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[0][k] = __ldcg(src + k);
+        int4 w[1];
         uint16_t dh[1];
-        q8_units<1>(v, word, dh, qs);
-        if (valid) q8_image_store(a.xq_img, nout / 32, unit, word[0], dh[0], qs[0]);
+        int qs[1];
+        q8_halves<1>(v, w, dh, qs);
+        if (valid) q8_image_store_half(a.xq_img, nout / 32, half, w[0], dh[0], qs[0]);
     }
 }
 
@@ -712,6 +716,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         mbar_fence_init();
         if (nq > 0) issue(0);
     }
+    // row partials zeroed (shared memory only; published by the prologue's
+    // closing barrier)
+    if (P.rpc == 1)
+        for (int64_t r = tid; r < 2 * (cr1 - cr0); r += kGemvThreads) part0[r] = 0.f;
     // The first stage of every ring reads only constant data, so under a
     // programmatic launch it overlaps the previous kernel's tail; the
     // activation, residual and outputs are touched only after this wait.
@@ -798,10 +806,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     __syncthreads();  // activation ready; also publishes every warp's barrier init
 
     // ---- stream this warp's chunks ----
-    if (P.rpc == 1) {
-        for (int64_t r = tid; r < 2 * (cr1 - cr0); r += kGemvThreads) part0[r] = 0.f;
-        __syncthreads();
-    }
     using Acc = typename GemvTraits<FMT>::Acc;
     Acc acc = 0;
     unsigned long long best = 0ull;
