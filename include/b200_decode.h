@@ -107,6 +107,19 @@ int b200_gemv_q8_0_q8_0(const void *w_packed, const float *x, float *y, int64_t 
 int b200_a8w8_transform(const void *w_f16, void *dst, int64_t n, int64_t k, b200_stream_t stream);
 int b200_gemv_a8w8(const void *w_packed, const float *x, float *y, int64_t n, int64_t k, b200_stream_t stream);
 
+/* Which weights the reference's A8W8 scheme takes (host only; replaces
+ * ggml_cann_310b_is_a8w8_weight and ggml_cann_310b_a8w8_layer_disabled,
+ * patch:1481-1533): an F16 weight with ne[2] == ne[3] == 1 that is an FFN
+ * gate/up/down weight ("ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"
+ * in its ggml name) of a layer "blk.N." not listed in disable_layers, or, with
+ * tied_output set, "token_embd.weight" of shape [1536, 151936].
+ * disable_layers is the GGML_CANN_A8W8_DISABLE_LAYERS value: comma-separated
+ * layers and inclusive ranges ("0-3, 27"); NULL or "" disables none.
+ * Returns 1 (selected), 0 (not), or B200_EINVAL for a NULL name or a list item
+ * that is not a number or a range of numbers (where the reference throws). */
+int b200_a8w8_selects_weight(const char *name, int type, const int64_t ne[4], const char *disable_layers,
+                             int tied_output);
+
 /* Exactness exports.  b200_quantize_q8_0 runs the activation quantiser that
  * the Q4_0/Q8_0 GEMVs fuse (replaces W8a8QuantizeCustom,
  * w8a8_quantize_custom_vector.cpp:97-106, with ggml's per-32 Q8_0 rule) and

@@ -84,6 +84,7 @@ def _declare(L):
         "b200_gemv_q8_0_q8_0": (C.c_int, [P, P, P, I64, I64, P]),
         "b200_a8w8_transform": (C.c_int, [P, P, I64, I64, P]),
         "b200_gemv_a8w8": (C.c_int, [P, P, P, I64, I64, P]),
+        "b200_a8w8_selects_weight": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(I64), C.c_char_p, C.c_int]),
         "b200_quantize_q8_0": (C.c_int, [P, P, I64, P]),
         "b200_gemv_block_dots": (C.c_int, [C.c_int, P, P, P, P, I64, I64, P]),
         "b200_fa_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
@@ -168,6 +169,21 @@ def repack(wtype: int, src, n: int, k: int) -> PackedWeight:
     dst = torch.empty(size, dtype=torch.uint8, device=src.device)
     _check(lib().b200_repack(wtype, _ptr(src), _ptr(dst), n, k, _stream(src.device)), "b200_repack")
     return PackedWeight(wtype, n, k, dst)
+
+
+def a8w8_selects_weight(name: str, wtype: int, ne, disable_layers: str | None = None,
+                        tied_output: bool = False) -> bool:
+    """The reference's A8W8 weight policy (ggml_cann_310b_is_a8w8_weight,
+    patch:1520-1533, with GGML_CANN_A8W8_DISABLE_LAYERS parsed as in
+    ggml_cann_310b_a8w8_layer_disabled, patch:1481-1514): True for an F16
+    FFN gate/up/down weight of a layer not in `disable_layers`, or the tied
+    1536 x 151936 token_embd.weight when `tied_output`."""
+    arr = (C.c_int64 * 4)(*[int(v) for v in (list(ne) + [1, 1, 1, 1])[:4]])
+    dl = disable_layers.encode() if disable_layers is not None else None
+    rc = lib().b200_a8w8_selects_weight(name.encode(), int(wtype), arr, dl, 1 if tied_output else 0)
+    if rc < 0:
+        _check(rc, "b200_a8w8_selects_weight")
+    return rc == 1
 
 
 def a8w8_transform(w_f16, n: int, k: int) -> PackedWeight:

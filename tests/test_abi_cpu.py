@@ -112,3 +112,33 @@ def test_kv_lengths_host_helper_matches_oracle():
     m[3, 20] = -np.inf  # interior -inf does not shorten the row
     np.testing.assert_array_equal(B.kv_lengths_from_mask(m), O.kv_lengths_from_mask(m))
     np.testing.assert_array_equal(B.kv_lengths_from_mask(m), [300, 1, 1, 150, 299, 7])
+
+
+@pytest.mark.parametrize("name,wtype,ne,disable,tied,want", [
+    ("blk.0.ffn_gate.weight", 1, (1536, 8960, 1, 1), None, False, True),
+    ("blk.11.ffn_up.weight", 1, (1536, 8960, 1, 1), "", False, True),
+    ("blk.11.ffn_down.weight", 1, (8960, 1536, 1, 1), "11", False, False),
+    ("blk.11.ffn_down.weight", 1, (8960, 1536, 1, 1), "0-3, 10-12", False, False),
+    ("blk.4.ffn_down.weight", 1, (8960, 1536, 1, 1), "0-3, 10-12", False, True),
+    ("blk.3.ffn_up.weight", 1, (1536, 8960, 1, 1), ",, 3 ,", False, False),
+    ("blk.3.attn_q.weight", 1, (1536, 1536, 1, 1), None, False, False),        # not an FFN weight
+    ("blk.3.ffn_up.weight", 2, (1536, 8960, 1, 1), None, False, False),        # Q4_0: not F16
+    ("blk.3.ffn_up.weight", 1, (1536, 8960, 2, 1), None, False, False),        # batched
+    ("ffn_up.weight", 1, (1536, 8960, 1, 1), "0-99", False, True),             # no layer number
+    ("token_embd.weight", 1, (1536, 151936, 1, 1), None, True, True),
+    ("token_embd.weight", 1, (1536, 151936, 1, 1), None, False, False),
+    ("token_embd.weight", 1, (896, 151936, 1, 1), None, True, False),          # other shape
+])
+def test_a8w8_weight_policy(name, wtype, ne, disable, tied, want):
+    """ggml_cann_310b_is_a8w8_weight / _layer_disabled (patch:1481-1533)."""
+    import b200_decode as B
+
+    assert B.a8w8_selects_weight(name, wtype, ne, disable, tied) is want
+
+
+@pytest.mark.parametrize("bad", ["x", "3-", "-3", "1,a-4"])
+def test_a8w8_weight_policy_malformed_list(bad):
+    import b200_decode as B
+
+    with pytest.raises(B.B200Error):
+        B.a8w8_selects_weight("blk.5.ffn_up.weight", 1, (1536, 8960, 1, 1), bad)
