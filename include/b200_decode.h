@@ -88,6 +88,16 @@ int b200_repack_interleave2(int type, const void *src_even, const void *src_odd,
  * patch:1223-1282) -- here one kernel launch each.
  * w_packed is b200_repack output; x f32 [k]; y f32 [n]. */
 int b200_gemv_f16(const void *w_packed, const float *x, float *y, int64_t n, int64_t k, b200_stream_t stream);
+/* Small-M F16 matmul (decode batches and speculative tokens): y[j][r] =
+ * sum_i w[r][i] * f16(x[j][i]) for j < m <= 8 (fp32 accumulation), the weight
+ * streamed once for all m columns on tensor cores.  Replaces the FRACTAL_NZ
+ * branch of ggml_cann_mat_mul_fp that the reference takes for up to 8 src1
+ * columns (patch:1290-1300).  w: the ggml F16 weight [n rows][k] (k % 8 ==
+ * 0, 16-byte aligned); x: f32 [m][ldx]; y: f32 [m][ldy].  m == 1 is
+ * b200_gemv_f16.  When m columns of k halves do not fit in shared memory
+ * beside the weight ring, the weight streams once per group of columns. */
+int b200_mul_mat_f16(const void *w, const float *x, float *y, int64_t n, int64_t k, int m, int64_t ldx, int64_t ldy,
+                     b200_stream_t stream);
 int b200_gemv_q4_0(const void *w_packed, const float *x, float *y, int64_t n, int64_t k, int mode,
                    b200_stream_t stream);
 int b200_gemv_q8_0_q8_0(const void *w_packed, const float *x, float *y, int64_t n, int64_t k,

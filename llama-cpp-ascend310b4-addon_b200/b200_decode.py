@@ -80,6 +80,7 @@ def _declare(L):
         "b200_repack": (C.c_int, [C.c_int, P, P, I64, I64, P]),
         "b200_repack_interleave2": (C.c_int, [C.c_int, P, P, P, I64, I64, P]),
         "b200_gemv_f16": (C.c_int, [P, P, P, I64, I64, P]),
+        "b200_mul_mat_f16": (C.c_int, [P, P, P, I64, I64, C.c_int, I64, I64, P]),
         "b200_gemv_q4_0": (C.c_int, [P, P, P, I64, I64, C.c_int, P]),
         "b200_gemv_q8_0_q8_0": (C.c_int, [P, P, P, I64, I64, P]),
         "b200_a8w8_transform": (C.c_int, [P, P, I64, I64, P]),
@@ -211,8 +212,21 @@ def repack_interleave2(wtype: int, src_even, src_odd, n_each: int, k: int) -> Pa
 # ------------------------------------------------------------------ mul_mat
 
 def mul_mat(w: PackedWeight, x, y=None, q4_mode: int = Q4_MODE_GGML):
-    """ggml_mul_mat(W, x) at M = 1: x f32 [K] -> y f32 [N]."""
+    """ggml_mul_mat(W, x): x f32 [K] -> y f32 [N] (M = 1, every weight type),
+    or x f32 [M, K] -> y f32 [M, N] for M <= 8 columns (F16 weights: the
+    reference's small-M NZ branch)."""
     torch = _torch()
+    if x.dim() == 2 and x.shape[0] > 1:
+        if w.wtype != TYPE_F16:
+            raise B200Unsupported(EUNSUPPORTED, f"mul_mat with {x.shape[0]} columns for weight type {w.wtype}")
+        assert x.dtype == torch.float32 and x.stride(1) == 1 and x.shape[1] == w.k
+        m = x.shape[0]
+        if y is None:
+            y = torch.empty(m, w.n, dtype=torch.float32, device=x.device)
+        rc = lib().b200_mul_mat_f16(_ptr(w.data), _ptr(x), _ptr(y), w.n, w.k, m, x.stride(0), y.stride(0),
+                                    _stream(x.device))
+        _check(rc, "mul_mat")
+        return y
     assert x.dtype == torch.float32 and x.is_contiguous() and x.numel() == w.k
     if y is None:
         y = torch.empty(w.n, dtype=torch.float32, device=x.device)

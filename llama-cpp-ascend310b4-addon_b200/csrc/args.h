@@ -209,6 +209,16 @@ struct FaArgs {
     CUtensorMap tmk, tmv;
 };
 
+// Small-M F16 matmul (gemm_small.cuh).
+struct SmallMArgs {
+    CUtensorMap tmw;      // weight [n rows][k halves]: 64 x 16 boxes, 128-byte swizzle
+    const float* x;       // [m][ldx] f32
+    float* y;             // [m][ldy] f32
+    int64_t n, k, ldx, ldy;
+    int64_t xstride;      // halves per activation row in shared memory
+    int m, stages;
+};
+
 struct FaLayout {
     int n_splits, chunks_per_split, gchunks;
     size_t off_o, off_ml, off_tickets, total;

@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "fa.cuh"
 #include "fa_mma.cuh"
+#include "gemm_small.cuh"
 #include "gemv.cuh"
 #include "internal.h"
 #include "model_ops.cuh"
@@ -285,6 +286,7 @@ int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st, bool pdl) {
 // How many clusters of each size (16, 8, 4, 2 CTAs) of the tensor-core
 // attention kernel can be resident at once, per head dim; set once per device.
 int g_fa_active[kMaxDevices][2][5];
+bool g_small_m_attr[kMaxDevices];
 bool g_fa_ready[kMaxDevices][2];
 
 template <int D>
@@ -590,6 +592,60 @@ int b200_repack_interleave2(int type, const void* src_even, const void* src_odd,
 
 int b200_gemv_f16(const void* w, const float* x, float* y, int64_t n, int64_t k, b200_stream_t stream) {
     return gemv_common(FMT_F16, w, x, y, n, k, nullptr, (cudaStream_t)stream);
+}
+
+int b200_mul_mat_f16(const void* w, const float* x, float* y, int64_t n, int64_t k, int m, int64_t ldx, int64_t ldy,
+                     b200_stream_t stream) {
+    if (!w || !x || !y || n <= 0 || k <= 0 || m < 1 || m > 8 || ldx < k || ldy < n) return B200_EINVAL;
+    if (k % 8 || !aligned16(w)) return B200_EINVAL;
+    if (m == 1) return b200_gemv_f16(w, x, y, n, k, stream);
+    if (n > (int64_t)1 << 30 || k > (int64_t)1 << 30) return B200_EUNSUPPORTED;  // TMA coordinates are int32
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return B200_EINVAL;
+    {
+        std::lock_guard<std::mutex> lk(g_attr_mu);
+        if (!g_small_m_attr[dev]) {
+            CR_(cuda_status(cudaFuncSetAttribute(gemm_small_m_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 227 * 1024)));
+            g_small_m_attr[dev] = true;
+        }
+    }
+    SmallMArgs a;
+    std::memset(&a, 0, sizeof(a));
+    {
+        PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+        if (!enc) return B200_ECUDA;
+        const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)n};
+        const cuuint64_t strides[1] = {(cuuint64_t)(2 * k)};
+        const cuuint32_t box[2] = {64, 16};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUresult r = enc(&a.tmw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(w), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return B200_EUNSUPPORTED;
+    }
+    // columns per launch and ring depth within the shared-memory budget; more
+    // columns than fit stream the weight once per group
+    int mg = m, S = kSmStagesMax;
+    while (mg > 1 && small_m_smem_bytes(k, mg, S) > (size_t)kGemvSmemBudget) --mg;
+    while (S > 2 && small_m_smem_bytes(k, mg, S) > (size_t)kGemvSmemBudget) --S;
+    if (small_m_smem_bytes(k, mg, S) > 227 * 1024) return B200_EUNSUPPORTED;
+    const int64_t tiles = (n + 15) / 16;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (tiles + kSmWarps - 1) / kSmWarps));
+    a.n = n;
+    a.k = k;
+    a.ldx = ldx;
+    a.ldy = ldy;
+    a.xstride = small_m_xstride(k);
+    a.stages = S;
+    for (int m0 = 0; m0 < m; m0 += mg) {
+        a.x = x + (int64_t)m0 * ldx;
+        a.y = y + (int64_t)m0 * ldy;
+        a.m = std::min(mg, m - m0);
+        gemm_small_m_kernel<<<grid, kSmThreads, small_m_smem_bytes(k, a.m, S), (cudaStream_t)stream>>>(a);
+        CR_(cuda_status(cudaGetLastError()));
+    }
+    return B200_OK;
 }
 
 int b200_gemv_q4_0(const void* w, const float* x, float* y, int64_t n, int64_t k, int mode,

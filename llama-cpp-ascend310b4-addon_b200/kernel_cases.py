@@ -50,6 +50,14 @@ def _copies(nbytes, limit=64):
 # name: (weight type, N, K, q4 mode)
 GEMV = {
     "config1_f16": (B.TYPE_F16, 8960, 1536, 0),
+    # config 1's weight with M = 2 / 4 / 8 columns (the small-M branch)
+    "config1_f16_m2": (B.TYPE_F16, 8960, 1536, 0),
+    "config1_f16_m4": (B.TYPE_F16, 8960, 1536, 0),
+    "config1_f16_m8": (B.TYPE_F16, 8960, 1536, 0),
+    # a 4x wider k: one column (GEMV), four (one pass), eight (two passes)
+    "wide_f16": (B.TYPE_F16, 8960, 6144, 0),
+    "wide_f16_m4": (B.TYPE_F16, 8960, 6144, 0),
+    "wide_f16_m8": (B.TYPE_F16, 8960, 6144, 0),
     "config3_q4_0": (B.TYPE_Q4_0, 1536, 8960, B.Q4_MODE_GGML),
     "config3_w4a16": (B.TYPE_Q4_0, 1536, 8960, B.Q4_MODE_W4A16),
     "config4_q8_0": (B.TYPE_Q8_0, 151936, 1536, 0),
@@ -78,7 +86,9 @@ def _row_bytes(wtype, k):
 def gemv_case(name, reps_copies=None):
     torch = _torch()
     wtype, n, k, mode = GEMV[name]
-    nbytes = n * _row_bytes(wtype, k) + 4 * k + 4 * n
+    tail = name.rsplit("_m", 1)[-1]
+    m = int(tail) if "_m" in name and tail.isdigit() else 1
+    nbytes = n * _row_bytes(wtype, k) + m * (4 * k + 4 * n)
     copies = reps_copies or _copies(nbytes)
     src = _blocks(wtype, n, k)
     if wtype == B.TYPE_A8W8:
@@ -86,8 +96,8 @@ def gemv_case(name, reps_copies=None):
     else:
         ws = [B.repack(wtype, src, n, k) for _ in range(copies)]
     del src
-    x = torch.randn(k, device="cuda")
-    y = torch.empty(n, device="cuda")
+    x = torch.randn(k, device="cuda") if m == 1 else torch.randn(m, k, device="cuda")
+    y = torch.empty(n, device="cuda") if m == 1 else torch.empty(m, n, device="cuda")
     return (lambda i: B.mul_mat(ws[i % copies], x, y, q4_mode=mode)), nbytes
 
 

@@ -98,6 +98,11 @@ def test_argument_validation_without_device():
     assert L.b200_upload_begin(2, 4, 64, None, C.byref(h)) == B.EINVAL
     assert L.b200_upload_write(None, 0, None, 16, None) == B.EINVAL
     assert L.b200_upload_end(None) == B.EINVAL
+    assert L.b200_mul_mat_f16(None, None, None, 16, 64, 2, 64, 16, None) == B.EINVAL
+    fake = C.c_void_p(256)  # never dereferenced: each call fails validation first
+    assert L.b200_mul_mat_f16(fake, fake, fake, 16, 64, 9, 64, 16, None) == B.EINVAL   # m > 8
+    assert L.b200_mul_mat_f16(fake, fake, fake, 16, 60, 2, 64, 16, None) == B.EINVAL   # k % 8
+    assert L.b200_mul_mat_f16(fake, fake, fake, 16, 64, 2, 32, 16, None) == B.EINVAL   # ldx < k
     assert L.b200_a8w8_transform(None, None, 4, 64, None) == B.EINVAL
     assert L.b200_gemv_a8w8(None, None, None, 4, 64, None) == B.EINVAL
 

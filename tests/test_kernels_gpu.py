@@ -78,6 +78,44 @@ def test_gemv_f16(n, k):
     assert_close(y, O.mul_mat_f16(w, x), what=f"f16 {n}x{k}")
 
 
+@pytest.mark.parametrize("m,n,k", [(2, 8960, 1536), (8, 8960, 1536), (3, 1537, 72), (5, 100, 4096), (8, 16, 8),
+                                   (4, 4097, 28672), (7, 1000, 520), (6, 8192, 8192)])
+def test_mul_mat_f16_small_m(m, n, k):
+    """M <= 8 columns on the F16 weight (tensor cores): every column within the
+    bar against the oracle's F16 dot (x rounded to f16, fp32 accumulation).
+    Covers ragged rows and k, k past the one-pass shared-memory limit (the
+    weight streamed once per column group) and tiny shapes."""
+    r = rng(n * 13 + k + m)
+    w = (r.standard_normal((n, k)) * 0.02).astype(np.float16)
+    x = r.standard_normal((m, k)).astype(np.float32)
+    bw = B()
+    pw = bw.repack(bw.TYPE_F16, dev(w), n, k)
+    y = bw.mul_mat(pw, dev(x)).cpu().numpy()
+    assert y.shape == (m, n)
+    for j in range(m):
+        assert_close(y[j], O.mul_mat_f16(w, x[j]), what=f"f16 small-M {m}x{n}x{k} column {j}")
+    assert bw.device_status() == 0
+
+
+def test_mul_mat_f16_small_m_strided():
+    """Row strides of x and y larger than k and n (ggml views); columns of y
+    past n are not written."""
+    torch = pytest.importorskip("torch")
+    m, n, k = 5, 3000, 1024
+    r = rng(5)
+    w = (r.standard_normal((n, k)) * 0.02).astype(np.float16)
+    xf = r.standard_normal((m, k + 24)).astype(np.float32)
+    bw = B()
+    pw = bw.repack(bw.TYPE_F16, dev(w), n, k)
+    xd = dev(xf)[:, :k]
+    yd = torch.full((m, n + 40), 7.0, dtype=torch.float32, device="cuda")
+    bw.mul_mat(pw, xd, y=yd[:, :n])
+    y = yd.cpu().numpy()
+    for j in range(m):
+        assert_close(y[j, :n], O.mul_mat_f16(w, xf[j, :k]), what=f"strided column {j}")
+    assert (y[:, n:] == 7.0).all()
+
+
 def test_gemv_f16_linearity_full_size():
     """Size-independent property at config 1: y(x1 + x2) = y(x1) + y(x2)
     up to f16 rounding of the activation."""
