@@ -217,6 +217,7 @@ struct SmallMArgs {
     int64_t n, k, ldx, ldy;
     int64_t xstride;      // halves per activation row in shared memory
     int m, stages;
+    int xvec;             // x rows 16-byte aligned: load them as float4
 };
 
 struct FaLayout {

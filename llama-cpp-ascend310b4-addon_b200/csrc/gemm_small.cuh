@@ -29,8 +29,9 @@ namespace b200 {
 constexpr int kSmWarps = 4;
 constexpr int kSmThreads = 32 * kSmWarps;
 constexpr int kSmChunk = 256;                   // halves of K per ring stage
+constexpr int kSmBoxes = kSmChunk / 64;         // TMA boxes per stage
 constexpr int kSmBoxBytes = 64 * 16 * 2;        // one TMA box: 64 halves x 16 rows
-constexpr int kSmStageBytes = 4 * kSmBoxBytes;  // 8 KiB
+constexpr int kSmStageBytes = kSmBoxes * kSmBoxBytes;
 constexpr int kSmStagesMax = 4;
 
 // 2-D tiled TMA load of one box (x: the k coordinate, a multiple of 64
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(kSmThreads) gemm_small_m_kernel(const __grid_c
         mbar_arrive_expect_tx(&bars[s], kSmStageBytes);
         const uint32_t dst = ring + (uint32_t)(s * kSmStageBytes);
 #pragma unroll
-        for (int b = 0; b < 4; ++b)
+        for (int b = 0; b < kSmBoxes; ++b)
             tma_load_2d(dst + b * kSmBoxBytes, &a.tmw, c * kSmChunk + 64 * b, (int)(tile * 16), &bars[s]);
     };
     if (lane == 0) {
@@ -83,13 +84,53 @@ __global__ void __launch_bounds__(kSmThreads) gemm_small_m_kernel(const __grid_c
         mbar_fence_init();
         for (int s = 0; s < S && s < nq; ++s) issue(s, s);
     }
-    // activation rows -> f16 (zero past k), while the first copies fly
+    // activation rows -> f16 (zero past k), while the first copies fly.  Each
+    // thread issues a batch of independent loads before converting any (16-byte
+    // loads when the rows allow), so the fill costs a few load latencies, not
+    // one per element.
     const int xw = (int)a.xstride;
-    for (int r = 0; r < a.m; ++r) {
-        const float* xr = a.x + (int64_t)r * a.ldx;
-        __half* dst = xs + (int64_t)r * xw;
-#pragma unroll 4
-        for (int c = tid; c < xw; c += kSmThreads) dst[c] = __float2half_rn(c < a.k ? xr[c] : 0.f);
+    if (a.xvec) {
+        const int q4 = xw / 4;  // float4 units per padded row (xstride is a multiple of 8)
+        const int total = a.m * q4;
+        constexpr int RB = 8;
+        for (int base = 0; base < total; base += RB * kSmThreads) {
+            float4 v[RB];
+#pragma unroll
+            for (int i = 0; i < RB; ++i) {
+                const int u = base + tid + i * kSmThreads;
+                const int r = u / q4, c4 = u - r * q4;
+                v[i] = (u < total && 4 * c4 < a.k)
+                           ? *reinterpret_cast<const float4*>(a.x + (int64_t)r * a.ldx + 4 * c4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < RB; ++i) {
+                const int u = base + tid + i * kSmThreads;
+                if (u < total) {
+                    const int r = u / q4, c4 = u - r * q4;
+                    __half2* d = reinterpret_cast<__half2*>(xs + (int64_t)r * xw + 4 * c4);
+                    d[0] = __floats2half2_rn(v[i].x, v[i].y);
+                    d[1] = __floats2half2_rn(v[i].z, v[i].w);
+                }
+            }
+        }
+    } else {
+        const int total = a.m * xw;
+        constexpr int RB = 16;
+        for (int base = 0; base < total; base += RB * kSmThreads) {
+            float v[RB];
+#pragma unroll
+            for (int i = 0; i < RB; ++i) {
+                const int u = base + tid + i * kSmThreads;
+                const int r = u / xw, c = u - r * xw;
+                v[i] = (u < total && c < a.k) ? a.x[(int64_t)r * a.ldx + c] : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < RB; ++i) {
+                const int u = base + tid + i * kSmThreads;
+                if (u < total) xs[u] = __float2half_rn(v[i]);
+            }
+        }
     }
     __syncthreads();
 
@@ -120,7 +161,7 @@ __global__ void __launch_bounds__(kSmThreads) gemm_small_m_kernel(const __grid_c
         const uint32_t st = ring + (uint32_t)(s * kSmStageBytes);
         float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
+        for (int b = 0; b < kSmBoxes; ++b) {
             const int kb = ch * kSmChunk + 64 * b;
             if (kb >= a.k) break;  // boxes past k are zero: skip them
 #pragma unroll

@@ -624,11 +624,12 @@ int b200_mul_mat_f16(const void* w, const float* x, float* y, int64_t n, int64_t
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return B200_EUNSUPPORTED;
     }
-    // columns per launch and ring depth within the shared-memory budget; more
-    // columns than fit stream the weight once per group
+    // columns per launch and ring depth within the shared-memory budget: all
+    // m columns in one pass with the deepest ring that fits (down to 2
+    // stages); otherwise 2 stages and the weight streamed once per group
     int mg = m, S = kSmStagesMax;
-    while (mg > 1 && small_m_smem_bytes(k, mg, S) > (size_t)kGemvSmemBudget) --mg;
     while (S > 2 && small_m_smem_bytes(k, mg, S) > (size_t)kGemvSmemBudget) --S;
+    while (mg > 1 && small_m_smem_bytes(k, mg, S) > (size_t)kGemvSmemBudget) --mg;
     if (small_m_smem_bytes(k, mg, S) > 227 * 1024) return B200_EUNSUPPORTED;
     const int64_t tiles = (n + 15) / 16;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (tiles + kSmWarps - 1) / kSmWarps));
@@ -638,6 +639,7 @@ int b200_mul_mat_f16(const void* w, const float* x, float* y, int64_t n, int64_t
     a.ldy = ldy;
     a.xstride = small_m_xstride(k);
     a.stages = S;
+    a.xvec = aligned16(x) && ldx % 4 == 0 ? 1 : 0;
     for (int m0 = 0; m0 < m; m0 += mg) {
         a.x = x + (int64_t)m0 * ldx;
         a.y = y + (int64_t)m0 * ldy;

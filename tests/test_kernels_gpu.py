@@ -97,14 +97,15 @@ def test_mul_mat_f16_small_m(m, n, k):
     assert bw.device_status() == 0
 
 
-def test_mul_mat_f16_small_m_strided():
-    """Row strides of x and y larger than k and n (ggml views); columns of y
-    past n are not written."""
+@pytest.mark.parametrize("pad", [24, 3])
+def test_mul_mat_f16_small_m_strided(pad):
+    """Row strides of x and y larger than k and n (ggml views; pad 3 leaves x
+    rows unaligned to 16 bytes); columns of y past n are not written."""
     torch = pytest.importorskip("torch")
     m, n, k = 5, 3000, 1024
-    r = rng(5)
+    r = rng(5 + pad)
     w = (r.standard_normal((n, k)) * 0.02).astype(np.float16)
-    xf = r.standard_normal((m, k + 24)).astype(np.float32)
+    xf = r.standard_normal((m, k + pad)).astype(np.float32)
     bw = B()
     pw = bw.repack(bw.TYPE_F16, dev(w), n, k)
     xd = dev(xf)[:, :k]
