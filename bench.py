@@ -295,13 +295,17 @@ def run_ours(args):
         e2e_s = float(t.item())
     e2e = args.steps / e2e_s
 
-    # ---- dominant kernel: gate/up GEMV, event-timed per launch (eager pass)
+    # ---- dominant kernel: gate/up GEMV.  Per-launch time from CUDA events
+    # around a graph of the step's 80 gate/up launches (each layer's own
+    # weights, so nothing is served from L2); the eager per-class pass below
+    # (events around every kernel, no launch overlap) gives the breakdown.
     m.set_state(128000, N_PREFILL, advance=True)
+    gu_us = m.time_gate_up(iters=5)
     prof = m.profile(iters=2)
     d, ff_l = cfg.d_model, cfg.d_ff // world
     gu_bytes = 2 * ff_l * (d // 32) * 18 + d * 4 * 2  # Q4_0 weights + x + ffn_norm
     peak, peak_kind = measured_peaks()
-    achieved = gu_bytes / (prof["gate_up"] * 1e-6) / 1e9
+    achieved = gu_bytes / (gu_us * 1e-6) / 1e9
     tr = ncu_traffic()
     traffic = None
     if tr and int(tr.get("tp", 1)) == world:
@@ -328,7 +332,8 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "kernel": "gemv_q4_0 gate/up (fused RMSNorm+Q8_0+SwiGLU)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": peak_kind, "traffic": traffic,
-                         "bytes_per_launch": gu_bytes, "us_per_launch": prof["gate_up"],
+                         "bytes_per_launch": gu_bytes, "us_per_launch": gu_us,
+                         "us_per_launch_eager": prof["gate_up"],
                          "step_bytes": step_bytes,
                          "step_frac": step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak},
             "kernel_us": prof,

@@ -106,6 +106,13 @@ int b200_model_step_bytes(b200_model *m, int ctx, uint64_t *bytes);
  * Leaves the step state where the last step put it. */
 int b200_model_profile(b200_model *m, int iters, float *us_per_class8);
 
+/* The gate/up GEMV alone: one CUDA graph of the n_layer gate/up launches of
+ * the step (each layer's own weights, chained as in the step), replayed
+ * `iters` times between CUDA events on the model's stream; *us_per_launch is
+ * the elapsed time over iters x n_layer launches.  Overwrites the SwiGLU
+ * output and its image (scratch of the step); call between steps. */
+int b200_model_time_gate_up(b200_model *m, int iters, float *us_per_launch);
+
 #ifdef __cplusplus
 }
 #endif

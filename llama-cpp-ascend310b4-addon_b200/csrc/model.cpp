@@ -806,4 +806,40 @@ int b200_model_profile(b200_model* m, int iters, float* us) {
     return B200_OK;
 }
 
+int b200_model_time_gate_up(b200_model* m, int iters, float* us_per_launch) {
+    if (!m || !us_per_launch || iters <= 0) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    CR(b200i_prepare_device());
+    CK(cudaStreamSynchronize(m->stream));
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = B200_OK;
+    for (int l = 0; l < m->c.n_layer && rc == B200_OK; ++l)
+        rc = b200i_gemv(FMT_Q4, gate_up_args(m, l), false, m->stream, m->pdl);
+    const cudaError_t ec = cudaStreamEndCapture(m->stream, &g);
+    if (rc != B200_OK || ec != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return rc != B200_OK ? rc : B200_ECUDA;
+    }
+    cudaGraphExec_t ge = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    for (int w = 0; w < 2 && e == cudaSuccess; ++w) e = cudaGraphLaunch(ge, m->stream);  // warm-up
+    if (e == cudaSuccess) e = cudaEventRecord(e0, m->stream);
+    for (int i = 0; i < iters && e == cudaSuccess; ++i) e = cudaGraphLaunch(ge, m->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(e1, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (ge) cudaGraphExecDestroy(ge);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return B200_ECUDA;
+    *us_per_launch = ms * 1000.f / (float)(iters * m->c.n_layer);
+    return B200_OK;
+}
+
 }  // extern "C"

@@ -70,6 +70,7 @@ def _lib():
             "b200_model_stream": (P, [P]),
             "b200_model_step_bytes": (C.c_int, [P, C.c_int, C.POINTER(C.c_uint64)]),
             "b200_model_profile": (C.c_int, [P, C.c_int, P]),
+            "b200_model_time_gate_up": (C.c_int, [P, C.c_int, C.POINTER(C.c_float)]),
             "b200_model_debug_step": (C.c_int, [P, C.c_int, C.c_int, P, P, P]),
         }
         for name, (res, args) in sig.items():
@@ -183,6 +184,13 @@ class DecodeModel:
                                               q.ctypes.data_as(C.c_void_p), a.ctypes.data_as(C.c_void_p)),
                  "debug_step")
         return x, q, a
+
+    def time_gate_up(self, iters: int = 5) -> float:
+        """us per gate/up GEMV launch, from a graph of the step's n_layer
+        gate/up launches (overwrites the step's SwiGLU scratch)."""
+        us = C.c_float(0.0)
+        B._check(_lib().b200_model_time_gate_up(self.h, iters, C.byref(us)), "time_gate_up")
+        return float(us.value)
 
     def profile(self, iters: int = 3) -> dict:
         us = (C.c_float * 8)()

@@ -128,6 +128,7 @@ def test_graph_replay_greedy_matches_decode():
     assert int(np.argmax(logits)) == toks[-1]
     prof = b.profile(iters=2)
     assert prof["qkv"] > 0 and prof["attn"] > 0 and prof["lm_head"] > 0
+    assert b.time_gate_up(iters=2) > 0
     a.close()
     b.close()
 
@@ -142,6 +143,10 @@ FUSED_SHAPES = {
     # head dim 64: attention slices of 16 blocks per kv head
     "d64": dict(n_layer=2, d_model=2048, n_head=32, n_head_kv=8, head_dim=64, d_ff=4096, vocab=4096,
                 kv_size=320),
+    # one rank's shapes of Llama-3-70B at tensor parallel 8: ~24 SwiGLU outputs per CTA (a 32-block can
+    # span three CTAs) and an o projection of k = 1024 (the short-row GEMV path) fed by the image
+    "tp8_rank": dict(n_layer=2, d_model=8192, n_head=8, n_head_kv=1, head_dim=128, d_ff=3584, vocab=4096,
+                     kv_size=320),
 }
 
 
