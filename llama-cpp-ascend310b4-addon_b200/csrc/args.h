@@ -19,7 +19,11 @@ namespace b200 {
 
 enum GemvFmt { FMT_F16 = 0, FMT_Q4 = 1, FMT_Q4W = 2, FMT_Q8 = 3, FMT_A8 = 4 };
 enum GemvPro { PRO_PLAIN = 0, PRO_RMSNORM = 1 };
-enum GemvEpi { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_ARGMAX = 4 };
+enum GemvEpi { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_ARGMAX = 4, EPI_PUSH = 5 };
+
+constexpr int kMaxRanks = 8;      // tensor-parallel ranks of one node
+constexpr int kArMaxCtas = 256;   // flag slots per source rank of the fused all-reduce
+struct StepState;
 
 constexpr int kGemvWarps = 16;              // warps per CTA; each runs its own copy ring
 constexpr int kGemvThreads = 32 * kGemvWarps;
@@ -179,6 +183,23 @@ struct GemvArgs {
     const uint8_t* xq_in;         // set: the prologue copies this image instead of quantising x
     uint8_t* xq_img;              // EPI_SWIGLU (rpc == 1): also quantise the output into this image
     unsigned int* xq_tickets;     // one counter per 32-block of the output, zero between launches
+    // Fused tensor-parallel all-reduce of a row-split projection's partial
+    // (collective number seq = step x ar_per_step + ar_idx + 1).
+    //   EPI_PUSH (producer): row n's partial (+ res[n] when res is set) goes
+    //   to ar_dst[r][n] on every rank r; then every CTA releases seq into
+    //   ar_flag_dst[r][blockIdx.x] on every rank.
+    //   Prologue (consumer, ar_src set): waits until ar_flags[r][c] >= seq
+    //   for every rank r and producer CTA c < ar_grid, sums the ranks'
+    //   partials ar_src + r ar_stride in rank order as x, and CTA 0 writes
+    //   that sum to ar_x_out.
+    float* ar_dst[kMaxRanks];
+    unsigned long long* ar_flag_dst[kMaxRanks];
+    const float* ar_src;
+    unsigned long long* ar_flags;  // [kMaxRanks][kArMaxCtas]
+    float* ar_x_out;
+    int64_t ar_stride;             // floats between two ranks' slots
+    int ar_world, ar_grid, ar_idx, ar_per_step;
+    const StepState* ar_st;
 };
 
 constexpr int kFaThreads = 128;
@@ -259,7 +280,6 @@ struct StepState {
 
 // Tensor-parallel all-reduce over peer memory (one-shot): every rank sums
 // all ranks' partial vectors for collective `idx` of the current step.
-constexpr int kMaxRanks = 8;
 struct ArArgs {
     int world, rank, n;        // ranks, this rank, floats per vector (multiple of 4)
     int idx, per_step;         // collective index within the step, collectives per step

@@ -23,6 +23,7 @@
 #include <type_traits>
 
 #include "args.h"
+#include "allreduce.cuh"
 #include "common.cuh"
 
 namespace b200 {
@@ -101,6 +102,9 @@ __device__ __forceinline__ void epi_row(const GemvArgs& a, int64_t n, float v, u
         a.y[n] = v;
     } else if (a.epi == EPI_ADD) {
         a.y[n] = __fadd_rn(v, a.res[n]);
+    } else if (a.epi == EPI_PUSH) {
+        const float o = a.res != nullptr ? __fadd_rn(v, a.res[n]) : v;
+        for (int r = 0; r < a.ar_world; ++r) a.ar_dst[r][n] = o;
     } else if (a.epi == EPI_ARGMAX) {
         a.y[n] = v;
         const unsigned long long k = pack_argmax(v, n + a.row_offset);
@@ -427,12 +431,37 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
     const int rounds = (nh + kGemvThreads - 1) / kGemvThreads;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
     const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
+    // Fused all-reduce: x is the rank-ordered sum of the ranks' partials,
+    // once every producer CTA of every rank has released this collective.
+    const bool ar = a.ar_src != nullptr;
+    if (ar) {
+        const unsigned long long seq =
+            a.ar_st->step * (unsigned long long)a.ar_per_step + (unsigned long long)a.ar_idx + 1ull;
+        const int nf = a.ar_world * a.ar_grid;
+        for (int i = tid; i < nf; i += kGemvThreads)
+            wait_flag_geq(a.ar_flags + (int64_t)(i / a.ar_grid) * kArMaxCtas + (i % a.ar_grid), seq);
+        __syncthreads();
+    }
+    auto ldx = [&](int u) -> float4 {
+        if (!ar) return x4[u];
+        const float4* s4 = reinterpret_cast<const float4*>(a.ar_src);
+        float4 acc = __ldcg(s4 + u);
+        for (int r = 1; r < a.ar_world; ++r) {
+            const float4 v = __ldcg(s4 + (int64_t)r * (a.ar_stride / 4) + u);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        if (blockIdx.x == 0) reinterpret_cast<float4*>(a.ar_x_out)[u] = acc;  // the residual stream
+        return acc;
+    };
     float4 xv[4], wv[4];
     auto load = [&](int r) {
         const int h = min(r * kGemvThreads + tid, nh - 1);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            xv[j] = x4[4 * h + j];
+            xv[j] = ldx(4 * h + j);
             if (norm) wv[j] = w4[4 * h + j];
         }
     };
@@ -445,7 +474,7 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
             float4 t[4];
             const int h = r * kGemvThreads + tid;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) t[j] = r == 0 ? xv[j] : x4[4 * min(h, nh - 1) + j];
+            for (int j = 0; j < 4; ++j) t[j] = r == 0 ? xv[j] : ldx(4 * min(h, nh - 1) + j);
             if (h < nh) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -907,6 +936,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             best = other > best ? other : best;
         }
         if (lane == 0 && best != 0ull) atomicMax(a.amax, best);
+    }
+    if (a.epi == EPI_PUSH) {
+        // every row of this CTA is on every rank: release the collective
+        __threadfence_system();
+        __syncthreads();
+        if (tid < a.ar_world) {
+            const unsigned long long seq =
+                a.ar_st->step * (unsigned long long)a.ar_per_step + (unsigned long long)a.ar_idx + 1ull;
+            st_release_sys_u64(a.ar_flag_dst[tid] + blockIdx.x, seq);
+        }
     }
 }
 

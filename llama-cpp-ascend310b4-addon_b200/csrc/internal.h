@@ -15,6 +15,7 @@ int b200i_fa(const b200::FaArgs& a, int head_dim, cudaStream_t st, bool pdl = fa
 // Tensor-parallel all-reduce of a.n floats over peer memory (allreduce.cuh).
 int b200i_tp_allreduce(const b200::ArArgs& a, cudaStream_t st, bool pdl);
 int b200i_sm_count();
+int b200i_gemv_grid(int fmt, int64_t n, int64_t k, int epi);
 // Sets per-kernel attributes and caches device properties; call before capture.
 int b200i_prepare_device();
 

@@ -443,6 +443,24 @@ int b200i_tp_allreduce(const ArArgs& a, cudaStream_t st, bool pdl) {
 
 int b200i_sm_count() { return sm_count(current_device()); }
 
+// The grid b200i_gemv launches for a GEMV of this shape (the same rule as
+// launch_gemv_u); 0 for an unsupported shape.
+int b200i_gemv_grid(int fmt, int64_t n, int64_t k, int epi) {
+    const int type = fmt == FMT_F16  ? B200_TYPE_F16
+                     : fmt == FMT_Q8 ? B200_TYPE_Q8_0
+                     : fmt == FMT_A8 ? B200_TYPE_A8W8
+                                     : B200_TYPE_Q4_0;
+    GemvPlan p;
+    if (!make_plan(type, n, k, &p)) return 0;
+    const bool pair = epi == EPI_SWIGLU || epi == EPI_QKV;
+    const int64_t item_rows = p.rpc > 1 ? p.rpc : (pair ? 2 : 1);
+    const int64_t items = (p.n + item_rows - 1) / item_rows;
+    const int sm = sm_count(current_device());
+    const int64_t grid64 = p.rpc > 1 ? std::min<int64_t>(sm, (items + kGemvWarps - 1) / kGemvWarps)
+                                     : std::min<int64_t>(sm, items);
+    return (int)std::max<int64_t>(1, grid64);
+}
+
 int set_fa_attrs();
 
 int b200i_prepare_device() {

@@ -132,6 +132,14 @@ struct b200_model {
     // (two partial buffers, then the per-rank flags) summed by the
     // peer-memory all-reduce; B200_TP_ALLREDUCE=nccl selects ncclAllReduce.
     bool peer_ar = true;
+    // B200_TP_ALLREDUCE=fused: no all-reduce kernel; the O / down epilogue
+    // pushes its rows to every rank's receive slots and releases a per-CTA
+    // flag, the next GEMV's prologue waits for the flags and sums the slots
+    // in rank order (GemvArgs::ar_*).  Layer-dump and profiling steps keep
+    // the all-reduce kernel (ar_now is the current step's choice).
+    bool ar_fused = false, ar_now = false;
+    size_t recv_off = 0, fflags_off = 0;
+    int ar_grid_o = 0, ar_grid_down = 0;
     uint8_t* comm_region = nullptr;
     void* peer_region[kMaxRanks] = {};
     size_t part_stride = 0, flags_off = 0;
@@ -233,6 +241,33 @@ struct Dump {
 bool fused_down(const b200_model* m) { return m->xq_fused && m->c.d_model / 32 >= 64 && m->ff % 32 == 0; }
 bool fused_o(const b200_model* m) { return m->xq_fused && (m->c.head_dim == 64 || m->c.head_dim == 128); }
 
+// Fused all-reduce (see b200_model::ar_fused).  Producer: collective idx
+// (2 l for O, 2 l + 1 for down) lands in slot [which][rank] of every rank.
+void set_push(const b200_model* m, GemvArgs& a, int idx, int which) {
+    for (int r = 0; r < m->world; ++r) {
+        uint8_t* base = static_cast<uint8_t*>(m->peer_region[r]);
+        a.ar_dst[r] = reinterpret_cast<float*>(base + m->recv_off + ((size_t)which * m->world + m->rank) * m->part_stride);
+        a.ar_flag_dst[r] = reinterpret_cast<unsigned long long*>(base + m->fflags_off) + (size_t)m->rank * kArMaxCtas;
+    }
+    a.ar_world = m->world;
+    a.ar_idx = idx;
+    a.ar_per_step = 2 * m->c.n_layer;
+    a.ar_st = m->st;
+}
+
+// Consumer of collective idx (slots `which`, produced by a grid of `grid`).
+void set_ar_consumer(const b200_model* m, GemvArgs& a, int idx, int which, int grid) {
+    a.ar_src = reinterpret_cast<const float*>(m->comm_region + m->recv_off + (size_t)which * m->world * m->part_stride);
+    a.ar_stride = (int64_t)(m->part_stride / sizeof(float));
+    a.ar_flags = reinterpret_cast<unsigned long long*>(m->comm_region + m->fflags_off);
+    a.ar_x_out = m->x;
+    a.ar_world = m->world;
+    a.ar_grid = grid;
+    a.ar_idx = idx;
+    a.ar_per_step = 2 * m->c.n_layer;
+    a.ar_st = m->st;
+}
+
 // Argument blocks of the step's kernels (layer l).
 GemvArgs qkv_args(const b200_model* m, int l) {
     const b200_llama_config& c = m->c;
@@ -256,6 +291,7 @@ GemvArgs qkv_args(const b200_model* m, int l) {
     a.theta_scale = powf(c.rope_theta, -2.0f / (float)D);
     a.kc = Ly.kc;
     a.vc = Ly.vc;
+    if (m->ar_now && l > 0) set_ar_consumer(m, a, 2 * (l - 1) + 1, 1, m->ar_grid_down);
     return a;
 }
 
@@ -311,6 +347,10 @@ GemvArgs proj_args(b200_model* m, int l, int which) {
     if (m->world == 1) {
         a.epi = EPI_ADD;
         a.y = m->x;
+    } else if (m->ar_now) {
+        a.epi = EPI_PUSH;  // rank 0's partial carries the residual
+        a.res = m->rank == 0 ? m->x : nullptr;
+        set_push(m, a, 2 * l + which, which);
     } else {
         a.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
         a.y = part_buf(m, which);
@@ -335,6 +375,7 @@ GemvArgs gate_up_args(const b200_model* m, int l) {
         a.xq_img = m->img_h;
         a.xq_tickets = m->img_tickets;
     }
+    if (m->ar_now) set_ar_consumer(m, a, 2 * l, 0, m->ar_grid_o);
     return a;
 }
 
@@ -353,6 +394,7 @@ GemvArgs head_args(const b200_model* m) {
     a.y = m->logits;
     a.amax = &m->st->amax;
     a.row_offset = (int64_t)m->rank * m->voc;
+    if (m->ar_now) set_ar_consumer(m, a, 2 * m->c.n_layer - 1, 1, m->ar_grid_down);
     return a;
 }
 
@@ -363,6 +405,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
     auto E = [&]() { return prof ? prof->end(s) : B200_OK; };
     // events and dump copies between the kernels would serialise them anyway
     const bool pdl = m->pdl && !prof && !dump;
+    m->ar_now = m->world > 1 && m->ar_fused && !prof && !dump;
 
     CR(B(0));
     CR(b200i_embed(m->tok_embd, c.d_model, c.vocab, m->st, m->x, s));
@@ -383,7 +426,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         CR(B(3));
         CR(b200i_gemv(FMT_Q4, proj_args(m, l, 0), false, s, pdl));
         CR(E());
-        if (m->world > 1) {
+        if (m->world > 1 && !m->ar_now) {
             CR(B(7));
             CR(allreduce_sum(m, 0, 2 * l, s, pdl));
             CR(E());
@@ -394,7 +437,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         CR(B(5));
         CR(b200i_gemv(FMT_Q4, proj_args(m, l, 1), false, s, pdl));
         CR(E());
-        if (m->world > 1) {
+        if (m->world > 1 && !m->ar_now) {
             CR(B(7));
             CR(allreduce_sum(m, 1, 2 * l + 1, s, pdl));
             CR(E());
@@ -423,7 +466,9 @@ int setup_comm_region(b200_model* m) {
     if (m->world == 1) return B200_OK;
     m->part_stride = (size_t)align256((size_t)m->c.d_model * sizeof(float));
     m->flags_off = 2 * m->part_stride;
-    const size_t bytes = m->flags_off + 256;
+    m->recv_off = m->flags_off + 256;  // fused all-reduce: receive slots [2][world][d], flags [kMaxRanks][kArMaxCtas]
+    m->fflags_off = m->recv_off + 2 * (size_t)m->world * m->part_stride;
+    const size_t bytes = m->fflags_off + (size_t)kMaxRanks * kArMaxCtas * sizeof(unsigned long long);
     if (cudaMalloc(reinterpret_cast<void**>(&m->comm_region), bytes) != cudaSuccess) return B200_ENOMEM;
     CK(cudaMemset(m->comm_region, 0, bytes));
     if (!m->peer_ar) return B200_OK;
@@ -507,9 +552,18 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
         std::memcpy(&id, nccl_id128, sizeof(id));
         if (ncclCommInitRank(&m->comm, tp_world, id, tp_rank) != ncclSuccess) return fail(B200_ENCCL);
     }
-    if (const char* e = getenv("B200_TP_ALLREDUCE")) m->peer_ar = std::strcmp(e, "nccl") != 0;
-    if (tp_world > kMaxRanks) m->peer_ar = false;
+    if (const char* e = getenv("B200_TP_ALLREDUCE")) {
+        m->peer_ar = std::strcmp(e, "nccl") != 0;
+        m->ar_fused = std::strcmp(e, "fused") == 0;
+    }
+    if (tp_world > kMaxRanks) m->peer_ar = m->ar_fused = false;
     if ((rc = setup_comm_region(m))) return fail(rc);
+    if (m->ar_fused) {
+        m->ar_grid_o = b200i_gemv_grid(FMT_Q4, c.d_model, (int64_t)m->hq * D, EPI_PUSH);
+        m->ar_grid_down = b200i_gemv_grid(FMT_Q4, c.d_model, m->ff, EPI_PUSH);
+        if (m->ar_grid_o <= 0 || m->ar_grid_o > kArMaxCtas || m->ar_grid_down <= 0 || m->ar_grid_down > kArMaxCtas)
+            m->ar_fused = false;
+    }
     const size_t p_qkv = b200_packed_size(B200_TYPE_Q4_0, m->qkv_rows, c.d_model);
     const size_t p_o = b200_packed_size(B200_TYPE_Q4_0, c.d_model, (int64_t)m->hq * D);
     const size_t p_gu = b200_packed_size(B200_TYPE_Q4_0, 2 * (int64_t)m->ff, c.d_model);
@@ -811,6 +865,7 @@ int b200_model_time_gate_up(b200_model* m, int iters, float* us_per_launch) {
     CK(cudaSetDevice(m->device));
     CR(b200i_prepare_device());
     CK(cudaStreamSynchronize(m->stream));
+    m->ar_now = false;  // the launches read x as it is
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int rc = B200_OK;

@@ -28,19 +28,29 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_tp2_model_per_layer_parity(tmp_path):
+@pytest.mark.parametrize("allreduce", ["peer", "fused"])
+def test_tp2_model_per_layer_parity(tmp_path, allreduce):
+    """peer: the one-shot all-reduce kernel after O and down; fused: the O /
+    down epilogue pushes its rows to every rank and the next GEMV's prologue
+    sums them (layer-dump steps keep the kernel, so the graph step's logits
+    are also compared bit for bit with a layer-dump step's)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     out = tmp_path / "tp2.json"
     cmd = ["timeout", "-k", "60", "900", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(HERE, "tp_worker.py"), "--out", str(out)]
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    env = dict(os.environ)
+    env.pop("B200_TP_ALLREDUCE", None)
+    if allreduce == "fused":
+        env["B200_TP_ALLREDUCE"] = "fused"
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     rep = json.loads(out.read_text())
     assert rep["status"] == 0
     assert rep["x_replicated"]
     assert rep["greedy"][0] == rep["greedy"][1]
+    assert all(rep["graph_vs_dump_equal"])
     for i, st in enumerate(rep["stages"]):
         for k, (nw, ew) in st.items():
             assert nw <= TOL, f"step {i} {k}: normwise {nw:.3e}"

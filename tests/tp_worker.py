@@ -73,6 +73,15 @@ def main():
     for i in range(4):
         t = m.decode(t, n_prefill + len(toks) + i)
         mine["greedy"].append(int(t))
+    # One captured-graph step (with B200_TP_ALLREDUCE=fused its O / down
+    # partials travel through the fused all-reduce) against a layer-dump step
+    # (all-reduce kernel) at the same token and position: the rank-ordered
+    # sums are the same, so the logits must be bit-identical.
+    pos_c = n_prefill + len(toks) + 4
+    _, lg_graph = m.decode(t, pos_c, want_logits=True)
+    m.debug_step(t, pos_c)
+    _, lg_dump = m.logits()
+    mine["graph_vs_dump_equal"] = bool(np.array_equal(lg_graph, lg_dump))
     torch.cuda.synchronize()
     status = int(__import__("b200_decode").device_status(reset=True))
 
@@ -83,7 +92,8 @@ def main():
 
     if rank == 0:
         report = {"world": world, "shape": args.shape, "status": status,
-                  "greedy": [g["greedy"] for g in gathered]}
+                  "greedy": [g["greedy"] for g in gathered],
+                  "graph_vs_dump_equal": [g["graph_vs_dump_equal"] for g in gathered]}
         report.update(check(cfg, n_prefill, gathered, M))
         with open(args.out, "w") as f:
             json.dump(report, f)
