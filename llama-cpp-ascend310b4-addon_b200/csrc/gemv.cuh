@@ -97,12 +97,13 @@ B200_HD inline int64_t gemv_x_bytes(int fmt, const GemvPlan& p) {
 
 // ------------------------------------------------------------- epilogues
 
+template <bool AR = false>
 __device__ __forceinline__ void epi_row(const GemvArgs& a, int64_t n, float v, unsigned long long& best) {
     if (a.epi == EPI_STORE) {
         a.y[n] = v;
     } else if (a.epi == EPI_ADD) {
         a.y[n] = __fadd_rn(v, a.res[n]);
-    } else if (a.epi == EPI_PUSH) {
+    } else if (AR && a.epi == EPI_PUSH) {
         const float o = a.res != nullptr ? __fadd_rn(v, a.res[n]) : v;
         for (int r = 0; r < a.ar_world; ++r) a.ar_dst[r][n] = o;
     } else if (a.epi == EPI_ARGMAX) {
@@ -423,7 +424,7 @@ __device__ __forceinline__ float4 norm_unit(float4 v, float4 w, float nscale) {
 // squares runs over each thread's values in order.  `after_issue` runs once
 // the first loads are in flight (the caller issues its remaining weight
 // copies there).  Ends with __syncthreads.
-template <class AfterIssue>
+template <bool AR, class AfterIssue>
 __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan& P, uint8_t* xr, float* red, int tid,
                                               int lane, int warp, AfterIssue after_issue) {
     const bool norm = a.pro == PRO_RMSNORM;
@@ -433,7 +434,7 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
     const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
     // Fused all-reduce: x is the rank-ordered sum of the ranks' partials,
     // once every producer CTA of every rank has released this collective.
-    const bool ar = a.ar_src != nullptr;
+    const bool ar = AR && a.ar_src != nullptr;
     if (ar) {
         const unsigned long long seq =
             a.ar_st->step * (unsigned long long)a.ar_per_step + (unsigned long long)a.ar_idx + 1ull;
@@ -636,7 +637,10 @@ __device__ __forceinline__ void swiglu_quantise(const GemvArgs& a, int64_t j0, i
     }
 }
 
-template <int FMT, bool DEBUG, int UPL>
+// AR: the fused tensor-parallel all-reduce variant (EPI_PUSH epilogue,
+// summing prologue), instantiated apart so that the other kernels keep
+// their register allocation.
+template <int FMT, bool DEBUG, int UPL, bool AR = false>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& P = a.p;
@@ -782,7 +786,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             if (tid == 0 && (P.U & 1))  // 40 U is a multiple of 8 only: the last 8 bytes
                 reinterpret_cast<int2*>(xr)[5 * (int64_t)P.U - 1] = reinterpret_cast<const int2*>(a.xq_in)[5 * (int64_t)P.U - 1];
         } else {
-            activation_q8(a, P, xr, red, tid, lane, warp, [&] {
+            activation_q8<AR>(a, P, xr, red, tid, lane, warp, [&] {
                 if (lane == 0)
                     for (int s = 1; s < S && s < nq; ++s) issue(s);
             });
@@ -881,7 +885,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
                 } else if (pair) {
                     if ((rr & 1) == 0) epi_pair(a, r0 + rr, v, vn);
                 } else {
-                    epi_row(a, r0 + rr, v, best);
+                    epi_row<AR>(a, r0 + rr, v, best);
                 }
             }
             crow += P.rpc;
@@ -926,7 +930,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
                 epi_pair(a, cr0 + r, part0[r] + part1[r], part0[r + 1] + part1[r + 1]);
             if (a.epi == EPI_SWIGLU && a.xq_img != nullptr) swiglu_quantise(a, cr0 / 2, cr1 / 2, tid, red);
         } else {
-            for (int64_t r = tid; r < nrows; r += kGemvThreads) epi_row(a, cr0 + r, part0[r] + part1[r], best);
+            for (int64_t r = tid; r < nrows; r += kGemvThreads) epi_row<AR>(a, cr0 + r, part0[r] + part1[r], best);
         }
     }
     if (a.epi == EPI_ARGMAX) {
@@ -937,7 +941,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         }
         if (lane == 0 && best != 0ull) atomicMax(a.amax, best);
     }
-    if (a.epi == EPI_PUSH) {
+    if (AR && a.epi == EPI_PUSH) {
         // every row of this CTA is on every rank: release the collective
         __threadfence_system();
         __syncthreads();

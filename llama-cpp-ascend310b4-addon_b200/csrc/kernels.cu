@@ -33,7 +33,7 @@ constexpr size_t kSmemBudget = 200 * 1024;
 
 int g_sms[kMaxDevices];
 std::mutex g_attr_mu;
-bool g_attr_done[kMaxDevices][5][2][9];
+bool g_attr_done[kMaxDevices][5][2][9][2];
 
 int current_device() {
     int d = 0;
@@ -78,15 +78,15 @@ int cuda_status(cudaError_t e) {
 // Opts a GEMV instantiation into large dynamic shared memory, once per device.
 // Done before any stream capture (b200i_prepare_device) so that capturing a
 // decode step never calls it.
-template <int FMT, bool DEBUG, int UPL>
+template <int FMT, bool DEBUG, int UPL, bool AR = false>
 int set_gemv_attr(int dev) {
     std::lock_guard<std::mutex> lk(g_attr_mu);
     const int slot = UPL;
-    if (dev < 0 || dev >= kMaxDevices || g_attr_done[dev][FMT][DEBUG ? 1 : 0][slot]) return B200_OK;
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<FMT, DEBUG, UPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (dev < 0 || dev >= kMaxDevices || g_attr_done[dev][FMT][DEBUG ? 1 : 0][slot][AR ? 1 : 0]) return B200_OK;
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<FMT, DEBUG, UPL, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
     if (e != cudaSuccess) return cuda_status(e);
-    g_attr_done[dev][FMT][DEBUG ? 1 : 0][slot] = true;
+    g_attr_done[dev][FMT][DEBUG ? 1 : 0][slot][AR ? 1 : 0] = true;
     return B200_OK;
 }
 
@@ -101,6 +101,16 @@ int set_gemv_attrs(int dev) {
         CR_((set_gemv_attr<FMT, DEBUG, 6>(dev)));
         CR_((set_gemv_attr<FMT, DEBUG, 7>(dev)));
         CR_((set_gemv_attr<FMT, DEBUG, 8>(dev)));
+    }
+    if constexpr (FMT == FMT_Q4 && !DEBUG) {  // the fused all-reduce variants of the model's GEMVs
+        CR_((set_gemv_attr<FMT, DEBUG, 0, true>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 2, true>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 3, true>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 4, true>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 5, true>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 6, true>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 7, true>(dev)));
+        CR_((set_gemv_attr<FMT, DEBUG, 8, true>(dev)));
     }
     return B200_OK;
 }
@@ -124,7 +134,16 @@ cudaLaunchAttribute pdl_attr() {
 template <int FMT, bool DEBUG, int UPL>
 int launch_gemv_u(GemvArgs a, const GemvPlan& p, cudaStream_t st, bool pdl) {
     const int dev = current_device();
-    CR_((set_gemv_attr<FMT, DEBUG, UPL>(dev)));
+    // the fused all-reduce variant only where it is asked for (model Q4_0 GEMVs)
+    bool ar = a.ar_src != nullptr || a.epi == EPI_PUSH;
+    if constexpr (FMT != FMT_Q4 || DEBUG) {
+        if (ar) return B200_EUNSUPPORTED;
+    }
+    if (ar) {
+        CR_((set_gemv_attr<FMT, DEBUG, UPL, true>(dev)));
+    } else {
+        CR_((set_gemv_attr<FMT, DEBUG, UPL>(dev)));
+    }
     const bool pair = a.epi == EPI_SWIGLU || a.epi == EPI_QKV;
     if (pair && (p.n & 1)) return B200_EINVAL;
     const int64_t item_rows = p.rpc > 1 ? p.rpc : (pair ? 2 : 1);
@@ -152,9 +171,13 @@ int launch_gemv_u(GemvArgs a, const GemvPlan& p, cudaStream_t st, bool pdl) {
         cudaLaunchAttribute at = pdl_attr();
         cfg.attrs = &at;
         cfg.numAttrs = 1;
+        if (ar) return cuda_status(cudaLaunchKernelEx(&cfg, gemv_kernel<FMT, DEBUG, UPL, FMT == FMT_Q4 && !DEBUG>, a));
         return cuda_status(cudaLaunchKernelEx(&cfg, gemv_kernel<FMT, DEBUG, UPL>, a));
     }
-    gemv_kernel<FMT, DEBUG, UPL><<<grid, kGemvThreads, smem, st>>>(a);
+    if (ar)
+        gemv_kernel<FMT, DEBUG, UPL, FMT == FMT_Q4 && !DEBUG><<<grid, kGemvThreads, smem, st>>>(a);
+    else
+        gemv_kernel<FMT, DEBUG, UPL><<<grid, kGemvThreads, smem, st>>>(a);
     return cuda_status(cudaGetLastError());
 }
 
