@@ -61,6 +61,13 @@ def lib():
                 f"{LIB_PATH} is missing; build it with `python {os.path.join(HERE, 'build.py')}` "
                 "(there is no fallback path)"
             )
+        # torch first: its bundled NCCL must own the libnccl.so.2 soname.  The
+        # library links NCCL too; loaded first, it would bring the system's
+        # older NCCL, which a later `import torch` then fails to bind to.
+        try:
+            import torch  # noqa: F401
+        except ImportError:
+            pass
         _lib = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
         _declare(_lib)
     return _lib
