@@ -315,7 +315,12 @@ def run_ours(args):
     if world > 1:
         barrier()
     if rank == 0:
+        # embed, 5 per layer (qkv, attention, o, gate/up, down), lm_head, finish; at
+        # tp > 1 the default mode adds our all-reduce kernel after o and down (the
+        # argmax all-reduce is NCCL's; B200_TP_ALLREDUCE=nccl or fused launch none of ours)
         launches_per_step = 1 + 5 * cfg.n_layer + 1 + 1
+        if world > 1 and os.environ.get("B200_TP_ALLREDUCE", "") not in ("nccl", "fused"):
+            launches_per_step += 2 * cfg.n_layer
         cpu_v, cores, sample = (None, None, None)
         if world == 1 and not args.no_cpu:
             cpu_v, cores, sample = cpu_baseline()
