@@ -1,26 +1,28 @@
 // fa_mma.cuh -- single-token GQA flash-decoding on tensor cores (head_dim 64
 // and 128).
 //
-// Grid (split, kv head, q-head chunk), two groups of 4 warps.  The query heads of one
-// GQA group (up to 8) form the M dimension of mma.sync m16n8k16 (rows 8..15
-// are zero), so each K/V tile is read from HBM once for the whole group:
-//   S = Q K^T : A = f16(q) (held in registers for the whole split), B = K
-//               tile via ldmatrix from an XOR-swizzled shared-memory stage;
-//   P V       : A = P (the S accumulator layout re-used as the A operand),
-//               B = V tile via ldmatrix.trans.  P is split into an f16 high
-//               part and an f16 residual so the product keeps ~22 bits.
-// K/V chunks of 64 positions arrive by TMA (a 3-D tensor map over
-// [head_dim, kv head, position]; boxes of 64 positions x 64 dims with the
-// 128-byte swizzle) into 3-stage rings counted on mbarriers; V rows past the
-// context are zeroed in shared memory.  The two warp groups walk alternate
-// chunks of the split, each with its own ring and named barrier, so two
-// independent load/mma/softmax chains run per SM.  Each warp owns 16
-// positions of its group's chunks and keeps its own online-softmax state
-// (max, sum, output); the eight warps are combined in shared memory.  The
-// splits of one (kv head, head chunk) form one thread-block cluster: every
-// CTA stores its partial of each slice of the outputs into the shared memory
-// of the CTA that owns the slice (distributed shared memory), and after one
-// cluster barrier the owners merge locally, so partials never leave the SMs.
+// Grid (split, kv head, q-head chunk), G = 2 or 3 groups of 4 warps.  mma.sync
+// m16n8k16 with the positions as the 16-row A side and the query heads of one
+// GQA group (up to 8) as the n = 8 side, so every row of every mma is used and
+// each K/V tile is read from HBM once for the whole group:
+//   S^T = K Q^T : A = 16 positions x 16 dims of K by ldmatrix from an
+//                 XOR-swizzled shared-memory stage, B = f16(q) (registers for
+//                 the whole split);
+//   O^T += V^T P^T : A = V^T by ldmatrix.trans, B = P^T, moved from the S^T
+//                 accumulator layout by movmatrix.  P is split into an f16
+//                 high part and an f16 residual so the product keeps ~22 bits.
+// Each thread keeps the online-softmax state (max, sum) of two heads over its
+// warp's 16 positions.  K/V chunks of 64 positions arrive by TMA (a 3-D tensor
+// map over [head_dim, kv head, position]; boxes of 64 positions x 64 dims with
+// the 128-byte swizzle) into per-group mbarrier rings; V rows past the context
+// are zeroed in shared memory.  The groups walk every G-th chunk of the split,
+// each with its own ring and named barrier (3 groups x 2 stages when a CTA has
+// 6 or more chunks, else 2 x 3), so G independent load/mma/softmax chains run
+// per SM; the warps are combined in shared memory.  The splits of one (kv
+// head, head chunk) form one thread-block cluster: every CTA stores its
+// partial of each slice of the outputs into the shared memory of the CTA that
+// owns the slice (distributed shared memory), and after one cluster barrier
+// the owners merge locally, so partials never leave the SMs.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -32,9 +34,12 @@ namespace b200 {
 
 namespace cgx = cooperative_groups;
 
-constexpr int kFmStages = 3;
-constexpr int kFmGroups = 2;  // warp groups walking alternate chunks
-constexpr int kFmThreads = 128 * kFmGroups;
+// Warp groups per CTA (each walks every G-th chunk of the split with its own
+// ring) and ring stages per group: 3 x 2 when a CTA has at least 6 chunks,
+// else 2 x 3 (both 6 stages of shared memory).
+B200_HD constexpr int fm_stages(int groups) { return groups == 3 ? 2 : 3; }
+B200_HD constexpr int fm_threads(int groups) { return 128 * groups; }
+constexpr int kFmMaxThreads = fm_threads(3);
 
 // Barrier of one 128-thread warp group (ids 1.. ; 0 is __syncthreads).
 __device__ __forceinline__ void group_sync(int grp) { asm volatile("bar.sync %0, 128;" ::"r"(grp + 1) : "memory"); }
@@ -70,26 +75,36 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
         : "memory");
 }
 
+// Transpose of an 8 x 8 b16 matrix held one row pair per lane (lane g*4+t
+// holds row g, columns 2t, 2t+1) into the same layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Shared memory of fa_mma_kernel<D>: per warp group kFmStages x (K tile + V
+// Shared memory of fa_mma_kernel<D, G>: per warp group fm_stages(G) x (K tile + V
 // tile) of kFaChunk rows x D halves; reused after the loop for the warp
 // combine (4 kFmGroups x kFaMaxG padded rows of D + 8 floats plus the CTA
 // partial, kFaMaxG x D floats).
 constexpr int kFmMaxCluster = 16;
 B200_HD inline size_t fa_mma_smem_bytes(int D) {
-    const size_t ring = (size_t)kFmGroups * kFmStages * 2 * kFaChunk * D * 2 + 1024;  // + alignment of the TMA boxes
-    const size_t merge = ((size_t)4 * kFmGroups * kFaMaxG * (D + 8) + (size_t)kFaMaxG * D) * sizeof(float);
+    const size_t ring = (size_t)6 * 2 * kFaChunk * D * 2 + 1024;  // groups x stages = 6; + alignment of the TMA boxes
+    const size_t merge = ((size_t)4 * 3 * kFaMaxG * (D + 8) + (size_t)kFaMaxG * D) * sizeof(float);
     return ring > merge ? ring : merge;
 }
 
-template <int D>
-__global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constant__ FaArgs a) {
+template <int D, int G>
+__global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_constant__ FaArgs a) {
+    constexpr int kFmGroups = G;
+    constexpr int kFmStages = fm_stages(G);
+    constexpr int kFmThreads = fm_threads(G);
     constexpr int KT = D / 16;       // k tiles of the QK^T product
-    constexpr int NT = D / 8;        // n tiles of the PV product
     constexpr int GR = D / 8;        // 16-byte granules per K/V row
     constexpr int BOXB = kFaChunk * 128;  // one TMA box: 64 positions x 64 halves
     constexpr int NB = D / 64;            // boxes per K (or V) tile
@@ -123,10 +138,12 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
     __shared__ __align__(8) uint64_t fbar[kFmGroups][kFmStages];
     __shared__ int fabort[kFmGroups];
 
-    float m_run = -INFINITY, l_run = 0.f;  // head g of this warp's positions
-    float o[NT][4];
+    // online-softmax state of heads 2t and 2t + 1 over this warp's positions
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    constexpr int MT = D / 16;  // 16-dim tiles of the output
+    float o[MT][4];             // O^T tile mt: (dim 16 mt + g, heads 2t, 2t+1), (dim + 8, same heads)
 #pragma unroll
-    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int n = 0; n < MT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
     // this group's chunks: c_begin + grp + kFmGroups * i, i < ncg
     const int ncg = active ? (c_end - c_begin - grp + kFmGroups - 1) / kFmGroups : 0;
@@ -163,8 +180,8 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
         griddep_wait();
         griddep_launch_dependents();
 
-        // Q fragments (A operand, rows = heads; rows 8..15 are zero), loaded
-        // while the first K/V copies are in flight
+        // Q fragments (the B operand: k = dims, n = heads; heads past the
+        // group are zero), loaded while the first K/V copies are in flight
         uint32_t qa[KT][2];
         {
             const bool hv = g < hn;
@@ -201,89 +218,84 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
             const uint32_t kst = gbase + (uint32_t)(stage * 2 * TILE);
             const uint32_t vst = kst + TILE;
             const int pw = 16 * gw;  // this warp's 16 positions in the chunk
-            // ---- S = Q K^T over 2 n-tiles of 8 positions ----
-            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            // ---- S^T = K Q^T: A = 16 positions x 16 dims of K, B = Q^T ----
+            float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd k tiles
             {
                 const int mi = lane >> 3, ri = lane & 7;
                 const int j = mi >> 1, hh = mi & 1;
                 const int r = pw + 8 * j + ri;
 #pragma unroll
-                // two accumulator chains (even / odd k tiles) halve the
-                // dependent mma sequence
-                float s2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
                 for (int kt = 0; kt < KT; ++kt) {
-                    uint32_t b[4];
+                    uint32_t b[4];  // (pos 0-7, k 0-7), (pos 0-7, k 8-15), (pos 8-15, k 0-7), (pos 8-15, k 8-15)
                     const int gk = 2 * kt + hh;  // 16-byte granule of the row
                     ldsm_x4(b, kst + (uint32_t)((gk >> 3) * BOXB + r * 128 + (((gk & 7) ^ ri) << 4)));
-                    const uint32_t af[4] = {qa[kt][0], 0u, qa[kt][1], 0u};
-                    float(*acc)[4] = (kt & 1) ? s2 : s;
-                    mma_16816(acc[0], af, b[0], b[1]);
-                    mma_16816(acc[1], af, b[2], b[3]);
+                    const uint32_t af[4] = {b[0], b[2], b[1], b[3]};
+                    mma_16816((kt & 1) ? sb : sa, af, qa[kt][0], qa[kt][1]);
                 }
-#pragma unroll
-                for (int j = 0; j < 2; ++j)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) s[j][e] += s2[j][e];
             }
-            // ---- scale, mask, online softmax (rows = head g) ----
+            // ---- scale, mask, online softmax; this thread: positions g and g + 8
+            // of its warp, heads 2t (values 0, 2) and 2t + 1 (values 1, 3) ----
             const int pbase = c * kFaChunk + pw;
             float sv[4];
-            float cmax = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int p = pbase + 8 * j + 2 * t + e;
-                    float mv = 0.f;
-                    if (a.mask != nullptr && p < ctx) mv = h2f(a.mask[p]);
-                    float x = (p < ctx && mv != -INFINITY) ? __fadd_rn(__fmul_rn(s[j][e], a.scale), mv) : -INFINITY;
-                    sv[2 * j + e] = x;
-                    cmax = fmaxf(cmax, x);
-                }
-            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
-            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
-            const float m_new = fmaxf(m_run, cmax);
-            float alpha = 1.f;
+            for (int e = 0; e < 4; ++e) {
+                const int p = pbase + g + (e >= 2 ? 8 : 0);
+                float mv = 0.f;
+                if (a.mask != nullptr && p < ctx) mv = h2f(a.mask[p]);
+                const float sc = sa[e] + sb[e];
+                sv[e] = (p < ctx && mv != -INFINITY) ? __fadd_rn(__fmul_rn(sc, a.scale), mv) : -INFINITY;
+            }
             float pv[4];
-            if (m_new == -INFINITY) {
-                pv[0] = pv[1] = pv[2] = pv[3] = 0.f;
-            } else {
-                alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+            float alpha[2];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) pv[e] = sv[e] == -INFINITY ? 0.f : expf(sv[e] - m_new);
+            for (int hh2 = 0; hh2 < 2; ++hh2) {
+                float cmax = fmaxf(sv[hh2], sv[hh2 + 2]);
+                cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 4));
+                cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 8));
+                cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 16));
+                const float m_new = fmaxf(m_run[hh2], cmax);
+                alpha[hh2] = 1.f;
+                if (m_new == -INFINITY) {
+                    pv[hh2] = pv[hh2 + 2] = 0.f;
+                } else {
+                    alpha[hh2] = m_run[hh2] == -INFINITY ? 0.f : expf(m_run[hh2] - m_new);
+                    pv[hh2] = sv[hh2] == -INFINITY ? 0.f : expf(sv[hh2] - m_new);
+                    pv[hh2 + 2] = sv[hh2 + 2] == -INFINITY ? 0.f : expf(sv[hh2 + 2] - m_new);
+                }
+                float psum = pv[hh2] + pv[hh2 + 2];
+                psum += __shfl_xor_sync(0xffffffffu, psum, 4);
+                psum += __shfl_xor_sync(0xffffffffu, psum, 8);
+                psum += __shfl_xor_sync(0xffffffffu, psum, 16);
+                l_run[hh2] = l_run[hh2] * alpha[hh2] + psum;
+                m_run[hh2] = m_new;
             }
-            float psum = (pv[0] + pv[1]) + (pv[2] + pv[3]);
-            psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-            psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-            l_run = l_run * alpha + psum;
-            m_run = m_new;
 #pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                o[n][0] *= alpha;
-                o[n][1] *= alpha;
+            for (int n = 0; n < MT; ++n) {
+                o[n][0] *= alpha[0];
+                o[n][1] *= alpha[1];
+                o[n][2] *= alpha[0];
+                o[n][3] *= alpha[1];
             }
-            // ---- O += P V, P = P_hi + P_lo in f16 ----
-            const uint32_t ph0 = pack_half2(pv[0], pv[1]), ph1 = pack_half2(pv[2], pv[3]);
-            const __half2 h0v = *reinterpret_cast<const __half2*>(&ph0);
-            const __half2 h1v = *reinterpret_cast<const __half2*>(&ph1);
-            const float2 f0 = __half22float2(h0v), f1 = __half22float2(h1v);
-            const uint32_t pl0 = pack_half2(pv[0] - f0.x, pv[1] - f0.y), pl1 = pack_half2(pv[2] - f1.x, pv[3] - f1.y);
-            const uint32_t pa_hi[4] = {ph0, 0u, ph1, 0u};
-            const uint32_t pa_lo[4] = {pl0, 0u, pl1, 0u};
+            // ---- O^T += V^T P^T, P = P_hi + P_lo in f16; P^T's B fragments by
+            // movmatrix from the S^T accumulator layout ----
+            const uint32_t hi0 = pack_half2(pv[0], pv[1]), hi1 = pack_half2(pv[2], pv[3]);
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&hi0));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&hi1));
+            const uint32_t lo0 = pack_half2(pv[0] - f0.x, pv[1] - f0.y), lo1 = pack_half2(pv[2] - f1.x, pv[3] - f1.y);
+            const uint32_t bh0 = movmatrix_trans(hi0), bh1 = movmatrix_trans(hi1);
+            const uint32_t bl0 = movmatrix_trans(lo0), bl1 = movmatrix_trans(lo1);
             {
                 const int mi = lane >> 3, ri = lane & 7;
                 const int ph = mi & 1, jn = mi >> 1;
                 const int r = pw + 8 * ph + ri;
 #pragma unroll
-                for (int jj = 0; jj < NT / 2; ++jj) {
-                    uint32_t b[4];
+                for (int jj = 0; jj < MT; ++jj) {
+                    uint32_t b[4];  // transposed: (d 0-7, p 0-7), (d 0-7, p 8-15), (d 8-15, p 0-7), (d 8-15, p 8-15)
                     const int gv = 2 * jj + jn;
                     ldsm_x4_trans(b, vst + (uint32_t)((gv >> 3) * BOXB + r * 128 + (((gv & 7) ^ ri) << 4)));
-                    mma_16816(o[2 * jj], pa_hi, b[0], b[1]);
-                    mma_16816(o[2 * jj], pa_lo, b[0], b[1]);
-                    mma_16816(o[2 * jj + 1], pa_hi, b[2], b[3]);
-                    mma_16816(o[2 * jj + 1], pa_lo, b[2], b[3]);
+                    const uint32_t av[4] = {b[0], b[2], b[1], b[3]};
+                    mma_16816(o[jj], av, bh0, bh1);
+                    mma_16816(o[jj], av, bl0, bl1);
                 }
             }
             group_sync(grp);  // every warp is done with this stage
@@ -305,30 +317,33 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
     // scales its output by its weight and the scaled outputs are summed in
     // warp order.  Rows are padded by 8 floats so the float2 stores of a
     // warp do not collide in shared-memory banks.
-    constexpr int WS = D + 8;                                 // padded row stride (floats)
+    constexpr int WS = D + 4;                                 // padded row stride (floats)
     float* wo = reinterpret_cast<float*>(smem);             // [NW][kFaMaxG][WS] scaled warp outputs
     float* co = wo + NW * kFaMaxG * WS;                       // [kFaMaxG][D]  this CTA's partial
     __shared__ float cm[kFaMaxG], cl[kFaMaxG], ew[NW][kFaMaxG];
     __syncthreads();  // the rings are no longer read
-    if (t == 0) {
-        wm[warp][g] = m_run;
-        wl[warp][g] = l_run;
+    if (g == 0) {
+        wm[warp][2 * t] = m_run[0];
+        wm[warp][2 * t + 1] = m_run[1];
+        wl[warp][2 * t] = l_run[0];
+        wl[warp][2 * t + 1] = l_run[1];
     }
     __syncthreads();
-    static_assert(NW == 8, "the warp combine reduces over groups of 8 lanes");
-    if (tid < NW * kFaMaxG) {
-        // thread (h, w) = (tid / 8, tid % 8): max and weighted sum over the
-        // 8 lanes of head h, a fixed shuffle tree
-        const int h = tid >> 3, w = tid & 7;
-        const float mw = (active && h < hn) ? wm[w][h] : -INFINITY;
+    static_assert(NW <= 16 && 16 * kFaMaxG <= kFmThreads, "the warp combine reduces over groups of 16 lanes");
+    if (tid < 16 * kFaMaxG) {
+        // thread (h, w) = (tid / 16, tid % 16): max and weighted sum over the
+        // 16 lanes of head h (warps w >= NW hold nothing), a fixed shuffle tree
+        const int h = tid >> 4, w = tid & 15;
+        const bool live = active && h < hn && w < NW;
+        const float mw = live ? wm[w][h] : -INFINITY;
         float M = mw;
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o, 8));
+        for (int o = 1; o < 16; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o, 16));
         const float e = (M == -INFINITY || mw == -INFINITY) ? 0.f : expf(mw - M);
-        ew[w][h] = e;
-        float L = (active && h < hn) ? wl[w][h] * e : 0.f;
+        if (w < NW) ew[w][h] = e;
+        float L = live ? wl[w][h] * e : 0.f;
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o, 8);
+        for (int o = 1; o < 16; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o, 16);
         if (w == 0) {
             cm[h] = M;
             cl[h] = L;
@@ -336,10 +351,16 @@ __global__ void __launch_bounds__(kFmThreads) fa_mma_kernel(const __grid_constan
     }
     __syncthreads();
     {
-        const float e = ew[warp][g];
-        float2* dst = reinterpret_cast<float2*>(wo + ((warp * kFaMaxG) + g) * WS + 2 * t);
+        const float e0 = ew[warp][2 * t], e1 = ew[warp][2 * t + 1];
+        float* r0 = wo + (warp * kFaMaxG + 2 * t) * WS + g;
+        float* r1 = r0 + WS;
 #pragma unroll
-        for (int n = 0; n < NT; ++n) dst[4 * n] = make_float2(o[n][0] * e, o[n][1] * e);
+        for (int n = 0; n < MT; ++n) {
+            r0[16 * n] = o[n][0] * e0;
+            r1[16 * n] = o[n][1] * e1;
+            r0[16 * n + 8] = o[n][2] * e0;
+            r1[16 * n + 8] = o[n][3] * e1;
+        }
     }
     __syncthreads();
     for (int i4 = tid; i4 < kFaMaxG * D / 4; i4 += kFmThreads) {

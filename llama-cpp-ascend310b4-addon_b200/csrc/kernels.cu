@@ -316,18 +316,22 @@ template <int D>
 int fa_cluster_probe(int dev) {
     const int slot = D == 64 ? 0 : 1;
     if (g_fa_ready[dev][slot]) return B200_OK;
-    cudaError_t e = cudaFuncSetAttribute(fa_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(fa_mma_kernel<D, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)fa_mma_smem_bytes(D));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fa_mma_kernel<D, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)fa_mma_smem_bytes(D));
     if (e != cudaSuccess) return cuda_status(e);
     const bool nonportable =
-        cudaFuncSetAttribute(fa_mma_kernel<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+        cudaFuncSetAttribute(fa_mma_kernel<D, 2>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+        cudaFuncSetAttribute(fa_mma_kernel<D, 3>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
     for (int li = 0; li < 5; ++li) {
         const int cs = 16 >> li;  // 16, 8, 4, 2, 1
         g_fa_active[dev][slot][li] = 0;
         if (cs > 8 && !nonportable) continue;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(cs, 1, 1);
-        cfg.blockDim = dim3(kFmThreads, 1, 1);
+        cfg.blockDim = dim3(kFmMaxThreads, 1, 1);  // the larger variant; both hold the same shared memory
         cfg.dynamicSmemBytes = fa_mma_smem_bytes(D);
         cudaLaunchAttribute at;
         at.id = cudaLaunchAttributeClusterDimension;
@@ -337,7 +341,7 @@ int fa_cluster_probe(int dev) {
         cfg.attrs = &at;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, fa_mma_kernel<D>, &cfg) == cudaSuccess) g_fa_active[dev][slot][li] = n;
+        if (cudaOccupancyMaxActiveClusters(&n, fa_mma_kernel<D, 3>, &cfg) == cudaSuccess) g_fa_active[dev][slot][li] = n;
     }
     cudaGetLastError();
     if (g_fa_active[dev][slot][4] <= 0) g_fa_active[dev][slot][4] = 1;
@@ -419,9 +423,11 @@ int launch_fa_mma(FaArgs a, cudaStream_t st, bool pdl) {
     const int S = fa_pick_cluster<D>(dev, a.Hkv * a.gchunks, nchunks);
     a.n_splits = S;
     a.chunks_per_split = (nchunks + S - 1) / S;
+    // three warp groups (2 stages each) once a CTA has 6 or more chunks
+    const int groups = a.chunks_per_split >= 6 ? 3 : 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S, a.Hkv, a.gchunks);
-    cfg.blockDim = dim3(kFmThreads, 1, 1);
+    cfg.blockDim = dim3(fm_threads(groups), 1, 1);
     cfg.dynamicSmemBytes = fa_mma_smem_bytes(D);
     cfg.stream = st;
     cudaLaunchAttribute at[2];
@@ -432,7 +438,8 @@ int launch_fa_mma(FaArgs a, cudaStream_t st, bool pdl) {
     at[1] = pdl_attr();
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cuda_status(cudaLaunchKernelEx(&cfg, fa_mma_kernel<D>, a));
+    return cuda_status(groups == 3 ? cudaLaunchKernelEx(&cfg, fa_mma_kernel<D, 3>, a)
+                                   : cudaLaunchKernelEx(&cfg, fa_mma_kernel<D, 2>, a));
 }
 
 // head_dim 64 / 128: tensor-core cluster kernel (fa_mma.cuh); 256: CUDA-core
