@@ -89,9 +89,10 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 }
 
 // Shared memory of fa_mma_kernel<D, G>: per warp group fm_stages(G) x (K tile + V
-// tile) of kFaChunk rows x D halves; reused after the loop for the warp
-// combine (4 kFmGroups x kFaMaxG padded rows of D + 8 floats plus the CTA
-// partial, kFaMaxG x D floats).
+// tile) of kFaChunk rows x D halves, sized for the six stage slots that both
+// variants hold (3 x 2, 2 x 3); reused after the loop for the warp combine
+// (at most 12 warps x kFaMaxG rows of D + 8 floats, a bound on the padded
+// rows used, plus the CTA partial, kFaMaxG x D floats).
 constexpr int kFmMaxCluster = 16;
 B200_HD inline size_t fa_mma_smem_bytes(int D) {
     const size_t ring = (size_t)6 * 2 * kFaChunk * D * 2 + 1024;  // groups x stages = 6; + alignment of the TMA boxes
