@@ -282,6 +282,19 @@ def test_fa_config2_padded_tail_and_kv_len():
     assert_close(run_fa(q, k, v, None, kv_len=kl), O.flash_attn_decode(q, k, v, None, kv_len=kl), what="kv_len only")
 
 
+@pytest.mark.parametrize("hq,hkv,n_kv", [(64, 8, 4160), (12, 2, 8192)])
+def test_fa_three_group_splits_d128(hq, hkv, n_kv):
+    """Head dim 128 with 6 or more 64-position chunks per CTA, where the
+    launcher runs three warp groups of two stages (the Llama-3-70B attention
+    shape has up to 9 chunks per split); also truncated by kv_len so the
+    groups end on different chunks."""
+    q, k, v, mask = fa_case(hq, hkv, 128, n_kv, n_kv + hq)
+    assert_close(run_fa(q, k, v, mask), O.flash_attn_decode(q, k, v, mask, mode=0), what=f"{hq}/{hkv} n_kv={n_kv}")
+    kl = n_kv - 77
+    assert_close(run_fa(q, k, v, None, kv_len=kl), O.flash_attn_decode(q, k, v, None, kv_len=kl),
+                 what=f"{hq}/{hkv} kv_len={kl}")
+
+
 @pytest.mark.parametrize("n_kv", [1, 2, 63, 64, 65, 127, 128, 129, 239, 240, 241, 255, 256, 257, 511, 512, 513, 8192])
 def test_fa_boundary_lengths(n_kv):
     q, k, v, mask = fa_case(14, 2, 64, n_kv, n_kv)
