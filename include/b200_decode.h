@@ -53,8 +53,36 @@ const char *b200_version(void);
 const char *b200_strerror(int code);
 
 /* Reads (and optionally clears) the status word of the current device.
- * Synchronises the device. */
+ * Synchronises the device.  Once a bounded wait has expired (TIMEOUT set),
+ * every later wait that depends on another CTA, kernel or rank gives up at
+ * once, so a dead peer costs one limit, not one per collective; clearing the
+ * word re-arms them. */
 int b200_device_status(unsigned int *status, int reset);
+
+/* Limit of every bounded device-side wait on the current device, in
+ * nanoseconds (0 restores the default, 2 s).  Synchronous; call between
+ * steps (it changes kernels launched after it). */
+int b200_set_wait_timeout(uint64_t ns);
+
+/* ------------------------------------------------------------------------
+ * One-shot all-reduce (sum) of n floats over peer-mapped memory: the
+ * collective after the row-split O and down projections of tensor
+ * parallelism.  The reference has no multi-device code; this replaces the
+ * ncclAllReduce(sum) a tensor-parallel llama.cpp backend issues there.  On
+ * every rank of `world`:
+ *   parts[r]      rank r's partial [n] (device pointers; peers' through
+ *                 CUDA IPC or another peer mapping), 16-byte aligned;
+ *   flags         this rank's flag array [world] (device; zero at start);
+ *   peer_flags[r] &flags_of_rank_r[rank];
+ *   seq           collective number, > every earlier one on these flags.
+ * The kernel stores seq into every peer_flags[r] (release, system scope),
+ * waits until flags[r] >= seq for every r (bounded; B200_DEVSTATUS_TIMEOUT
+ * when a rank never arrives) and writes x = sum of parts in rank order 0,
+ * 1, ... (bit-identical on every rank).  A rank may overwrite its partial
+ * for collective seq + 2 only; alternate two partial buffers. */
+int b200_tp_allreduce_f32(float *x, const float *const *parts, int world, int rank, int64_t n,
+                          unsigned long long *flags, unsigned long long *const *peer_flags, uint64_t seq,
+                          b200_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Weight pre-layout.  Replaces the FRACTAL_NZ dual layout of the reference

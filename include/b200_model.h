@@ -97,6 +97,41 @@ b200_stream_t b200_model_stream(b200_model *m);
  * the roped q and the attention output of every layer
  * ([n_layer][n_head_local * head_dim] each).  Logits land as after a decode. */
 int b200_model_debug_step(b200_model *m, int token, int pos, float *x_host, float *q_host, float *att_host);
+/* Full layer dump of one eager step at (token, pos): every stage's output
+ * and every quantised activation the step's GEMVs consume, so that a test
+ * can check each stage against a CPU oracle fed the GPU's own stage input
+ * (stage-level teacher forcing).  Any pointer may be NULL (not dumped).
+ * Shapes are this rank's: hq = n_head / tp_world heads, hkv = n_head_kv /
+ * tp_world, ff = d_ff / tp_world, qkv_rows = (hq + 2 hkv) head_dim.  Q8_0
+ * activations are ggml block_q8_0 rows (k / 32 blocks of 34 bytes): for
+ * QKV, gate/up and the lm_head the bytes the GEMV's own prologue quantised
+ * (its first CTA's copy), for O and down the image the producing kernel
+ * (attention, the SwiGLU epilogue) wrote and the GEMV copies.  dots_* are
+ * the int32 dot of every (packed weight row, 32-block) from the same GEMV
+ * launch (its export variant): QKV rows are q, then k, then v rows; gate/up
+ * rows alternate gate i, up i. */
+typedef struct {
+    float *x;          /* [n_layer + 1][d_model] residual after the embedding and after every layer */
+    float *x_mid;      /* [n_layer][d_model] residual after the O projection (summed over ranks) */
+    float *q;          /* [n_layer][hq * head_dim] roped q */
+    uint16_t *k_row;   /* [n_layer][hkv * head_dim] f16 K row written at pos */
+    uint16_t *v_row;   /* [n_layer][hkv * head_dim] f16 V row written at pos */
+    float *att;        /* [n_layer][hq * head_dim] attention output */
+    float *h;          /* [n_layer][ff] SwiGLU output */
+    float *logits;     /* [vocab / tp_world] */
+    uint8_t *xq_qkv;   /* [n_layer][d_model / 32 * 34] */
+    uint8_t *xq_o;     /* [n_layer][hq * head_dim / 32 * 34] */
+    uint8_t *xq_gu;    /* [n_layer][d_model / 32 * 34] */
+    uint8_t *xq_down;  /* [n_layer][ff / 32 * 34] */
+    uint8_t *xq_head;  /* [d_model / 32 * 34] */
+    int32_t *dots_qkv; /* [n_layer][qkv_rows][d_model / 32] */
+    int32_t *dots_o;   /* [n_layer][d_model][hq * head_dim / 32] */
+    int32_t *dots_gu;  /* [n_layer][2 ff][d_model / 32] */
+    int32_t *dots_down;/* [n_layer][d_model][ff / 32] */
+    int32_t *dots_head;/* [vocab / tp_world][d_model / 32] */
+} b200_step_dump;
+int b200_model_debug_step_ex(b200_model *m, int token, int pos, const b200_step_dump *dump);
+
 /* Algorithmic HBM bytes one decode step reads on this rank at context ctx. */
 int b200_model_step_bytes(b200_model *m, int ctx, uint64_t *bytes);
 /* Runs `iters` eager (not captured) steps with CUDA events around every

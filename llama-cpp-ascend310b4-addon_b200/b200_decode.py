@@ -82,6 +82,8 @@ def _declare(L):
         "b200_version": (C.c_char_p, []),
         "b200_strerror": (C.c_char_p, [C.c_int]),
         "b200_device_status": (C.c_int, [C.POINTER(C.c_uint), C.c_int]),
+        "b200_set_wait_timeout": (C.c_int, [C.c_uint64]),
+        "b200_tp_allreduce_f32": (C.c_int, [P, C.POINTER(P), C.c_int, C.c_int, I64, P, C.POINTER(P), C.c_uint64, P]),
         "b200_packed_row_stride": (I64, [C.c_int, I64, I64]),
         "b200_packed_size": (C.c_size_t, [C.c_int, I64, I64]),
         "b200_repack": (C.c_int, [C.c_int, P, P, I64, I64, P]),
@@ -149,6 +151,41 @@ def device_status(reset: bool = True) -> int:
     v = C.c_uint(0)
     _check(lib().b200_device_status(C.byref(v), 1 if reset else 0), "b200_device_status")
     return int(v.value)
+
+
+DEVSTATUS_TIMEOUT = 1
+DEVSTATUS_BOUNDS = 2
+
+
+def set_wait_timeout(ns: int = 0):
+    """Limit of every bounded device-side wait on the current device (0: the
+    default 2 s)."""
+    _check(lib().b200_set_wait_timeout(int(ns)), "b200_set_wait_timeout")
+
+
+def tp_allreduce_f32(x, parts, rank: int, flags, peer_flags, seq: int, stream=None):
+    """One-shot peer-memory all-reduce (sum in rank order) of n floats.
+
+    x: f32 [n] device tensor (result); parts: world device pointers (ints)
+    or tensors holding every rank's partial; flags: this rank's u64 flag
+    array [world]; peer_flags: world device addresses of
+    &flags_of_rank_r[rank]; seq: collective number (> 0, increasing)."""
+    torch = _torch()
+    world = len(parts)
+    if len(peer_flags) != world:
+        raise B200Error(EINVAL, "tp_allreduce_f32: parts and peer_flags differ in length")
+    if x.dtype != torch.float32 or not x.is_contiguous() or not x.is_cuda:
+        raise B200Error(EINVAL, "tp_allreduce_f32: x must be a contiguous f32 CUDA tensor")
+
+    def addr(p):
+        return int(p.data_ptr()) if hasattr(p, "data_ptr") else int(p)
+
+    pa = (P * world)(*[addr(p) for p in parts])
+    fa = (P * world)(*[addr(p) for p in peer_flags])
+    st = C.c_void_p(stream) if stream is not None else _stream(x.device)
+    _check(lib().b200_tp_allreduce_f32(_ptr(x), pa, world, rank, x.numel(), C.c_void_p(addr(flags)), fa, int(seq),
+                                       st), "tp_allreduce_f32")
+    return x
 
 
 # ----------------------------------------------------------- packed weights
@@ -289,6 +326,42 @@ def fa_workspace(head_dim: int, n_head: int, n_head_kv: int, n_kv: int, device):
     return ws
 
 
+def _check_fa_tensors(what, q, k, v, mask, kv_lengths, out):
+    """The op contract of FLASH_ATTN_EXT at one query token (the reference
+    asserts the same types, patch:1378-1382 and patch:2017-2020): q f32
+    [Hq, D]; k, v f16 [n_kv, Hkv, D] with a contiguous head dim; mask f16
+    with at least n_kv entries; kv_lengths int32 with at least one; out f32
+    [Hq, D] contiguous; all on q's device.  Returns (hq, d, n_kv, hkv)."""
+    torch = _torch()
+
+    def bad(msg):
+        raise B200Error(EINVAL, f"{what}: {msg}")
+
+    if q.dim() != 2 or k.dim() != 3 or v.dim() != 3:
+        bad("q must be [Hq, D] and k, v [n_kv, Hkv, D]")
+    hq, d = q.shape
+    n_kv, hkv, d2 = k.shape
+    if d2 != d or tuple(v.shape) != tuple(k.shape):
+        bad("shapes")
+    if q.dtype != torch.float32 or k.dtype != torch.float16 or v.dtype != torch.float16:
+        bad("q must be f32 and k, v f16")
+    dev = q.device
+    if not q.is_cuda or k.device != dev or v.device != dev:
+        bad("q, k, v must be on one CUDA device")
+    if k.stride(2) != 1 or v.stride(2) != 1:
+        bad("needs contiguous head dim")
+    if mask is not None and (mask.dtype != torch.float16 or mask.device != dev or not mask.is_contiguous()
+                             or mask.numel() < n_kv):
+        bad("mask must be a contiguous f16 tensor of at least n_kv entries on q's device")
+    if kv_lengths is not None and (kv_lengths.dtype != torch.int32 or kv_lengths.device != dev
+                                   or kv_lengths.numel() < 1):
+        bad("kv_lengths must be an int32 tensor on q's device")
+    if out is not None and (out.dtype != torch.float32 or out.device != dev or not out.is_contiguous()
+                            or tuple(out.shape) != (hq, d)):
+        bad("out must be a contiguous f32 [Hq, D] tensor on q's device")
+    return hq, d, n_kv, hkv
+
+
 def flash_attn_ext(q, k, v, mask=None, scale: float = 1.0, max_bias: float = 0.0, logit_softcap: float = 0.0,
                    kv_lengths=None, out=None, workspace=None):
     """ggml_flash_attn_ext for one query token.
@@ -299,12 +372,7 @@ def flash_attn_ext(q, k, v, mask=None, scale: float = 1.0, max_bias: float = 0.0
     torch = _torch()
     if max_bias != 0.0 or logit_softcap != 0.0:
         raise B200Unsupported(EUNSUPPORTED, "flash_attn_ext with ALiBi or softcap")
-    hq, d = q.shape
-    n_kv, hkv, d2 = k.shape
-    if d2 != d or tuple(v.shape) != tuple(k.shape):
-        raise B200Error(EINVAL, "flash_attn_ext shapes")
-    if k.stride(2) != 1 or v.stride(2) != 1:
-        raise B200Error(EINVAL, "flash_attn_ext needs contiguous head dim")
+    hq, d, n_kv, hkv = _check_fa_tensors("flash_attn_ext", q, k, v, mask, kv_lengths, out)
     q = q.contiguous()
     if out is None:
         out = torch.empty((hq, d), dtype=torch.float32, device=q.device)
@@ -329,12 +397,9 @@ def flash_attn_ext_static_scratch(q, k, v, mask=None, scale: float = 1.0, kv_len
     one GPU share the array and race.  Only ``out`` may be allocated here, and
     only when the caller passes none."""
     torch = _torch()
-    hq, d = q.shape
-    n_kv, hkv, d2 = k.shape
-    if d2 != d or tuple(v.shape) != tuple(k.shape):
-        raise B200Error(EINVAL, "flash_attn_ext_static_scratch shapes")
-    if k.stride(2) != 1 or v.stride(2) != 1 or not q.is_contiguous():
-        raise B200Error(EINVAL, "flash_attn_ext_static_scratch needs contiguous q and head dim")
+    hq, d, n_kv, hkv = _check_fa_tensors("flash_attn_ext_static_scratch", q, k, v, mask, kv_lengths, out)
+    if not q.is_contiguous():
+        raise B200Error(EINVAL, "flash_attn_ext_static_scratch needs a contiguous q")
     if out is None:
         out = torch.empty((hq, d), dtype=torch.float32, device=q.device)
     es = k.element_size()

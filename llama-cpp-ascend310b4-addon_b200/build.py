@@ -40,7 +40,12 @@ def nvcc() -> str:
 
 
 def _deps(src: str) -> list[str]:
-    return [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE)]
+    """The source and the headers it may include: host .cpp files see only
+    the .h headers; the device unit (.cu) sees every header."""
+    host = src.endswith(".cpp")
+    own = [os.path.join(CSRC, f) for f in os.listdir(CSRC)
+           if f == src or f.endswith(".h") or (not host and f.endswith(".cuh"))]
+    return own + [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE)]
 
 
 def _compile(src: str, force: bool) -> str:

@@ -46,15 +46,21 @@ __device__ __forceinline__ float4 ld_sys_f4(const float* p) {
 }
 
 // Spins until *flag >= want (flags only grow).  Gives up after
-// kWaitTimeoutNs, records B200_DEVSTATUS_TIMEOUT and returns false.
+// g_wait_timeout_ns, records B200_DEVSTATUS_TIMEOUT and returns false; gives
+// up at once when an earlier wait on this device already expired (a dead
+// peer then costs one limit per step, not one per collective).
 __device__ __forceinline__ bool wait_flag_geq(const unsigned long long* flag, unsigned long long want) {
     if (ld_acquire_sys_u64(flag) >= want) return true;
-    const unsigned long long t0 = globaltimer();
+    if (waits_abandoned()) return false;
+    const unsigned long long t0 = globaltimer(), limit = g_wait_timeout_ns;
     for (uint32_t it = 1;; ++it) {
         if (ld_acquire_sys_u64(flag) >= want) return true;
-        if ((it & 63u) == 0 && globaltimer() - t0 > kWaitTimeoutNs) {
-            record_status(B200_DEVSTATUS_TIMEOUT);
-            return false;
+        if ((it & 63u) == 0) {
+            if (waits_abandoned()) return false;
+            if (globaltimer() - t0 > limit) {
+                record_status(B200_DEVSTATUS_TIMEOUT);
+                return false;
+            }
         }
     }
 }
@@ -62,7 +68,8 @@ __device__ __forceinline__ bool wait_flag_geq(const unsigned long long* flag, un
 __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const ArArgs a) {
     griddep_wait();  // this rank's partial is complete
     griddep_launch_dependents();
-    const unsigned long long seq = a.st->step * (unsigned long long)a.per_step + (unsigned long long)a.idx + 1ull;
+    const unsigned long long seq =
+        a.st != nullptr ? a.st->step * (unsigned long long)a.per_step + (unsigned long long)a.idx + 1ull : a.seq;
     if (blockIdx.x == 0 && threadIdx.x < a.world) {
         __threadfence_system();
         st_release_sys_u64(a.peer_flag[threadIdx.x], seq);

@@ -283,7 +283,8 @@ struct StepState {
 struct ArArgs {
     int world, rank, n;        // ranks, this rank, floats per vector (multiple of 4)
     int idx, per_step;         // collective index within the step, collectives per step
-    const StepState* st;
+    const StepState* st;       // null: the collective's number is `seq`
+    unsigned long long seq;
     float* x;                  // result [n] on this rank
     const float* part[kMaxRanks];                  // rank r's partial [n] (peer mapped)
     unsigned long long* flags;                      // this rank's flags [kMaxRanks]: flags[r] = last seq rank r announced

@@ -17,7 +17,18 @@ namespace b200 {
 // expires or a runtime bound check fails.  Read with b200_device_status().
 __device__ unsigned int g_status;
 
-constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
+// Limit of one bounded wait in nanoseconds (2 s unless b200_set_wait_timeout
+// changed it for this device).
+__device__ unsigned long long g_wait_timeout_ns = 2000000000ull;
+
+// True once any bounded wait on this device has expired (the status word's
+// TIMEOUT bit, read without caching).  Waits that depend on another kernel,
+// CTA or rank then give up at once instead of spinning their full limit
+// again: after a peer dies every later collective of the step returns in
+// microseconds.  Cleared by b200_device_status(..., reset = 1).
+__device__ __forceinline__ bool waits_abandoned() {
+    return (*reinterpret_cast<volatile unsigned int*>(&g_status) & B200_DEVSTATUS_TIMEOUT) != 0u;
+}
 
 __device__ __forceinline__ unsigned long long globaltimer() {
     unsigned long long t;
@@ -56,15 +67,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the mbarrier phase with the given parity.  Gives up after
-// kWaitTimeoutNs, records B200_DEVSTATUS_TIMEOUT and returns false.
+// g_wait_timeout_ns, records B200_DEVSTATUS_TIMEOUT and returns false; gives
+// up at once (false, nothing recorded) when an earlier wait already expired.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer();
+    if (waits_abandoned()) return false;
+    const unsigned long long t0 = globaltimer(), limit = g_wait_timeout_ns;
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0 && globaltimer() - t0 > kWaitTimeoutNs) {
+        if ((it & 255u) == 0) {
+            if (waits_abandoned()) return false;
+            if (globaltimer() - t0 > limit) {
+                atomicOr(&g_status, (unsigned int)B200_DEVSTATUS_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
+// For a CTA that gave up: waits (time-bounded only, never abandoned early)
+// for a bulk copy it issued, so that no copy is still writing into shared
+// memory when the CTA reuses it or exits.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return;
+    const unsigned long long t0 = globaltimer(), limit = g_wait_timeout_ns;
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return;
+        if ((it & 255u) == 0 && globaltimer() - t0 > limit) {
             atomicOr(&g_status, (unsigned int)B200_DEVSTATUS_TIMEOUT);
-            return false;
+            return;
         }
     }
 }

@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
             // a wait expired: let the copies still in flight land before the
             // shared memory is reused or the CTA exits
             for (int cj = ci; cj < ncg && cj < ci + kFmStages; ++cj)
-                mbar_wait_bounded(&bars[cj % kFmStages], (uint32_t)((cj / kFmStages) & 1));
+                mbar_wait_drain(&bars[cj % kFmStages], (uint32_t)((cj / kFmStages) & 1));
         }
     }
 

@@ -145,15 +145,15 @@ __global__ void __launch_bounds__(kSmThreads) gemm_small_m_kernel(const __grid_c
         const int64_t tile = t0 + q / nck;
         const int ch = (int)(q % nck);
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[s], parity))) {
-            if (lane == 0) {  // let the copies in flight land before the CTA exits
+            if (lane == 0) {  // let the copies in flight (stages q .. q + S - 1) land before the CTA exits
                 int s2 = s;
                 uint32_t p2 = parity;
-                for (int64_t q2 = q + 1; q2 < nq && q2 < q + S; ++q2) {
+                for (int64_t q2 = q; q2 < nq && q2 < q + S; ++q2) {
+                    mbar_wait_drain(&bars[s2], p2);
                     if (++s2 == S) {
                         s2 = 0;
                         p2 ^= 1u;
                     }
-                    mbar_wait_bounded(&bars[s2], p2);
                 }
             }
             break;

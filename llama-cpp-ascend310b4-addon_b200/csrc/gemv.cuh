@@ -408,6 +408,32 @@ __device__ __forceinline__ typename GemvTraits<FMT>::Acc chunk_full_dot(const ui
 
 // ------------------------------------------------------------ activation
 
+// ggml rms_norm's sum of squares: every square rounded to f32 (x * x), the
+// sum kept in double (ggml_float); here a per-thread double sum, then warp
+// and CTA sums in double.  Rounded to f32 only as mean = sum / n, as ggml
+// does, so the scale matches ggml-cpu's bit for bit unless the two double
+// sums (different orders, each within ~n * 2^-53 of the exact value)
+// straddle an f32 rounding boundary of the mean.
+__device__ __forceinline__ double sumsq4(float4 v) {
+    return ((double)__fmul_rn(v.x, v.x) + (double)__fmul_rn(v.y, v.y)) +
+           ((double)__fmul_rn(v.z, v.z) + (double)__fmul_rn(v.w, v.w));
+}
+
+// CTA-wide: 1 / sqrtf(mean + eps) with mean = f32(sum / n).  `red` holds
+// kGemvWarps doubles.  Ends with every thread holding the scale.
+__device__ __forceinline__ float rms_scale(double ss, int64_t n, float eps, float* red, int lane, int warp) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    double* rd = reinterpret_cast<double*>(red);
+    if (lane == 0) rd[warp] = ss;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < kGemvWarps; ++w) tot += rd[w];
+    const float mean = __double2float_rn(__ddiv_rn(tot, (double)n));
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
 __device__ __forceinline__ float4 norm_unit(float4 v, float4 w, float nscale) {
     v.x = __fmul_rn(__fmul_rn(v.x, nscale), w.x);
     v.y = __fmul_rn(__fmul_rn(v.y, nscale), w.y);
@@ -439,8 +465,13 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
         const unsigned long long seq =
             a.ar_st->step * (unsigned long long)a.ar_per_step + (unsigned long long)a.ar_idx + 1ull;
         const int nf = a.ar_world * a.ar_grid;
-        for (int i = tid; i < nf; i += kGemvThreads)
-            wait_flag_geq(a.ar_flags + (int64_t)(i / a.ar_grid) * kArMaxCtas + (i % a.ar_grid), seq);
+        bool ok = true;
+        for (int i = tid; i < nf && ok; i += kGemvThreads)
+            ok = wait_flag_geq(a.ar_flags + (int64_t)(i / a.ar_grid) * kArMaxCtas + (i % a.ar_grid), seq);
+        // a flag that never came: the sums below would read partials that
+        // are not there; the quantised image is still written (from
+        // whatever the slots hold) so the kernel's shape of work is kept,
+        // and the status word tells the host that the step is void
         __syncthreads();
     }
     auto ldx = [&](int u) -> float4 {
@@ -470,7 +501,7 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
     after_issue();
     float nscale = 1.f;
     if (norm) {
-        float ss = 0.f;
+        double ss = 0.0;
         for (int r = 0; r < rounds; ++r) {
             float4 t[4];
             const int h = r * kGemvThreads + tid;
@@ -478,22 +509,10 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
             for (int j = 0; j < 4; ++j) t[j] = r == 0 ? xv[j] : ldx(4 * min(h, nh - 1) + j);
             if (h < nh) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    ss = fmaf(t[j].x, t[j].x, ss);
-                    ss = fmaf(t[j].y, t[j].y, ss);
-                    ss = fmaf(t[j].z, t[j].z, ss);
-                    ss = fmaf(t[j].w, t[j].w, ss);
-                }
+                for (int j = 0; j < 4; ++j) ss += sumsq4(t[j]);
             }
         }
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w) tot += red[w];
-        const float mean = __fdiv_rn(tot, (float)a.k);
-        nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        nscale = rms_scale(ss, a.k, a.eps, red, lane, warp);
     }
     uint8_t* xq_out = blockIdx.x == 0 ? a.xq_out : nullptr;
     for (int r = 0; r < rounds; ++r) {
@@ -652,7 +671,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     uint8_t* ring = rings + (int64_t)warp * S * P.stage_bytes;
     uint64_t* bars_all = reinterpret_cast<uint64_t*>(rings + (int64_t)kGemvWarps * S * P.stage_bytes);
     uint64_t* bars = bars_all + warp * S;
-    float* red = reinterpret_cast<float*>(bars_all + kGemvWarps * S);  // [kGemvWarps]
+    float* red = reinterpret_cast<float*>(bars_all + kGemvWarps * S);  // [kGemvWarps] doubles (8-byte aligned)
 
     // ---- work distribution ----
     // rpc > 1 (short rows): every warp owns a contiguous range of row groups
@@ -694,7 +713,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     // Row partials of this CTA (rpc == 1): part0 gets the partial of the warp
     // that holds the row's first chunk, part1 the rest (at most two warps
     // share a row; see the launcher), summed in that order.
-    float* part0 = red + kGemvWarps;
+    float* part0 = red + 2 * kGemvWarps;  // red: kGemvWarps doubles
     float* part1 = part0 + (P.rpc > 1 ? 0 : (cr1 - cr0));
 
     // Lane 0 only: stage the next chunk into ring slot s.  The issue cursor
@@ -801,23 +820,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             for (int s = 1; s < S && s < nq; ++s) issue(s);
         float nscale = 1.f;
         if (norm) {
-            float ss = 0.f;
+            double ss = 0.0;
             const float4* x4 = reinterpret_cast<const float4*>(a.x);
-            for (int64_t i = tid; i < a.k / 4; i += kGemvThreads) {
-                const float4 v = x4[i];
-                ss = fmaf(v.x, v.x, ss);
-                ss = fmaf(v.y, v.y, ss);
-                ss = fmaf(v.z, v.z, ss);
-                ss = fmaf(v.w, v.w, ss);
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) red[warp] = ss;
-            __syncthreads();
-            float tot = 0.f;
-#pragma unroll
-            for (int w = 0; w < kGemvWarps; ++w) tot += red[w];
-            const float mean = __fdiv_rn(tot, (float)a.k);
-            nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+            for (int64_t i = tid; i < a.k / 4; i += kGemvThreads) ss += sumsq4(x4[i]);
+            nscale = rms_scale(ss, a.k, a.eps, red, lane, warp);
         }
         uint4* xh = reinterpret_cast<uint4*>(xr);
         for (int64_t i = tid; i < a.k / 8; i += kGemvThreads) {
@@ -857,14 +863,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[s], parity));
         if (!ok) {
             if (lane == 0) {
+                // let every copy this warp issued (stages q .. q + S - 1) land
+                // before the shared memory is reused or the CTA exits
                 int s2 = s;
                 uint32_t p2 = parity;
-                for (int64_t q2 = q + 1; q2 < nq && q2 < q + S; ++q2) {
+                for (int64_t q2 = q; q2 < nq && q2 < q + S; ++q2) {
+                    mbar_wait_drain(&bars[s2], p2);
                     if (++s2 == S) {
                         s2 = 0;
                         p2 ^= 1u;
                     }
-                    mbar_wait_bounded(&bars[s2], p2);
                 }
             }
             break;  // the status word records the timeout; still meet the CTA barrier below

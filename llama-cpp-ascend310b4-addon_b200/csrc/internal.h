@@ -27,3 +27,6 @@ int b200i_fill_f32(float* p, int64_t n, float v, cudaStream_t st);
 int b200i_embed(const void* table, int64_t d_model, int64_t vocab, b200::StepState* state, float* x,
                 cudaStream_t st);
 int b200i_finish(b200::StepState* state, cudaStream_t st);
+// A quantised-activation image (GemvArgs::xq_in layout, U blocks) as ggml
+// block_q8_0 rows (U x 34 bytes).
+int b200i_image_to_q8_0(const uint8_t* img, int64_t U, uint8_t* out, cudaStream_t st);

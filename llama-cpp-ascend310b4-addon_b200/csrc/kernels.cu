@@ -119,7 +119,7 @@ int set_gemv_attrs(int dev) {
 // `stages` chunks, their barriers, and a small reduction scratch.
 size_t gemv_smem_bytes(int fmt, const GemvPlan& p, int stages, int64_t rows_per_cta) {
     return (size_t)gemv_x_bytes(fmt, p) + (size_t)kGemvWarps * stages * (size_t)p.stage_bytes +
-           (size_t)kGemvWarps * stages * sizeof(uint64_t) + kGemvWarps * sizeof(float) +
+           (size_t)kGemvWarps * stages * sizeof(uint64_t) + kGemvWarps * sizeof(double) +
            (p.rpc > 1 ? 0 : (size_t)(2 * rows_per_cta) * sizeof(float));
 }
 
@@ -536,6 +536,12 @@ int b200i_embed(const void* table, int64_t d_model, int64_t vocab, StepState* st
     return cuda_status(cudaGetLastError());
 }
 
+int b200i_image_to_q8_0(const uint8_t* img, int64_t U, uint8_t* out, cudaStream_t st) {
+    if (U <= 0) return B200_OK;
+    image_to_q8_0_kernel<<<grid_for(U, 128), 128, 0, st>>>(img, U, out);
+    return cuda_status(cudaGetLastError());
+}
+
 int b200i_finish(StepState* state, cudaStream_t st) {
     finish_step_kernel<<<1, 1, 0, st>>>(state);
     return cuda_status(cudaGetLastError());
@@ -559,6 +565,35 @@ const char* b200_strerror(int code) {
         case B200_ESCRATCH: return "request exceeds the fixed static scratch (B200_FA_STATIC_SCRATCH_BYTES)";
         default: return "unknown status";
     }
+}
+
+int b200_set_wait_timeout(uint64_t ns) {
+    const unsigned long long v = ns == 0 ? 2000000000ull : (unsigned long long)ns;
+    return cuda_status(cudaMemcpyToSymbol(g_wait_timeout_ns, &v, sizeof(v)));
+}
+
+int b200_tp_allreduce_f32(float* x, const float* const* parts, int world, int rank, int64_t n,
+                          unsigned long long* flags, unsigned long long* const* peer_flags, uint64_t seq,
+                          b200_stream_t stream) {
+    if (!x || !parts || !flags || !peer_flags || world < 1 || world > kMaxRanks || rank < 0 || rank >= world ||
+        n <= 0 || (n & 3) || n > (int64_t)1 << 30 || seq == 0)
+        return B200_EINVAL;
+    if (!aligned16(x)) return B200_EINVAL;
+    ArArgs a;
+    memset(&a, 0, sizeof(a));
+    a.world = world;
+    a.rank = rank;
+    a.n = (int)n;
+    a.st = nullptr;
+    a.seq = (unsigned long long)seq;
+    a.x = x;
+    a.flags = flags;
+    for (int r = 0; r < world; ++r) {
+        if (!parts[r] || !peer_flags[r] || !aligned16(parts[r])) return B200_EINVAL;
+        a.part[r] = parts[r];
+        a.peer_flag[r] = peer_flags[r];
+    }
+    return b200i_tp_allreduce(a, (cudaStream_t)stream, false);
 }
 
 int b200_device_status(unsigned int* status, int reset) {
@@ -882,19 +917,43 @@ namespace {
 
 std::mutex g_static_scratch_mu;
 unsigned char* g_static_scratch_dev[kMaxDevices];
+CUcontext g_static_scratch_ctx[kMaxDevices];
+
+// The calling thread's current CUDA context (driver entry point through the
+// runtime, so the library needs no link against the driver library).
+CUcontext current_context() {
+    using Fn = CUresult (*)(CUcontext*);
+    static const Fn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<Fn>(p);
+    }();
+    CUcontext c = nullptr;
+    if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
 
 // Device address of g_fa_static_scratch on the current device, looked up on
-// the first call there (with that device current) and cached.
+// the first call there (with that device current) and cached with the
+// context it belongs to: after a cudaDeviceReset the device's next primary
+// context loads the module again, so a call in a different context than
+// the cached one looks the address up again.
 int static_scratch(unsigned char** out) {
     int dev = -1;
     CR_(cuda_status(cudaGetDevice(&dev)));
     if (dev < 0 || dev >= kMaxDevices) return B200_EINVAL;
+    CR_(cuda_status(cudaFree(nullptr)));  // makes the device's primary context current (allocates nothing)
+    const CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lk(g_static_scratch_mu);
-    if (g_static_scratch_dev[dev] == nullptr) {
+    if (g_static_scratch_dev[dev] == nullptr || ctx == nullptr || g_static_scratch_ctx[dev] != ctx) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_fa_static_scratch);
         if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? cuda_status(e) : B200_ECUDA;
         g_static_scratch_dev[dev] = static_cast<unsigned char*>(p);
+        g_static_scratch_ctx[dev] = ctx;
     }
     *out = g_static_scratch_dev[dev];
     return B200_OK;

@@ -147,10 +147,39 @@ struct b200_model {
 
 namespace {
 
+// Host-side fault injection for failure-detection tests (no GPU fault is
+// ever made): B200_INJECT_FAULT=nccl_init makes the communicator set-up
+// report an NCCL failure instead of calling NCCL; =alloc:N makes the N-th
+// device allocation of b200_model_create report cudaErrorMemoryAllocation.
+// Read once per b200_model_create.
+struct FaultPlan {
+    bool nccl_init = false;
+    long alloc_at = -1;  // 1-based index of the allocation that fails
+    long allocs = 0;
+};
+
+FaultPlan fault_plan() {
+    FaultPlan f;
+    if (const char* e = getenv("B200_INJECT_FAULT")) {
+        if (std::strcmp(e, "nccl_init") == 0) f.nccl_init = true;
+        if (std::strncmp(e, "alloc:", 6) == 0) f.alloc_at = atol(e + 6);
+    }
+    return f;
+}
+
+thread_local FaultPlan* t_fault = nullptr;
+
 int dalloc(b200_model* m, void** p, size_t bytes) {
     if (bytes == 0) bytes = 16;
-    cudaError_t e = cudaMalloc(p, bytes);
+    cudaError_t e;
+    if (t_fault != nullptr && ++t_fault->allocs == t_fault->alloc_at) {
+        e = cudaErrorMemoryAllocation;
+        *p = nullptr;
+    } else {
+        e = cudaMalloc(p, bytes);
+    }
     if (e != cudaSuccess) {
+        cudaGetLastError();  // a failed allocation is reported here, not by the next launch check
         fprintf(stderr, "b200_model: cudaMalloc(%zu) failed: %s\n", bytes, cudaGetErrorString(e));
         return B200_ENOMEM;
     }
@@ -229,10 +258,19 @@ int allreduce_sum(b200_model* m, int which, int idx, cudaStream_t s, bool pdl) {
     return b200i_tp_allreduce(a, s, pdl);
 }
 
+// Device buffers of a layer dump (b200_step_dump, same shapes); any may be
+// null.  Q8_0 images are ggml block_q8_0 rows.
 struct Dump {
-    float* x = nullptr;    // device [(n_layer + 1) * d]
-    float* q = nullptr;    // device [n_layer * hq * D]
-    float* att = nullptr;  // device [n_layer * hq * D]
+    float* x = nullptr;      // [(n_layer + 1) * d]
+    float* x_mid = nullptr;  // [n_layer * d]
+    float* q = nullptr;      // [n_layer * hq * D]
+    uint16_t* k_row = nullptr;
+    uint16_t* v_row = nullptr;  // [n_layer * hkv * D]
+    float* att = nullptr;    // [n_layer * hq * D]
+    float* h = nullptr;      // [n_layer * ff]
+    uint8_t *xq_qkv = nullptr, *xq_o = nullptr, *xq_gu = nullptr, *xq_down = nullptr, *xq_head = nullptr;
+    int32_t *dots_qkv = nullptr, *dots_o = nullptr, *dots_gu = nullptr, *dots_down = nullptr, *dots_head = nullptr;
+    int pos = 0;
 };
 
 // Producer-side quantisation (see b200_model::xq_fused): the SwiGLU
@@ -412,42 +450,98 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
     CR(E());
 
     const size_t qbytes = (size_t)m->hq * D * sizeof(float);
-    if (dump) CK(cudaMemcpyAsync(dump->x, m->x, c.d_model * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    const int64_t qd = (int64_t)m->hq * D, kvd = (int64_t)m->hkv * D, d = c.d_model;
+    // Layer-dump hooks: the GEMV's own prologue image (CTA 0) and its
+    // per-block dots (the export variant of the same kernel), or a copy of
+    // the producer-written image the GEMV reads.
+    auto dcopy = [&](void* dst, const void* src, size_t bytes) {
+        return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s);
+    };
+    auto hook = [&](GemvArgs& a, uint8_t* xq, int32_t* dots) {
+        if (xq != nullptr && a.xq_in == nullptr) a.xq_out = xq;
+        if (dots != nullptr) a.dots = dots;
+        return dots != nullptr;
+    };
+    auto image_out = [&](const uint8_t* img, uint8_t* xq, int64_t k) -> int {
+        return b200i_image_to_q8_0(img, k / 32, xq, s);
+    };
+    if (dump && dump->x) CK(dcopy(dump->x, m->x, d * sizeof(float)));
     for (int l = 0; l < c.n_layer; ++l) {
         CR(B(1));
-        CR(b200i_gemv(FMT_Q4, qkv_args(m, l), false, s, pdl));
+        {
+            GemvArgs a = qkv_args(m, l);
+            bool dbg = false;
+            if (dump)
+                dbg = hook(a, dump->xq_qkv ? dump->xq_qkv + (size_t)l * (d / 32) * 34 : nullptr,
+                           dump->dots_qkv ? dump->dots_qkv + (size_t)l * m->qkv_rows * (d / 32) : nullptr);
+            CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
+        }
         CR(E());
-        if (dump) CK(cudaMemcpyAsync(dump->q + (size_t)l * m->hq * D, m->q, qbytes, cudaMemcpyDeviceToDevice, s));
+        if (dump) {
+            if (dump->q) CK(dcopy(dump->q + (size_t)l * qd, m->q, qbytes));
+            const size_t off = (size_t)dump->pos * kvd;
+            if (dump->k_row) CK(dcopy(dump->k_row + (size_t)l * kvd, m->L[l].kc + off, kvd * 2));
+            if (dump->v_row) CK(dcopy(dump->v_row + (size_t)l * kvd, m->L[l].vc + off, kvd * 2));
+        }
         CR(B(2));
         CR(b200i_fa(fa_args(m, l), D, s, pdl));
         CR(E());
-        if (dump)
-            CK(cudaMemcpyAsync(dump->att + (size_t)l * m->hq * D, m->att, qbytes, cudaMemcpyDeviceToDevice, s));
+        if (dump && dump->att) CK(dcopy(dump->att + (size_t)l * qd, m->att, qbytes));
         CR(B(3));
-        CR(b200i_gemv(FMT_Q4, proj_args(m, l, 0), false, s, pdl));
+        {
+            GemvArgs a = proj_args(m, l, 0);
+            bool dbg = false;
+            if (dump) {
+                uint8_t* xq = dump->xq_o ? dump->xq_o + (size_t)l * (qd / 32) * 34 : nullptr;
+                if (xq && a.xq_in) CR(image_out(a.xq_in, xq, qd));
+                dbg = hook(a, xq, dump->dots_o ? dump->dots_o + (size_t)l * d * (qd / 32) : nullptr);
+            }
+            CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
+        }
         CR(E());
         if (m->world > 1 && !m->ar_now) {
             CR(B(7));
             CR(allreduce_sum(m, 0, 2 * l, s, pdl));
             CR(E());
         }
+        if (dump && dump->x_mid) CK(dcopy(dump->x_mid + (size_t)l * d, m->x, d * sizeof(float)));
         CR(B(4));
-        CR(b200i_gemv(FMT_Q4, gate_up_args(m, l), false, s, pdl));
+        {
+            GemvArgs a = gate_up_args(m, l);
+            bool dbg = false;
+            if (dump)
+                dbg = hook(a, dump->xq_gu ? dump->xq_gu + (size_t)l * (d / 32) * 34 : nullptr,
+                           dump->dots_gu ? dump->dots_gu + (size_t)l * 2 * m->ff * (d / 32) : nullptr);
+            CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
+        }
         CR(E());
+        if (dump && dump->h) CK(dcopy(dump->h + (size_t)l * m->ff, m->h, (size_t)m->ff * sizeof(float)));
         CR(B(5));
-        CR(b200i_gemv(FMT_Q4, proj_args(m, l, 1), false, s, pdl));
+        {
+            GemvArgs a = proj_args(m, l, 1);
+            bool dbg = false;
+            if (dump) {
+                uint8_t* xq = dump->xq_down ? dump->xq_down + (size_t)l * (m->ff / 32) * 34 : nullptr;
+                if (xq && a.xq_in) CR(image_out(a.xq_in, xq, m->ff));
+                dbg = hook(a, xq, dump->dots_down ? dump->dots_down + (size_t)l * d * (m->ff / 32) : nullptr);
+            }
+            CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
+        }
         CR(E());
         if (m->world > 1 && !m->ar_now) {
             CR(B(7));
             CR(allreduce_sum(m, 1, 2 * l + 1, s, pdl));
             CR(E());
         }
-        if (dump)
-            CK(cudaMemcpyAsync(dump->x + (size_t)(l + 1) * c.d_model, m->x, c.d_model * sizeof(float),
-                               cudaMemcpyDeviceToDevice, s));
+        if (dump && dump->x) CK(dcopy(dump->x + (size_t)(l + 1) * d, m->x, d * sizeof(float)));
     }
     CR(B(6));
-    CR(b200i_gemv(FMT_Q4, head_args(m), false, s, pdl));
+    {
+        GemvArgs a = head_args(m);
+        bool dbg = false;
+        if (dump) dbg = hook(a, dump->xq_head, dump->dots_head);
+        CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
+    }
     CR(E());
     if (m->world > 1) {
         CR(B(7));
@@ -469,7 +563,10 @@ int setup_comm_region(b200_model* m) {
     m->recv_off = m->flags_off + 256;  // fused all-reduce: receive slots [2][world][d], flags [kMaxRanks][kArMaxCtas]
     m->fflags_off = m->recv_off + 2 * (size_t)m->world * m->part_stride;
     const size_t bytes = m->fflags_off + (size_t)kMaxRanks * kArMaxCtas * sizeof(unsigned long long);
-    if (cudaMalloc(reinterpret_cast<void**>(&m->comm_region), bytes) != cudaSuccess) return B200_ENOMEM;
+    if (cudaMalloc(reinterpret_cast<void**>(&m->comm_region), bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return B200_ENOMEM;
+    }
     CK(cudaMemset(m->comm_region, 0, bytes));
     if (!m->peer_ar) return B200_OK;
     cudaIpcMemHandle_t mine;
@@ -547,10 +644,20 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
         return r;
     };
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(B200_ECUDA);
+    FaultPlan fp = fault_plan();
+    t_fault = &fp;
+    struct Reset {
+        ~Reset() { t_fault = nullptr; }
+    } reset_fault;
     if (tp_world > 1) {
         ncclUniqueId id;
         std::memcpy(&id, nccl_id128, sizeof(id));
-        if (ncclCommInitRank(&m->comm, tp_world, id, tp_rank) != ncclSuccess) return fail(B200_ENCCL);
+        const ncclResult_t nr = fp.nccl_init ? ncclSystemError : ncclCommInitRank(&m->comm, tp_world, id, tp_rank);
+        if (nr != ncclSuccess) {
+            fprintf(stderr, "b200_model: NCCL communicator set-up failed: %s\n", ncclGetErrorString(nr));
+            m->comm = nullptr;
+            return fail(B200_ENCCL);
+        }
     }
     if (const char* e = getenv("B200_TP_ALLREDUCE")) {
         m->peer_ar = std::strcmp(e, "nccl") != 0;
@@ -805,17 +912,46 @@ int b200_model_step_bytes(b200_model* m, int ctx, uint64_t* bytes) {
     return B200_OK;
 }
 
-int b200_model_debug_step(b200_model* m, int token, int pos, float* x_host, float* q_host, float* att_host) {
-    if (!m || !x_host || pos < 0 || pos >= m->c.kv_size || token < 0 || token >= m->c.vocab) return B200_EINVAL;
+int b200_model_debug_step_ex(b200_model* m, int token, int pos, const b200_step_dump* hd) {
+    if (!m || !hd || pos < 0 || pos >= m->c.kv_size || token < 0 || token >= m->c.vocab) return B200_EINVAL;
     CK(cudaSetDevice(m->device));
     CR(b200i_prepare_device());
     const b200_llama_config& c = m->c;
-    const size_t nx = (size_t)(c.n_layer + 1) * c.d_model, nq = (size_t)c.n_layer * m->hq * c.head_dim;
-    Dump d;
-    CK(cudaMalloc(&d.x, nx * sizeof(float)));
-    cudaError_t e1 = cudaMalloc(&d.q, nq * sizeof(float));
-    cudaError_t e2 = cudaMalloc(&d.att, nq * sizeof(float));
-    int rc = (e1 == cudaSuccess && e2 == cudaSuccess) ? B200_OK : B200_ENOMEM;
+    const size_t L = (size_t)c.n_layer, d = (size_t)c.d_model, qd = (size_t)m->hq * c.head_dim,
+                 kvd = (size_t)m->hkv * c.head_dim, ff = (size_t)m->ff;
+    // (host pointer, device pointer slot, bytes) of every requested part
+    struct Part {
+        void* host;
+        void** dev;
+        size_t bytes;
+    };
+    Dump dd;
+    dd.pos = pos;
+    const Part parts[] = {
+        {hd->x, (void**)&dd.x, (L + 1) * d * 4},
+        {hd->x_mid, (void**)&dd.x_mid, L * d * 4},
+        {hd->q, (void**)&dd.q, L * qd * 4},
+        {hd->k_row, (void**)&dd.k_row, L * kvd * 2},
+        {hd->v_row, (void**)&dd.v_row, L * kvd * 2},
+        {hd->att, (void**)&dd.att, L * qd * 4},
+        {hd->h, (void**)&dd.h, L * ff * 4},
+        {hd->xq_qkv, (void**)&dd.xq_qkv, L * (d / 32) * 34},
+        {hd->xq_o, (void**)&dd.xq_o, L * (qd / 32) * 34},
+        {hd->xq_gu, (void**)&dd.xq_gu, L * (d / 32) * 34},
+        {hd->xq_down, (void**)&dd.xq_down, L * (ff / 32) * 34},
+        {hd->xq_head, (void**)&dd.xq_head, (d / 32) * 34},
+        {hd->dots_qkv, (void**)&dd.dots_qkv, L * (size_t)m->qkv_rows * (d / 32) * 4},
+        {hd->dots_o, (void**)&dd.dots_o, L * d * (qd / 32) * 4},
+        {hd->dots_gu, (void**)&dd.dots_gu, L * 2 * ff * (d / 32) * 4},
+        {hd->dots_down, (void**)&dd.dots_down, L * d * (ff / 32) * 4},
+        {hd->dots_head, (void**)&dd.dots_head, (size_t)m->voc * (d / 32) * 4},
+    };
+    int rc = B200_OK;
+    for (const Part& p : parts)
+        if (rc == B200_OK && p.host != nullptr && cudaMalloc(p.dev, p.bytes) != cudaSuccess) {
+            cudaGetLastError();
+            rc = B200_ENOMEM;
+        }
     if (rc == B200_OK) {
         m->h_st->token = token;
         m->h_st->pos = pos;
@@ -824,19 +960,28 @@ int b200_model_debug_step(b200_model* m, int token, int pos, float* x_host, floa
         if (cudaMemcpyAsync(m->st, m->h_st, 4 * sizeof(int), cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
             rc = B200_ECUDA;
     }
-    if (rc == B200_OK) rc = enqueue_step(m, m->stream, nullptr, &d);
+    if (rc == B200_OK) rc = enqueue_step(m, m->stream, nullptr, &dd);
     if (rc == B200_OK && cudaStreamSynchronize(m->stream) != cudaSuccess) rc = B200_ECUDA;
-    if (rc == B200_OK && cudaMemcpy(x_host, d.x, nx * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+    for (const Part& p : parts)
+        if (rc == B200_OK && p.host != nullptr &&
+            cudaMemcpy(p.host, *p.dev, p.bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = B200_ECUDA;
+    if (rc == B200_OK && hd->logits != nullptr &&
+        cudaMemcpy(hd->logits, m->logits, (size_t)m->voc * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
         rc = B200_ECUDA;
-    if (rc == B200_OK && q_host && cudaMemcpy(q_host, d.q, nq * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
-        rc = B200_ECUDA;
-    if (rc == B200_OK && att_host &&
-        cudaMemcpy(att_host, d.att, nq * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
-        rc = B200_ECUDA;
-    cudaFree(d.x);
-    if (d.q) cudaFree(d.q);
-    if (d.att) cudaFree(d.att);
+    for (const Part& p : parts)
+        if (*p.dev != nullptr) cudaFree(*p.dev);
     return rc;
+}
+
+int b200_model_debug_step(b200_model* m, int token, int pos, float* x_host, float* q_host, float* att_host) {
+    if (!x_host) return B200_EINVAL;
+    b200_step_dump d;
+    std::memset(&d, 0, sizeof(d));
+    d.x = x_host;
+    d.q = q_host;
+    d.att = att_host;
+    return b200_model_debug_step_ex(m, token, pos, &d);
 }
 
 int b200_model_profile(b200_model* m, int iters, float* us) {

@@ -104,6 +104,22 @@ __global__ void embed_kernel(const uint8_t* table, int64_t d_model, int64_t voca
     }
 }
 
+// Image -> ggml block_q8_0: block b's q bytes 0..15 from plane 0, 16..31
+// from plane 1, its scale from the f32 copy of the f16 value (exact).
+__global__ void image_to_q8_0_kernel(const uint8_t* img, int64_t U, uint8_t* out) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= U) return;
+    const float d = __int_as_float(reinterpret_cast<const int2*>(img + 32 * U)[b].x);
+    uint8_t* o = out + b * 34;
+    const uint16_t dh = f2h(d);
+    o[0] = (uint8_t)(dh & 0xff);
+    o[1] = (uint8_t)(dh >> 8);
+    for (int i = 0; i < 16; ++i) {
+        o[2 + i] = img[16 * b + i];
+        o[18 + i] = img[16 * U + 16 * b + i];
+    }
+}
+
 __global__ void finish_step_kernel(StepState* st) {
     const unsigned long long a = st->amax;
     const int idx = (int)(0xffffffffu - (unsigned int)(a & 0xffffffffull));

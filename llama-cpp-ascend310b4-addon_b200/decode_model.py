@@ -46,6 +46,14 @@ class _Cfg(C.Structure):
                 ("rope_theta", C.c_float), ("rms_eps", C.c_float)]
 
 
+class _StepDump(C.Structure):
+    _fields_ = [(name, C.c_void_p) for name in (
+        "x", "x_mid", "q", "k_row", "v_row", "att", "h", "logits", "xq_qkv", "xq_o", "xq_gu", "xq_down", "xq_head",
+        "dots_qkv", "dots_o", "dots_gu", "dots_down", "dots_head")]
+
+
+DUMP_PARTS = [f for f, _ in _StepDump._fields_]
+
 _declared = False
 
 
@@ -72,6 +80,7 @@ def _lib():
             "b200_model_profile": (C.c_int, [P, C.c_int, P]),
             "b200_model_time_gate_up": (C.c_int, [P, C.c_int, C.POINTER(C.c_float)]),
             "b200_model_debug_step": (C.c_int, [P, C.c_int, C.c_int, P, P, P]),
+            "b200_model_debug_step_ex": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(_StepDump)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -185,6 +194,37 @@ class DecodeModel:
                  "debug_step")
         return x, q, a
 
+    def dump_step(self, token: int, pos: int, parts=None) -> dict:
+        """Full layer dump of one eager step (b200_model_debug_step_ex):
+        every stage output and every Q8_0 activation (ggml block_q8_0 bytes)
+        and per-block int32 dot array the step's GEMVs used.  `parts` names
+        the entries to fetch (default: all of DUMP_PARTS)."""
+        c = self.cfg
+        w = self.tp_world
+        L, d, D = c.n_layer, c.d_model, c.head_dim
+        hq, hkv, ff, voc = c.n_head // w, c.n_head_kv // w, c.d_ff // w, c.vocab // w
+        qd, kvd = hq * D, hkv * D
+        qkv_rows = qd + 2 * kvd
+        shapes = {
+            "x": ((L + 1, d), np.float32), "x_mid": ((L, d), np.float32), "q": ((L, qd), np.float32),
+            "k_row": ((L, kvd), np.float16), "v_row": ((L, kvd), np.float16), "att": ((L, qd), np.float32),
+            "h": ((L, ff), np.float32), "logits": ((voc,), np.float32),
+            "xq_qkv": ((L, d // 32 * 34), np.uint8), "xq_o": ((L, qd // 32 * 34), np.uint8),
+            "xq_gu": ((L, d // 32 * 34), np.uint8), "xq_down": ((L, ff // 32 * 34), np.uint8),
+            "xq_head": ((d // 32 * 34,), np.uint8),
+            "dots_qkv": ((L, qkv_rows, d // 32), np.int32), "dots_o": ((L, d, qd // 32), np.int32),
+            "dots_gu": ((L, 2 * ff, d // 32), np.int32), "dots_down": ((L, d, ff // 32), np.int32),
+            "dots_head": ((voc, d // 32), np.int32),
+        }
+        want = DUMP_PARTS if parts is None else list(parts)
+        out, sd = {}, _StepDump()
+        for name in want:
+            shape, dt = shapes[name]
+            out[name] = np.empty(shape, dtype=dt)
+            setattr(sd, name, out[name].ctypes.data_as(C.c_void_p).value)
+        B._check(_lib().b200_model_debug_step_ex(self.h, token, pos, C.byref(sd)), "debug_step_ex")
+        return out
+
     def time_gate_up(self, iters: int = 5) -> float:
         """us per gate/up GEMV launch, from a graph of the step's n_layer
         gate/up launches (overwrites the step's SwiGLU scratch)."""
@@ -211,27 +251,3 @@ def oracle_weights(model: DecodeModel):
     w["ffn_norm"] = [np.ones(cfg.d_model, np.float32) for _ in range(L)]
     w["out_norm"] = np.ones(cfg.d_model, np.float32)
     return w
-
-
-def smoke_step():
-    """Two-layer, small-width model: one decode step against the oracle."""
-    import oracle as O
-
-    cfg = LlamaConfig(n_layer=2, d_model=512, n_head=8, n_head_kv=2, head_dim=64, d_ff=1024, vocab=1024,
-                      kv_size=64)
-    m = DecodeModel(cfg)
-    m.init_synthetic(seed=7, sigma=0.02)
-    m.fill_kv_synthetic(seed=9, n_pos=16)
-    kvd = cfg.n_head_kv * cfg.head_dim
-    kc = [np.zeros((cfg.kv_size, kvd), np.float16) for _ in range(cfg.n_layer)]
-    vc = [np.zeros((cfg.kv_size, kvd), np.float16) for _ in range(cfg.n_layer)]
-    for l in range(cfg.n_layer):
-        kc[l][:16] = m.export_kv(l, 0, 16)
-        vc[l][:16] = m.export_kv(l, 1, 16)
-    ref = O.OracleLlama(cfg.as_dict(), oracle_weights(m), kc, vc)
-    tok, logits = m.decode(5, 16, want_logits=True)
-    ref_tok = ref.step(5, 16)
-    d = np.abs(logits - ref.logits).max() / np.abs(ref.logits).max()
-    if d > 1e-3:
-        raise AssertionError(f"decode-step logits differ: {d:.3e}")
-    m.close()

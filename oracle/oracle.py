@@ -60,6 +60,8 @@ def _declare(L):
         "ref_mul_mat_q4_0": (None, [P, P, P, I64, I64, I32, I32]),
         "ref_mul_mat_q8_0": (None, [P, P, P, I64, I64, I32]),
         "ref_block_dots_q4_0": (None, [P, P, P, I64, I64]),
+        "ref_mul_mat_q4_0_xq": (None, [P, P, P, I64, I64, I32]),
+        "ref_block_dots_q4_0_xq": (None, [P, P, P, I64, I64]),
         "ref_block_dots_q8_0": (None, [P, P, P, I64, I64]),
         "ref_flash_attn_ext_decode": (
             None,
@@ -168,6 +170,45 @@ def block_dots(fmt: str, w_blocks: np.ndarray, x: np.ndarray) -> np.ndarray:
     fn = lib().ref_block_dots_q4_0 if fmt == "q4_0" else lib().ref_block_dots_q8_0
     fn(_p(w_blocks), _p(x), _p(dots), n, k)
     return dots
+
+
+def mul_mat_q4_0_xq(w_blocks: np.ndarray, xq_blocks: np.ndarray, nthreads: int = 0) -> np.ndarray:
+    """Q4_0 x Q8_0 MUL_MAT from given Q8_0 activation blocks (ggml-cpu after
+    its src1 conversion): f32 [N]."""
+    w_blocks = np.ascontiguousarray(w_blocks, dtype=np.uint8)
+    xq_blocks = np.ascontiguousarray(xq_blocks, dtype=np.uint8)
+    k = xq_blocks.size // Q8_0_BLOCK_BYTES * QK
+    n = w_blocks.size // (k // QK * Q4_0_BLOCK_BYTES)
+    y = np.empty(n, dtype=np.float32)
+    lib().ref_mul_mat_q4_0_xq(_p(w_blocks), _p(xq_blocks), _p(y), n, k, nthreads)
+    return y
+
+
+def block_dots_q4_0_xq(w_blocks: np.ndarray, xq_blocks: np.ndarray) -> np.ndarray:
+    """int32 [N, K/32] dots of Q4_0 rows with given Q8_0 activation blocks."""
+    w_blocks = np.ascontiguousarray(w_blocks, dtype=np.uint8)
+    xq_blocks = np.ascontiguousarray(xq_blocks, dtype=np.uint8)
+    k = xq_blocks.size // Q8_0_BLOCK_BYTES * QK
+    n = w_blocks.size // (k // QK * Q4_0_BLOCK_BYTES)
+    dots = np.empty((n, k // QK), dtype=np.int32)
+    lib().ref_block_dots_q4_0_xq(_p(w_blocks), _p(xq_blocks), _p(dots), n, k)
+    return dots
+
+
+def rms_norm_mul(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """ggml RMS_NORM (squares in f32, sum in double) followed by MUL."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().ref_rms_norm_mul(_p(x), _p(w), _p(y), x.size, C.c_float(eps))
+    return y
+
+
+def rope_norm(x: np.ndarray, n_heads: int, head_dim: int, pos: int, theta: float) -> np.ndarray:
+    """ggml ROPE (NORM mode) of [n_heads * head_dim] f32 at one position."""
+    y = np.ascontiguousarray(x, dtype=np.float32).copy()
+    lib().ref_rope_norm(_p(y), n_heads, head_dim, pos, C.c_float(theta))
+    return y
 
 
 # -------------------------------------------------------------- attention

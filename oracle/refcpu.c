@@ -223,6 +223,34 @@ void ref_mul_mat_f16(const uint16_t *w, const float *x, float *y, int64_t n, int
     free(xh);
 }
 
+/* ggml-cpu Q4_0 x F32 after src1 has been converted to Q8_0 blocks (the
+ * vec_dot_type of Q4_0): y[r] = sum_b d_w * d_x * dot_b.  Takes the Q8_0
+ * activation as given, so a test can feed the bytes a GPU kernel used. */
+void ref_mul_mat_q4_0_xq(const void *wv, const void *xqv, float *y, int64_t n, int64_t k, int nthreads) {
+    f16_table_init();
+    const ref_block_q4_0 *w = (const ref_block_q4_0 *)wv;
+    const ref_block_q8_0 *xq = (const ref_block_q8_0 *)xqv;
+    const int64_t nb = k / REF_QK;
+    const int nt = pick_threads(nthreads);
+    float *xd = (float *)malloc(sizeof(float) * (size_t)nb);
+    for (int64_t b = 0; b < nb; ++b) xd[b] = h2f(xq[b].d);
+#pragma omp parallel for num_threads(nt) schedule(static)
+    for (int64_t r = 0; r < n; ++r) {
+        const ref_block_q4_0 *row = w + r * nb;
+        double acc = 0.0;
+        float accf = 0.0f;
+        for (int64_t b = 0; b < nb; ++b) {
+            const int32_t s = ref_dot_block_q4_0_q8_0(row + b, xq + b);
+            if (g_accum_mode == 0)
+                acc += (double)(h2f(row[b].d) * xd[b]) * (double)s;
+            else
+                accf += (h2f(row[b].d) * xd[b]) * (float)s;
+        }
+        y[r] = g_accum_mode == 0 ? (float)acc : accf;
+    }
+    free(xd);
+}
+
 void ref_mul_mat_q4_0(const void *wv, const float *x, float *y, int64_t n, int64_t k, int mode, int nthreads) {
     f16_table_init();
     const ref_block_q4_0 *w = (const ref_block_q4_0 *)wv;
@@ -231,23 +259,7 @@ void ref_mul_mat_q4_0(const void *wv, const float *x, float *y, int64_t n, int64
     if (mode == 0) {
         ref_block_q8_0 *xq = (ref_block_q8_0 *)malloc(sizeof(ref_block_q8_0) * (size_t)nb);
         ref_quantize_q8_0(x, xq, k);
-        float *xd = (float *)malloc(sizeof(float) * (size_t)nb);
-        for (int64_t b = 0; b < nb; ++b) xd[b] = h2f(xq[b].d);
-#pragma omp parallel for num_threads(nt) schedule(static)
-        for (int64_t r = 0; r < n; ++r) {
-            const ref_block_q4_0 *row = w + r * nb;
-            double acc = 0.0;
-            float accf = 0.0f;
-            for (int64_t b = 0; b < nb; ++b) {
-                const int32_t s = ref_dot_block_q4_0_q8_0(row + b, xq + b);
-                if (g_accum_mode == 0)
-                    acc += (double)(h2f(row[b].d) * xd[b]) * (double)s;
-                else
-                    accf += (h2f(row[b].d) * xd[b]) * (float)s;
-            }
-            y[r] = g_accum_mode == 0 ? (float)acc : accf;
-        }
-        free(xd);
+        ref_mul_mat_q4_0_xq(wv, xq, y, n, k, nthreads);
         free(xq);
     } else {
         float *xh = (float *)malloc(sizeof(float) * (size_t)k);
@@ -294,13 +306,21 @@ void ref_mul_mat_q8_0(const void *wv, const float *x, float *y, int64_t n, int64
     free(xq);
 }
 
-void ref_block_dots_q4_0(const void *wv, const float *x, int32_t *dots, int64_t n, int64_t k) {
+/* Per-(row, 32-block) int32 dots of Q4_0 rows with given Q8_0 blocks. */
+void ref_block_dots_q4_0_xq(const void *wv, const void *xqv, int32_t *dots, int64_t n, int64_t k) {
     const ref_block_q4_0 *w = (const ref_block_q4_0 *)wv;
+    const ref_block_q8_0 *xq = (const ref_block_q8_0 *)xqv;
+    const int64_t nb = k / REF_QK;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < n; ++r)
+        for (int64_t b = 0; b < nb; ++b) dots[r * nb + b] = ref_dot_block_q4_0_q8_0(w + r * nb + b, xq + b);
+}
+
+void ref_block_dots_q4_0(const void *wv, const float *x, int32_t *dots, int64_t n, int64_t k) {
     const int64_t nb = k / REF_QK;
     ref_block_q8_0 *xq = (ref_block_q8_0 *)malloc(sizeof(ref_block_q8_0) * (size_t)nb);
     ref_quantize_q8_0(x, xq, k);
-    for (int64_t r = 0; r < n; ++r)
-        for (int64_t b = 0; b < nb; ++b) dots[r * nb + b] = ref_dot_block_q4_0_q8_0(w + r * nb + b, xq + b);
+    ref_block_dots_q4_0_xq(wv, xq, dots, n, k);
     free(xq);
 }
 

@@ -67,6 +67,8 @@ void ref_mul_mat_f16(const uint16_t *w, const float *x, float *y, int64_t n, int
 /* mode 0: ggml-cpu semantics (x -> Q8_0, integer block dots)
  * mode 1: true W4A16 (x -> f16, dequantised weights, fp accumulation) */
 void ref_mul_mat_q4_0(const void *w, const float *x, float *y, int64_t n, int64_t k, int mode, int nthreads);
+void ref_mul_mat_q4_0_xq(const void *w, const void *xq, float *y, int64_t n, int64_t k, int nthreads);
+void ref_block_dots_q4_0_xq(const void *w, const void *xq, int32_t *dots, int64_t n, int64_t k);
 void ref_mul_mat_q8_0(const void *w, const float *x, float *y, int64_t n, int64_t k, int nthreads);
 /* per-(row, block) int32 dots for exactness checks; dots is [n][k/32] */
 void ref_block_dots_q4_0(const void *w, const float *x, int32_t *dots, int64_t n, int64_t k);

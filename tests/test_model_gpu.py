@@ -1,18 +1,23 @@
 """Whole-model decode parity (GPU), reduced depth, small and full widths.
 
-Every step is teacher-forced (the given token, not the model's own argmax) and
-checked per layer: the oracle consumes the GPU's layer input (layer dump) and
-each stage -- roped q, attention output, layer output, logits -- must match
-within 1e-3 of its max magnitude (normwise).  Stages that do not follow a Q8_0
-activation quantisation (q, attention) must also meet the elementwise bar.
-The end-to-end logits without per-layer forcing are checked loosely and set
-against the divergence of two CPU accumulation orders (see model_ref.py)."""
+Every step is teacher-forced (the given token, not the model's own argmax)
+and checked stage by stage (model_ref.stage_check): the oracle takes the
+GPU's own input to each stage, every Q8_0 activation and per-block int32 dot
+the step's GEMVs used must be bit-exact, and every fp stage -- roped q, K/V
+rows, attention, both residuals, the SwiGLU output and the logits -- must be
+within max relative error 1e-3, normwise and elementwise.
+
+Without the stage forcing, logits drift further: two valid CPU accumulation
+orders of the same semantics already differ by ~1e-2 after two layers,
+because the Q8_0 activation quantisation is discontinuous
+(test_accumulation_order_sensitivity_of_quantised_decode).  That drift is
+measured below against the same CPU-vs-CPU figure, not held to 1e-3."""
 import numpy as np
 import pytest
 
 import oracle as O
-from helpers import TOL, assert_close, errs
-from model_ref import per_layer_errors
+from helpers import TOL, errs
+from model_ref import assert_stages, stage_check
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -41,39 +46,52 @@ def build(cfg_kw, n_prefill, seed=11):
 SMALL = dict(n_layer=2, d_model=512, n_head=8, n_head_kv=2, head_dim=64, d_ff=1024, vocab=2048, kv_size=96)
 
 
-def check_stages(e, what):
-    """Normwise <= 1e-3 for every stage.  q and attention (no Q8_0 step
-    upstream within the layer) must also hold elementwise at 1e-2: with the
-    1e-3 * max floor, an elementwise 1e-3 bar asks near-zero outputs for
-    absolute errors of ~1e-6 * max, the resolution of fp32 accumulation order
-    itself (the kernel-level attention tests keep the 1e-3 elementwise bar)."""
-    for k, (nw, ew) in e.items():
-        assert nw <= TOL, f"{what} {k}: normwise {nw:.3e}"
-        if k.endswith(".q") or k.endswith(".attn") or k == "embed":
-            assert ew <= 10 * TOL, f"{what} {k}: elementwise {ew:.3e}"
+def _free_run_drift_bound(cfg_kw, W, kc0, vc0, toks, pos0):
+    """How far two valid CPU accumulation orders of the oracle drift apart
+    over the same teacher-forced steps (max normwise error of the logits)."""
+    worst = 0.0
+    refs = []
+    for mode in (0, 1):
+        O.lib().ref_set_accum_mode(mode)
+        r = O.OracleLlama(dict(cfg_kw, rope_theta=500000.0, rms_eps=1e-5), W, [k.copy() for k in kc0],
+                          [v.copy() for v in vc0])
+        out = []
+        for i, t in enumerate(toks):
+            r.step(t, pos0 + i)
+            out.append(r.logits.copy())
+        refs.append(out)
+    O.lib().ref_set_accum_mode(0)
+    for a, b in zip(*refs):
+        worst = max(worst, errs(a, b)[0])
+    return worst
 
 
-def test_small_teacher_forced_per_layer():
+def test_small_teacher_forced_per_stage():
     m, ref = build(SMALL, n_prefill=40)
     import decode_model as M
 
     cfg = M.LlamaConfig(**SMALL)
     W = M.oracle_weights(m)
-    kc = [k.copy() for k in ref.k_cache]
-    vc = [v.copy() for v in ref.v_cache]
+    kc0 = [k.copy() for k in ref.k_cache]
+    vc0 = [v.copy() for v in ref.v_cache]
+    kc = [k.copy() for k in kc0]
+    vc = [v.copy() for v in vc0]
     toks = [3, 17, 1999, 0, 256, 1024, 7, 8]
+    drift = []
     for i, t in enumerate(toks):
         pos = 40 + i
-        x, q, a = m.debug_step(t, pos)
-        _, logits = m.logits()
-        check_stages(per_layer_errors(cfg, W, kc, vc, x, q, a, logits, t, pos), f"step {i}")
+        D = m.dump_step(t, pos)
+        exact, fp = stage_check(cfg, W, kc, vc, D, t, pos)
+        assert_stages(exact, fp, TOL, f"step {i}")
         ref.step(t, pos)
-        # end to end (no per-layer forcing): loose bound, see module docstring
-        assert errs(logits, ref.logits)[0] <= 1e-2
+        drift.append(errs(D["logits"], ref.logits)[0])
+    # free-running (no stage forcing): within a few times the CPU-vs-CPU drift
+    cpu = _free_run_drift_bound(SMALL, W, kc0, vc0, toks, 40)
+    assert max(drift) <= max(4 * cpu, 2 * TOL), (max(drift), cpu)
     m.close()
 
 
-def test_llama70b_widths_two_layers_per_layer():
+def test_llama70b_widths_two_layers_per_stage():
     import decode_model as M
 
     kw = dict(n_layer=2, d_model=8192, n_head=64, n_head_kv=8, head_dim=128, d_ff=28672, vocab=128256,
@@ -85,10 +103,26 @@ def test_llama70b_widths_two_layers_per_layer():
     vc = [v.copy() for v in ref.v_cache]
     for i, t in enumerate([128000, 9906]):
         pos = 4096 + i
-        x, q, a = m.debug_step(t, pos)
-        _, logits = m.logits()
-        check_stages(per_layer_errors(cfg, W, kc, vc, x, q, a, logits, t, pos), f"70b step {i}")
+        D = m.dump_step(t, pos)
+        exact, fp = stage_check(cfg, W, kc, vc, D, t, pos)
+        assert_stages(exact, fp, TOL, f"70b step {i}")
     m.close()
+
+
+def test_dump_step_matches_debug_step_and_decode():
+    """The full dump, the plain layer dump and the captured graph agree."""
+    m, _ = build(SMALL, n_prefill=30)
+    D = m.dump_step(9, 30)
+    m2, _ = build(SMALL, n_prefill=30)
+    x, q, a = m2.debug_step(9, 30)
+    np.testing.assert_array_equal(D["x"], x)
+    np.testing.assert_array_equal(D["q"], q)
+    np.testing.assert_array_equal(D["att"], a)
+    m3, _ = build(SMALL, n_prefill=30)
+    _, logits = m3.decode(9, 30, want_logits=True)
+    np.testing.assert_array_equal(D["logits"], logits)
+    for mm in (m, m2, m3):
+        mm.close()
 
 
 def test_decode_matches_debug_step():

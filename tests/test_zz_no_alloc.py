@@ -4,9 +4,11 @@ It serves hosts that cannot allocate device memory when attention runs; its
 split-KV partials live in a fixed per-device array of the library.  The GPU
 test checks it against b200_fa_decode (the workspace entry point) through
 the C ABI, on two calls in a row with different shapes, so the second call
-runs on the array the first one left behind.  This file is named to be
-collected last and passes alone in a fresh process as well as after the
-other tests.
+runs on the array the first one left behind, and against the CPU oracle
+(fp64 attention of the same inputs), so that the head dim 256 case -- where
+both entry points run the same CUDA-core kernel -- also meets an
+independent answer.  This file is named to be collected last and passes
+alone in a fresh process as well as after the other tests.
 """
 import ctypes as C
 
@@ -60,6 +62,10 @@ def _case(name, seed):
 
 
 def _both(torch, q, k, v, mask, kv_len=None):
+    """(static-scratch result, workspace-entry result); both are also held
+    to the CPU oracle here."""
+    import oracle as O
+
     bw = B()
     dq, dk, dv, dm = (torch.from_numpy(a).cuda() for a in (q, k, v, mask))
     kl = None if kv_len is None else torch.tensor([kv_len], dtype=torch.int32, device="cuda")
@@ -68,7 +74,11 @@ def _both(torch, q, k, v, mask, kv_len=None):
     out = torch.full_like(dq, float("nan"))
     got = bw.flash_attn_ext_static_scratch(dq, dk, dv, dm, scale=scale, kv_lengths=kl, out=out)
     assert got.data_ptr() == out.data_ptr()
-    return got.cpu().numpy(), ref
+    got = got.cpu().numpy()
+    truth = O.flash_attn_decode(q, k, v, mask, kv_len=kv_len, scale=scale)
+    assert_close(got, truth, tol=TOL, what="static scratch vs oracle")
+    assert_close(ref, truth, tol=TOL, what="workspace entry vs oracle")
+    return got, ref
 
 
 @pytest.mark.gpu
