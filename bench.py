@@ -1,7 +1,9 @@
 """Benchmark: batch-1 greedy decode of the Llama-3-70B-shaped Q4_0 model
-on N B200s of one node, tensor parallel.
+(80 layers, Q4_0 weights, KV cache prefilled to 4096 positions) on N B200s
+of one node, tensor parallel.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --case NAME [--launches L]     # one kernel (bench_cases.py)
 
 N > 1 is launched one process per GPU with torch.distributed.run.  A step is
 one decode token: the whole captured CUDA graph (80 layers + lm_head + argmax,
@@ -14,8 +16,8 @@ ranks.  Prints one JSON line on rank 0.
 --impl reference times the CPU oracle (oracle/refcpu.c, a C restatement of
 ggml-cpu's decode semantics; the reference add-on's own kernels need an
 Ascend NPU and llama.cpp's CPU backend is not in this image) on the host
-cores, on a bounded sample of the same workload (2 of the 80 layers plus the
-lm_head per token, extrapolated to 80 layers).
+cores over whole 80-layer greedy tokens of the same model: the same seeded
+weights and KV prefill, regenerated on the host bit for bit.
 """
 from __future__ import annotations
 
@@ -129,62 +131,82 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ CPU side
 
-class CpuSample:
-    """The CPU oracle on a bounded sample of config 5: `layers` of the 80
-    layers at full width plus the lm_head (random Q4_0 blocks; the arithmetic
-    does not depend on the values).  step() times one token and returns
-    tok/s extrapolated to 80 layers."""
+def host_mem_available() -> int:
+    try:
+        with open("/proc/meminfo") as f:
+            for ln in f:
+                if ln.startswith("MemAvailable:"):
+                    return int(ln.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
 
-    def __init__(self, layers: int = 2, threads: int = 0, n_tokens: int = 64):
-        import numpy as np
 
+class CpuModel:
+    """The CPU oracle (oracle/refcpu.c: ggml-cpu's decode semantics restated
+    in C, OpenMP over every host core) holding the same synthetic model as
+    the GPU arm: the first `layers` layers of the Llama-3-70B shape (all 80
+    for the reference arm), the same seeded Q4_0 weights and KV prefill,
+    regenerated on the host bit for bit (oracle.synth_llama_weights)."""
+
+    def __init__(self, layers: int, n_tokens: int):
         import decode_model as M
         import oracle as O
 
         O.build()
-        self.layers, self.threads = layers, threads
-        cfg = M.LlamaConfig(kv_size=N_PREFILL + n_tokens + 2, **M.LLAMA3_70B)
+        cfg = model_cfg(n_tokens)
         cfg.n_layer = layers
-        rng = np.random.default_rng(SEED)
-        d, ff = cfg.d_model, cfg.d_ff
-        qd, kvd = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
+        c = cfg.as_dict()
+        self.layers = layers
+        W = O.synth_llama_weights(c, SEED, 0.02)
+        kc, vc = O.synth_llama_kv(c, SEED + 1, N_PREFILL)
+        self.ref = O.OracleLlama(c, W, kc, vc)
+        self.cores = os.cpu_count() or 1
+        self.tok, self.pos = 128000, N_PREFILL
 
-        def q4(rows, cols):
-            b = rng.integers(0, 256, size=(rows, cols // 32, 18), dtype=np.uint8)
-            b[:, :, 1] = 0x22  # f16 scale ~0.003: finite, N(0, 0.02^2)-like magnitudes
-            return np.ascontiguousarray(b.reshape(rows, -1))
-
-        w = {"tok_embd": q4(cfg.vocab, d), "lm_head": q4(cfg.vocab, d), "out_norm": np.ones(d, np.float32)}
-        for key, (r, c) in (("wq", (qd, d)), ("wk", (kvd, d)), ("wv", (kvd, d)), ("wo", (d, qd)),
-                            ("wgate", (ff, d)), ("wup", (ff, d)), ("wdown", (d, ff))):
-            w[key] = [q4(r, c) for _ in range(layers)]
-        w["attn_norm"] = [np.ones(d, np.float32) for _ in range(layers)]
-        w["ffn_norm"] = [np.ones(d, np.float32) for _ in range(layers)]
-        kc = [rng.standard_normal((cfg.kv_size, kvd), dtype=np.float32).astype(np.float16) for _ in range(layers)]
-        vc = [rng.standard_normal((cfg.kv_size, kvd), dtype=np.float32).astype(np.float16) for _ in range(layers)]
-        self.ref = O.OracleLlama(cfg.as_dict(), w, kc, vc)
-        self.i = 0
-        self.cores = threads if threads > 0 else (os.cpu_count() or 1)
-        self.sample = (f"{layers} of 80 layers at full width + lm_head per token, timed per token and "
-                       f"extrapolated (80 x layer time + head time), KV {N_PREFILL}")
-
-    def step(self) -> float:
-        L = self.layers
-        pos = N_PREFILL + self.i
+    def step(self, l0=0, l1=None, head=True) -> float:
+        """Layers [l0, l1) of the current greedy token (the embedding when
+        l0 == 0) and, with head, the lm_head + argmax that ends the token;
+        returns seconds."""
         t0 = time.perf_counter()
-        self.ref.step(1 + self.i, pos, l0=0, l1=L, do_head=False, nthreads=self.threads)
-        t1 = time.perf_counter()
-        self.ref.step(1 + self.i, pos, l0=L, l1=L, do_head=True, nthreads=self.threads)
-        t2 = time.perf_counter()
-        self.i += 1
-        return 1.0 / (80 * (t1 - t0) / L + (t2 - t1))
+        nxt = self.ref.step(self.tok, self.pos, l0=l0, l1=l1, do_head=head)
+        t = time.perf_counter() - t0
+        if head:
+            self.tok, self.pos = nxt, self.pos + 1
+        return t
+
+    def sampled_token(self):
+        """(seconds of the sampled layers, seconds of the lm_head) of one token."""
+        t_layers = self.step(0, self.layers, head=False)
+        t_head = self.step(self.layers, self.layers, head=True)
+        return t_layers, t_head
 
 
 def cpu_baseline(tokens: int = 3):
-    cs = CpuSample()
-    cs.step()
-    v = statistics.median([cs.step() for _ in range(tokens)])
-    return v, cs.cores, cs.sample + f", median of {tokens} tokens"
+    """Bounded CPU sample for the GPU arm's line: 2 of the 80 layers plus the
+    lm_head per token (same weights as the GPU arm's first layers), tok/s
+    extrapolated to 80 layers."""
+    cm = CpuModel(layers=2, n_tokens=tokens + 2)
+    cm.sampled_token()
+    vals = []
+    for _ in range(tokens):
+        t_layers, t_head = cm.sampled_token()
+        vals.append(1.0 / (80 * t_layers / 2 + t_head))
+    sample = (f"2 of 80 layers at full width + lm_head per token, the GPU arm's weights and KV, "
+              f"timed per token and extrapolated (80 x layer time + head time), median of {tokens} tokens")
+    return statistics.median(vals), cm.cores, sample
+
+
+def bench_config(world: int, steps: int) -> dict:
+    """The workload description both arms print (identical for the same N, K)."""
+    return {"workload": "Llama-3-70B-shape Q4_0 batch-1 greedy decode, KV prefilled 4096",
+            "model": "llama3-70b-shape (80L, d8192, 64/8 heads, ffn 28672, vocab 128256)",
+            "global_batch": 1, "seq_len": N_PREFILL + steps // 2, "prefill": N_PREFILL,
+            "parallelism": f"tp{world}",
+            "data_seed": SEED}
+
+
+DATA = "synthetic (seeded N(0,0.02^2) weights quantised to Q4_0; KV prefilled N(0,1) f16; same bytes in both arms)"
 
 
 # --------------------------------------------------------------------- arms
@@ -199,26 +221,48 @@ def dist_setup(n_gpus: int):
 
 
 def run_reference(args):
+    """The reference arm: the CPU oracle on the host cores timing whole
+    80-layer greedy tokens of the same model (weights, KV prefill, start
+    token and positions as the GPU arm).  Rank 0 only."""
     world, rank, _ = dist_setup(args.gpus)
     if rank != 0:
         return
-    cs = CpuSample(n_tokens=args.warmup + args.steps)
-    for _ in range(args.warmup):
-        cs.step()
-    vals = [cs.step() for _ in range(args.steps)]
-    value = len(vals) / sum(1.0 / v for v in vals)
-    cores, sample = cs.cores, cs.sample
+    need = 44 << 30  # 39.5 GB of Q4_0 weights + KV cache + working set
+    avail = host_mem_available()
+    total = args.warmup + args.steps
+    if avail and avail < need:
+        # not enough host memory for the whole model: time a bounded sample
+        cm = CpuModel(layers=2, n_tokens=total + 2)
+        tl, th = [], []
+        for i in range(total):
+            a, b = cm.sampled_token()
+            if i >= args.warmup:
+                tl.append(a)
+                th.append(b)
+        per_step = statistics.mean(tl) + statistics.mean(th)
+        value = 1.0 / (80 * statistics.mean(tl) / 2 + statistics.mean(th))
+        sample = (f"host memory {avail >> 30} GiB < {need >> 30} GiB: each step times 2 of the 80 layers + the "
+                  "lm_head (ms_per_step); value extrapolated to 80 layers")
+        extrapolated = True
+    else:
+        cm = CpuModel(layers=80, n_tokens=total + 2)
+        for _ in range(args.warmup):
+            cm.step()
+        ts = [cm.step() for _ in range(args.steps)]
+        per_step = statistics.mean(ts)
+        value = len(ts) / sum(ts)
+        sample = "whole 80-layer greedy tokens (embedding, 80 layers, lm_head, argmax), every step timed"
+        extrapolated = False
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "q4_0xq8_0 int32 dots, fp32",
-        "data": "synthetic (random Q4_0 blocks, N(0,1) f16 KV)",
-        "config": {"workload": "config 5: Llama-3-70B-shape Q4_0 batch-1 decode, KV prefilled 4096",
-                   "model": "llama3-70b-shape", "global_batch": 1, "seq_len": N_PREFILL, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1000.0, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "q4_0xq8_0 int32 dots, fp32", "data": DATA,
+        "config": bench_config(args.gpus, args.steps),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cm.cores, "kind": "port", "sample": sample,
+                         "extrapolated": extrapolated},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "CPU oracle (C restatement of ggml-cpu decode semantics, OpenMP); the reference add-on runs "
-                "on an Ascend NPU and llama.cpp's CPU backend is absent from this image",
+        "note": "CPU oracle (C restatement of ggml-cpu decode semantics, OpenMP over all host cores); the "
+                "reference add-on runs on an Ascend NPU and llama.cpp's CPU backend is absent from this image",
     }
     print(json.dumps(line), flush=True)
 
@@ -327,13 +371,9 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "q4_0xq8_0 int32 dots, fp32",
-            "data": "synthetic (random-init Q4_0 weights N(0,0.02^2); KV prefilled N(0,1) f16)",
-            "config": {"workload": "config 5: Llama-3-70B-shape Q4_0 batch-1 greedy decode, KV prefilled 4096",
-                       "model": "llama3-70b-shape (80L, d8192, 64/8 heads, ffn 28672, vocab 128256)",
-                       "global_batch": 1, "seq_len": ctx_mid, "parallelism": f"tp{world}",
-                       "l2": "no flush needed: each step streams %.1f GB of weights per GPU (> 126 MB L2)"
-                             % (step_bytes / 1e9)},
+            "vs_baseline": None, "dtype": "q4_0xq8_0 int32 dots, fp32", "data": DATA,
+            "config": bench_config(world, args.steps),
+            "l2": "no flush needed: each step streams %.1f GB of weights per GPU (> 126 MB L2)" % (step_bytes / 1e9),
             "roofline": {"bound": "hbm", "kernel": "gemv_q4_0 gate/up (fused RMSNorm+Q8_0+SwiGLU)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": peak_kind, "traffic": traffic,
@@ -347,12 +387,38 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
         }
         if cpu_v is not None:
-            line["cpu_baseline"] = {"value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+            line["cpu_baseline"] = {"value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+                                    "extrapolated": True}
         print(json.dumps(line), flush=True)
     m.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_case(args):
+    """One JSON line per kernel case: L2-flushed exact-config and rotated
+    (copies larger than L2) timings, roofline fraction, CPU oracle beside."""
+    import torch
+
+    import bench_cases as BC
+
+    names = BC.CASES if args.case == "all" else [args.case]
+    for n in names:
+        if n not in BC.CASES:
+            raise SystemExit(f"unknown case {n}; known: {', '.join(BC.CASES)}")
+    torch.cuda.set_device(0)
+    if args.launches:
+        for n in names:
+            BC.run_launches(n, args.launches)
+        return
+    peak, kind = measured_peaks()
+    for n in names:
+        clocks = ClockSampler(0)
+        clocks.start()
+        line = BC.case_line(n, peak, kind, with_cpu=not args.no_cpu)
+        line["clocks"] = clocks.stop()
+        print(json.dumps(line), flush=True)
 
 
 def main():
@@ -362,9 +428,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--case", default=None,
+                    help="one kernel case instead of the decode step (bench_cases.CASES, or 'all')")
+    ap.add_argument("--launches", type=int, default=0, help="with --case: only run L plain launches (profilers)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.case is not None:
+        run_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -250,6 +250,9 @@ int b200_get_rows_q4_0_packed(const void *table_packed, const int32_t *idx, floa
                               int64_t vocab, b200_stream_t stream);
 int b200_swiglu_f32(const float *g, const float *u, float *y, int64_t n, b200_stream_t stream);
 int b200_add_f32(const float *a, const float *b, float *y, int64_t n, b200_stream_t stream);
+/* y = a * b (ggml MUL): b has n elements, or nb elements broadcast over the
+ * n / nb rows of a (a norm weight). */
+int b200_mul_f32(const float *a, const float *b, float *y, int64_t n, int64_t nb, b200_stream_t stream);
 int b200_argmax_f32(const float *x, int64_t n, int32_t *out, b200_stream_t stream);
 
 /* ------------------------------------------------------------------------

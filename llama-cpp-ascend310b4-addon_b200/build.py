@@ -26,6 +26,7 @@ SOURCES = [
     "host.cpp",
     "model.cpp",
     "upload.cpp",
+    "graph.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

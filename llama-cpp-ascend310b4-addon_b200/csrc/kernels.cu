@@ -851,6 +851,12 @@ int b200_add_f32(const float* a, const float* b, float* y, int64_t n, b200_strea
     return cuda_status(cudaGetLastError());
 }
 
+int b200_mul_f32(const float* a, const float* b, float* y, int64_t n, int64_t nb, b200_stream_t stream) {
+    if (!a || !b || !y || n <= 0 || nb <= 0 || n % nb) return B200_EINVAL;
+    mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(a, b, y, n, nb);
+    return cuda_status(cudaGetLastError());
+}
+
 int b200_argmax_f32(const float* x, int64_t n, int32_t* out, b200_stream_t stream) {
     if (!x || !out || n <= 0 || n > INT32_MAX) return B200_EINVAL;
     argmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, out);

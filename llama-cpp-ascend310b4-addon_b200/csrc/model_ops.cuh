@@ -15,15 +15,60 @@ __host__ __device__ inline uint64_t splitmix64(uint64_t z) {
     return z ^ (z >> 31);
 }
 
-// Box-Muller on two 24-bit uniforms drawn from splitmix64(seed, index); the
-// same counter stream as the CPU oracle's ref_synth_normal (values agree up
-// to libm rounding of logf/cosf).
+// ln(u) for a normal float u > 0: u = m 2^e with m in [sqrt(1/2), sqrt(2)),
+// ln m = 2 atanh(s) = 2 s (1 + s^2/3 + ... + s^10/11) with s = (m-1)/(m+1),
+// |s| < 0.1716 (series truncation < 1e-10).  Only correctly rounded f32
+// operations (add, mul, div, fma), so a host restatement with the same
+// steps gives the same bits.
+__device__ __forceinline__ float synth_ln(float u) {
+    const unsigned b = __float_as_uint(u);
+    int e = (int)((b >> 23) & 0xffu) - 127;
+    float m = __uint_as_float((b & 0x7fffffu) | 0x3f800000u);
+    if (m > 1.41421356f) {
+        m = __fmul_rn(m, 0.5f);
+        e += 1;
+    }
+    const float s = __fdiv_rn(__fsub_rn(m, 1.0f), __fadd_rn(m, 1.0f));
+    const float s2 = __fmul_rn(s, s);
+    float p = __fmaf_rn(s2, 0.0909090909f, 0.111111111f);
+    p = __fmaf_rn(s2, p, 0.142857143f);
+    p = __fmaf_rn(s2, p, 0.2f);
+    p = __fmaf_rn(s2, p, 0.333333333f);
+    p = __fmaf_rn(s2, p, 1.0f);
+    return __fmaf_rn((float)e, 0.693147181f, __fmul_rn(__fmul_rn(2.0f, s), p));
+}
+
+// cos(2 pi t) for t in [0, 1): folded to a in [0, 1/4] (cos is even and
+// cos(2 pi (1/2 - a)) = -cos(2 pi a); each fold is exact in f32), then the
+// Taylor series of cos(x), x = 2 pi a <= pi/2, through x^16 (error < 1e-12).
+__device__ __forceinline__ float synth_cos2pi(float t) {
+    float a = t > 0.5f ? __fsub_rn(1.0f, t) : t;
+    const bool flip = a > 0.25f;
+    if (flip) a = __fsub_rn(0.5f, a);
+    const float x = __fmul_rn(a, 6.28318531f);
+    const float x2 = __fmul_rn(x, x);
+    float p = __fmaf_rn(x2, 4.77947733e-14f, -1.14707456e-11f);
+    p = __fmaf_rn(x2, p, 2.08767570e-9f);
+    p = __fmaf_rn(x2, p, -2.75573192e-7f);
+    p = __fmaf_rn(x2, p, 2.48015873e-5f);
+    p = __fmaf_rn(x2, p, -1.38888889e-3f);
+    p = __fmaf_rn(x2, p, 4.16666667e-2f);
+    p = __fmaf_rn(x2, p, -0.5f);
+    p = __fmaf_rn(x2, p, 1.0f);
+    return flip ? -p : p;
+}
+
+// N(0, 1) by Box-Muller on two 24-bit uniforms drawn from
+// splitmix64(seed_mixed ^ index * odd constant): r = sqrt(-2 ln u1),
+// value r cos(2 pi u2).  Bit-identical to the CPU oracle's ref_synth_normal
+// (same operations, all correctly rounded), so a host can regenerate the
+// device's synthetic weights and KV cache exactly.
 __device__ __forceinline__ float synth_normal(uint64_t seed_mixed, uint64_t index) {
     const uint64_t h = splitmix64(seed_mixed ^ (index * 0xD1B54A32D192ED03ull));
-    const float u1 = ((float)(uint32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
-    const float u2 = (float)(uint32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);
-    const float r = sqrtf(-2.0f * logf(u1));
-    return r * cosf(6.283185307179586f * u2);
+    const float u1 = __fmul_rn(__fadd_rn((float)(uint32_t)(h >> 40), 0.5f), 1.0f / 16777216.0f);
+    const float u2 = __fmul_rn((float)(uint32_t)(h & 0xFFFFFFu), 1.0f / 16777216.0f);
+    const float r = __fsqrt_rn(__fmul_rn(-2.0f, synth_ln(u1)));
+    return __fmul_rn(r, synth_cos2pi(u2));
 }
 
 // ggml Q4_0 blocks of N(0, sigma^2) samples: local rows [0, nrows) are global
@@ -41,7 +86,7 @@ __global__ void synth_q4_0_kernel(uint64_t seed, float sigma, int64_t row0, int6
     float amax = 0.f, mx = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-        v[j] = sigma * synth_normal(sm, base + j);
+        v[j] = __fmul_rn(sigma, synth_normal(sm, base + j));
         if (amax < fabsf(v[j])) {
             amax = fabsf(v[j]);
             mx = v[j];

@@ -135,6 +135,13 @@ __global__ void add_kernel(const float* a, const float* b, float* y, int64_t n) 
     if (i < n) y[i] = __fadd_rn(a[i], b[i]);
 }
 
+// ggml MUL with src1 the same shape (nb == n) or one row broadcast over
+// the rows of src0 (n % nb == 0).
+__global__ void mul_kernel(const float* a, const float* b, float* y, int64_t n, int64_t nb) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __fmul_rn(a[i], b[nb == n ? i : i % nb]);
+}
+
 // One CTA: packed (value, ~index) keys, so the first maximum wins.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* x, int64_t n, int32_t* out) {
     unsigned long long best = 0ull;

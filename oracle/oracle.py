@@ -75,6 +75,7 @@ def _declare(L):
         "ref_w4a16_probe": (None, [P, P, P, P, I64, I64, I64]),
         "ref_synth_normal": (C.c_float, [C.c_uint64, C.c_uint64]),
         "ref_synth_q4_0": (None, [C.c_uint64, C.c_float, I64, I64, I64, P, I32]),
+        "ref_synth_rows_f16": (None, [C.c_uint64, C.c_uint64, I64, I64, I64, I64, P, I32]),
         "ref_rms_norm_mul": (None, [P, P, P, I64, C.c_float]),
         "ref_rope_norm": (None, [P, I32, I32, I32, C.c_float]),
         "ref_argmax": (I64, [P, I64]),
@@ -307,6 +308,52 @@ def synth_q4_0(seed: int, sigma: float, row0: int, nrows: int, k: int, nthreads:
     out = np.empty((nrows, k // QK * Q4_0_BLOCK_BYTES), dtype=np.uint8)
     lib().ref_synth_q4_0(seed, sigma, row0, nrows, k, _p(out), nthreads)
     return out
+
+
+def synth_rows_f16(seed: int, base: int, nrows: int, rl: int, rg: int | None = None, col0: int = 0,
+                   nthreads: int = 0) -> np.ndarray:
+    """f16 [nrows, rl] of the synthetic N(0,1) stream (the KV-cache fill)."""
+    out = np.empty((nrows, rl), dtype=np.float16)
+    lib().ref_synth_rows_f16(seed, base, nrows, rl, rl if rg is None else rg, col0, _p(out), nthreads)
+    return out
+
+
+def model_tensor_seed(seed: int, layer: int, which: int) -> int:
+    """Seed of one weight tensor of the synthetic decode model (the native
+    driver's tensor_seed): layer -1 for the embedding and the lm_head."""
+    return (seed * 0x9E3779B97F4A7C15 + (layer + 2) * 0x100 + which) & 0xFFFFFFFFFFFFFFFF
+
+
+def synth_llama_weights(cfg: dict, seed: int, sigma: float = 0.02, nthreads: int = 0) -> dict:
+    """The synthetic decode model's weights (ggml Q4_0 rows, norms = 1) as
+    b200_model_init_synthetic makes them on the device, regenerated on the
+    host bit for bit (tensor parallel world 1)."""
+    L, d, D = cfg["n_layer"], cfg["d_model"], cfg["head_dim"]
+    qd, kvd, ff = cfg["n_head"] * D, cfg["n_head_kv"] * D, cfg["d_ff"]
+    shapes = {"wq": (1, qd, d), "wk": (2, kvd, d), "wv": (3, kvd, d), "wo": (4, d, qd), "wgate": (5, ff, d),
+              "wup": (6, ff, d), "wdown": (7, d, ff)}
+    W = {"tok_embd": synth_q4_0(model_tensor_seed(seed, -1, 0), sigma, 0, cfg["vocab"], d, nthreads),
+         "lm_head": synth_q4_0(model_tensor_seed(seed, -1, 8), sigma, 0, cfg["vocab"], d, nthreads)}
+    for key, (which, rows, k) in shapes.items():
+        W[key] = [synth_q4_0(model_tensor_seed(seed, l, which), sigma, 0, rows, k, nthreads) for l in range(L)]
+    W["attn_norm"] = [np.ones(d, np.float32) for _ in range(L)]
+    W["ffn_norm"] = [np.ones(d, np.float32) for _ in range(L)]
+    W["out_norm"] = np.ones(d, np.float32)
+    return W
+
+
+def synth_llama_kv(cfg: dict, seed: int, n_pos: int, nthreads: int = 0):
+    """KV caches [kv_size, n_head_kv * head_dim] f16 per layer, rows < n_pos
+    filled as b200_model_fill_kv_synthetic does (world 1), the rest zero."""
+    kvd = cfg["n_head_kv"] * cfg["head_dim"]
+    kc, vc = [], []
+    for l in range(cfg["n_layer"]):
+        for w, dst in ((0, kc), (1, vc)):
+            c = np.zeros((cfg["kv_size"], kvd), np.float16)
+            if n_pos > 0:
+                c[:n_pos] = synth_rows_f16(seed, (2 * l + w) << 40, n_pos, kvd, kvd, 0, nthreads)
+            dst.append(c)
+    return kc, vc
 
 
 # ------------------------------------------------------------------ llama

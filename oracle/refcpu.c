@@ -567,24 +567,86 @@ static inline uint64_t splitmix64(uint64_t z) {
     return z ^ (z >> 31);
 }
 
+/* The synthetic-data generator of the GPU path (not a reference
+ * behaviour: the benchmark's own seeded data), restated step for step so
+ * that the CPU arm regenerates the device's weights and KV cache bit for
+ * bit.  ln u: u = m 2^e, m in [sqrt(1/2), sqrt(2)), ln m = 2 atanh(s) with
+ * s = (m-1)/(m+1) by its series through s^10/11; cos(2 pi t): folded to
+ * [0, 1/4], Taylor series of cos through x^16.  Only correctly rounded f32
+ * operations (compiled with -ffp-contract=off; fmaf is a single rounding). */
+static inline float synth_ln(float u) {
+    union { float f; uint32_t b; } v = {u}, mv;
+    mv.b = (v.b & 0x7fffffu) | 0x3f800000u;
+    /* branch-free (vectorisable) form of: if m > sqrt(2): m /= 2, e += 1 */
+    const int big = mv.f > 1.41421356f;
+    const int e = (int)((v.b >> 23) & 0xffu) - 127 + big;
+    const float m = mv.f * (big ? 0.5f : 1.0f);
+    const float s = (m - 1.0f) / (m + 1.0f);
+    const float s2 = s * s;
+    float p = fmaf(s2, 0.0909090909f, 0.111111111f);
+    p = fmaf(s2, p, 0.142857143f);
+    p = fmaf(s2, p, 0.2f);
+    p = fmaf(s2, p, 0.333333333f);
+    p = fmaf(s2, p, 1.0f);
+    return fmaf((float)e, 0.693147181f, (2.0f * s) * p);
+}
+
+static inline float synth_cos2pi(float t) {
+    /* t > 1/2: 1 - t (exact); then a > 1/4: 1/2 - a (exact), negated result.
+     * fminf picks the same operand as those comparisons do. */
+    const float t1 = 1.0f - t;
+    const float a0 = t < t1 ? t : t1;
+    const float sign = a0 > 0.25f ? -1.0f : 1.0f;
+    const float a1 = 0.5f - a0;
+    const float a = a0 < a1 ? a0 : a1;
+    const float x = a * 6.28318531f;
+    const float x2 = x * x;
+    float p = fmaf(x2, 4.77947733e-14f, -1.14707456e-11f);
+    p = fmaf(x2, p, 2.08767570e-9f);
+    p = fmaf(x2, p, -2.75573192e-7f);
+    p = fmaf(x2, p, 2.48015873e-5f);
+    p = fmaf(x2, p, -1.38888889e-3f);
+    p = fmaf(x2, p, 4.16666667e-2f);
+    p = fmaf(x2, p, -0.5f);
+    p = fmaf(x2, p, 1.0f);
+    return p * sign;
+}
+
 /* Box-Muller on two 24-bit uniforms drawn from splitmix64(seed, index). */
-float ref_synth_normal(uint64_t seed, uint64_t index) {
-    const uint64_t h = splitmix64(splitmix64(seed) ^ (index * 0xD1B54A32D192ED03ull));
-    const float u1 = ((float)(uint32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
-    const float u2 = (float)(uint32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);
-    const float r = sqrtf(-2.0f * logf(u1));
-    return r * cosf(6.283185307179586f * u2);
+static inline float synth_normal_mixed(uint64_t seed_mixed, uint64_t index) {
+    const uint64_t h = splitmix64(seed_mixed ^ (index * 0xD1B54A32D192ED03ull));
+    /* both values are below 2^24: exact through a signed conversion */
+    const float u1 = ((float)(int32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)(int32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    const float r = sqrtf(-2.0f * synth_ln(u1));
+    return r * synth_cos2pi(u2);
+}
+
+float ref_synth_normal(uint64_t seed, uint64_t index) { return synth_normal_mixed(splitmix64(seed), index); }
+
+/* Rows [0, nrows) of f16 N(0,1) values: element (r, c) takes stream index
+ * base + r * rg + col0 + c (the device's KV-cache fill). */
+void ref_synth_rows_f16(uint64_t seed, uint64_t base, int64_t nrows, int64_t rl, int64_t rg, int64_t col0,
+                        uint16_t *out, int nthreads) {
+    const int nt = pick_threads(nthreads);
+    const uint64_t sm = splitmix64(seed);
+#pragma omp parallel for num_threads(nt) schedule(static)
+    for (int64_t r = 0; r < nrows; ++r)
+        for (int64_t c = 0; c < rl; ++c)
+            out[r * rl + c] = ref_f32_to_f16(synth_normal_mixed(sm, base + (uint64_t)(r * rg + col0 + c)));
 }
 
 void ref_synth_q4_0(uint64_t seed, float sigma, int64_t row0, int64_t nrows, int64_t k, ref_block_q4_0 *out, int nthreads) {
     const int nt = pick_threads(nthreads);
     const int64_t nb = k / REF_QK;
+    const uint64_t sm = splitmix64(seed);
 #pragma omp parallel for num_threads(nt) schedule(static)
     for (int64_t r = 0; r < nrows; ++r) {
         float buf[REF_QK];
         for (int64_t b = 0; b < nb; ++b) {
-            for (int j = 0; j < REF_QK; ++j)
-                buf[j] = sigma * ref_synth_normal(seed, (uint64_t)(row0 + r) * (uint64_t)k + (uint64_t)(b * REF_QK + j));
+            const uint64_t base = (uint64_t)(row0 + r) * (uint64_t)k + (uint64_t)(b * REF_QK);
+#pragma omp simd
+            for (int j = 0; j < REF_QK; ++j) buf[j] = sigma * synth_normal_mixed(sm, base + (uint64_t)j);
             ref_quantize_q4_0(buf, out + r * nb + b, REF_QK);
         }
     }

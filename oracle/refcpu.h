@@ -105,6 +105,8 @@ void ref_w4a16_probe(const uint16_t *x_f16, const uint8_t *packed, const uint16_
 float ref_synth_normal(uint64_t seed, uint64_t index);   /* N(0,1) */
 /* Q4_0 rows of N(0, sigma^2): rows [row0, row0+nrows) of a matrix with k columns */
 void  ref_synth_q4_0(uint64_t seed, float sigma, int64_t row0, int64_t nrows, int64_t k, ref_block_q4_0 *out, int nthreads);
+void  ref_synth_rows_f16(uint64_t seed, uint64_t base, int64_t nrows, int64_t rl, int64_t rg, int64_t col0,
+                         uint16_t *out, int nthreads);
 
 /* ---- Llama-architecture decode ---- */
 typedef struct {

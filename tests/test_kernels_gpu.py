@@ -1,8 +1,10 @@
 """GPU parity of the sm_100a kernels against the CPU oracle, through the C ABI.
 
 Bit-exact: Q8_0 activation bytes and scales, per-block int32 dots, repacked
-layouts.  Floating point: the north-star bar (helpers.TOL = 1e-3).  Shapes are
-the BASELINE configs plus ragged and boundary cases the reference's own
+layouts.  Floating point: max relative error 1e-3 (helpers.TOL).  Shapes are
+the four single-kernel benchmark configs (F16 8960 x 1536, GQA 12/2 x 128
+over 4096, Q4_0 1536 x 8960, Q8_0 151936 x 1536) plus ragged and boundary
+cases the reference's own
 probes sweep (attention lengths 1, 127-129, 239-241, 255-257, 511-513, 4096,
 8192; GQA ratios 8/2, 16/4, 32/8 as in patch:408-431, 450).
 """

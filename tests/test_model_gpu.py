@@ -228,3 +228,27 @@ def test_model_rejects_bad_config():
     with pytest.raises(B.B200Error):
         m.decode(SMALL["vocab"], 0)    # token id out of range
     m.close()
+
+
+def test_synthetic_model_regenerates_bit_for_bit_on_host():
+    """The device's synthetic weights and KV prefill equal the host
+    generator's (oracle.synth_llama_weights / synth_llama_kv) byte for byte,
+    so the CPU arm of bench.py times exactly the GPU arm's model."""
+    import decode_model as M
+
+    cfg = M.LlamaConfig(**SMALL)
+    m = M.DecodeModel(cfg)
+    m.init_synthetic(seed=11, sigma=0.02)
+    m.fill_kv_synthetic(seed=12, n_pos=40)
+    W = O.synth_llama_weights(cfg.as_dict(), 11, 0.02)
+    G = M.oracle_weights(m)
+    for key in ("tok_embd", "lm_head"):
+        np.testing.assert_array_equal(G[key].reshape(-1), W[key].reshape(-1), err_msg=key)
+    for key in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown"):
+        for l in range(cfg.n_layer):
+            np.testing.assert_array_equal(G[key][l].reshape(-1), W[key][l].reshape(-1), err_msg=f"{key}[{l}]")
+    kc, vc = O.synth_llama_kv(cfg.as_dict(), 12, 40)
+    for l in range(cfg.n_layer):
+        np.testing.assert_array_equal(m.export_kv(l, 0, 40).view(np.uint16), kc[l][:40].view(np.uint16))
+        np.testing.assert_array_equal(m.export_kv(l, 1, 40).view(np.uint16), vc[l][:40].view(np.uint16))
+    m.close()

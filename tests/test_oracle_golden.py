@@ -187,3 +187,16 @@ def test_accumulation_order_sensitivity_of_quantised_decode():
     nw, _ = errs(outs[1], outs[0])
     assert nw > 0.0  # the two orders are not bit-identical downstream of quantisation
     assert nw < 5e-2
+
+
+def test_synthetic_normal_generator_moments():
+    """The counter-based N(0,1) generator of the synthetic model (own ln and
+    cos polynomials, shared bit for bit with the device): mean, variance,
+    tail mass and the Box-Muller pieces against numpy's math."""
+    L = O.lib()
+    v = np.array([L.ref_synth_normal(17, i) for i in range(200000)], dtype=np.float64)
+    assert abs(v.mean()) < 0.01 and abs(v.std() - 1.0) < 0.01
+    assert 1e-5 < (np.abs(v) > 4).mean() < 2e-4  # N(0,1): 6.3e-5
+    w = O.synth_q4_0(3, 0.02, 0, 64, 256)
+    deq = O.dequantize_q4_0(w)
+    assert 0.015 < deq.std() < 0.025
