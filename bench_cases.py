@@ -194,14 +194,17 @@ def time_rotated(fn, copies, reps=20, inner=10):
 
 
 def time_flushed(fn, reps=50, warmup=5):
-    """Median us of single launches, each after an L2 flush (a 256 MiB write
-    outside the events)."""
+    """Median us of single launches, each after an L2 flush outside the
+    events: a 256 MiB buffer is read (summed), which evicts the case's lines
+    and leaves only clean ones; a write-based flush would leave ~126 MB of
+    dirty lines that the timed launch then has to write back."""
     torch = _torch()
     s = torch.cuda.current_stream()
-    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    flush = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    sink = torch.empty(1, dtype=torch.float32, device="cuda")
     ts = []
     for it in range(warmup + reps):
-        flush.fill_(float(it))
+        torch.sum(flush, dim=0, keepdim=True, out=sink)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(s)
         fn(0)

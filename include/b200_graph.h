@@ -106,9 +106,9 @@ int b200_supports_op(const b200_tensor *op);
 
 /* Is this tensor a matmul weight whose buffer keeps a packed copy?  Weight
  * buffers only (weights_buffer != 0), F16 / Q4_0 / Q8_0, two-dimensional,
- * rows that the packed layout supports (the reference's is_matmul_weight,
- * patch:1451-1468, without its name test: every 2-D tensor of these types in
- * a weight buffer is a matmul or GET_ROWS operand). */
+ * rows that the packed layout supports, and -- when the descriptor carries
+ * a name -- a ggml name ending in ".weight" (the reference's
+ * is_matmul_weight, patch:1451-1468), so a 2-D F16 KV cache is not packed. */
 int b200_is_matmul_weight(const b200_tensor *t, int weights_buffer);
 /* Bytes a tensor takes in a buffer: ggml_nbytes, and for a matmul weight
  * the ggml bytes rounded up to 256 plus the packed copy, which lives at

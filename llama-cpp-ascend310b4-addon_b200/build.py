@@ -77,9 +77,37 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+def build_ggml_backend(ggml_dir: str, verbose: bool = False) -> str:
+    """libggml-b200.so: the ggml backend adapter (ggml-b200/ggml-b200.cpp)
+    compiled against an upstream ggml tree (llama.cpp 37b3a9e0's ggml/, which
+    holds include/ggml*.h and src/ggml-backend-impl.h) and linked to
+    libb200_decode.so.  Upstream ggml is not part of this repository, so this
+    runs only when its path is given (or GGML_DIR is set)."""
+    lib = build(verbose=False)
+    out = os.path.join(HERE, "libggml-b200.so")
+    inc = [os.path.join(ggml_dir, "include"), os.path.join(ggml_dir, "src")]
+    for d in inc:
+        if not os.path.isdir(d):
+            raise RuntimeError(f"{d} not found: --ggml-dir must be a ggml source tree")
+    cmd = ([shutil.which("g++") or "g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-I" + INCLUDE] +
+           ["-I" + d for d in inc] + ["-I/usr/local/cuda/include", os.path.join(HERE, "ggml-b200", "ggml-b200.cpp"),
+                                      "-o", out, "-L" + HERE, "-lb200_decode", "-Wl,-rpath,$ORIGIN",
+                                      "-L/usr/local/cuda/lib64", "-lcudart"])
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ggml backend build failed:\n{r.stdout}\n{r.stderr}")
+    if verbose:
+        print(out)
+    return out
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--ggml-dir", default=os.environ.get("GGML_DIR"),
+                    help="upstream ggml tree: also build the ggml backend adapter libggml-b200.so")
     a = ap.parse_args()
     build(force=a.force, verbose=True)
+    if a.ggml_dir:
+        build_ggml_backend(a.ggml_dir, verbose=True)
     sys.exit(0)

@@ -143,6 +143,15 @@ bool is_weight_type(int type) {
 
 bool f32_rows(const b200_tensor* t) { return t != nullptr && t->type == B200_TYPE_F32 && contiguous(t); }
 
+// A named tensor is a weight only when its ggml name ends in ".weight" (the
+// loader's naming: "blk.0.ffn_up.weight", "token_embd.weight"), so that an
+// F16 KV cache ("cache_k_l0") in the same buffer is never packed.
+bool weight_name(const b200_tensor* t) {
+    if (t->name == nullptr) return true;
+    const size_t n = std::strlen(t->name);
+    return n >= 7 && std::strcmp(t->name + n - 7, ".weight") == 0;
+}
+
 bool supports_mul_mat(const b200_tensor* op, const Config& c) {
     const b200_tensor* w = op->src[0];
     const b200_tensor* x = op->src[1];
@@ -457,6 +466,7 @@ int b200_supports_op(const b200_tensor* op) {
 
 int b200_is_matmul_weight(const b200_tensor* t, int weights_buffer) {
     if (!t || !weights_buffer || !is_weight_type(t->type) || t->ne[2] != 1 || t->ne[3] != 1) return 0;
+    if (!weight_name(t)) return 0;
     if (!contiguous(t)) return 0;
     return b200_packed_size(t->type, t->ne[1], t->ne[0]) != 0 ? 1 : 0;
 }

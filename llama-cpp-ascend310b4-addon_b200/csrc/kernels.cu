@@ -951,8 +951,14 @@ int static_scratch(unsigned char** out) {
     int dev = -1;
     CR_(cuda_status(cudaGetDevice(&dev)));
     if (dev < 0 || dev >= kMaxDevices) return B200_EINVAL;
-    CR_(cuda_status(cudaFree(nullptr)));  // makes the device's primary context current (allocates nothing)
-    const CUcontext ctx = current_context();
+    CUcontext ctx = current_context();
+    if (ctx == nullptr) {
+        // no context yet on this thread: cudaFree(NULL) makes the device's
+        // primary context current and allocates nothing (not allowed while
+        // a stream captures, hence only here, on a first call)
+        CR_(cuda_status(cudaFree(nullptr)));
+        ctx = current_context();
+    }
     std::lock_guard<std::mutex> lk(g_static_scratch_mu);
     if (g_static_scratch_dev[dev] == nullptr || ctx == nullptr || g_static_scratch_ctx[dev] != ctx) {
         void* p = nullptr;

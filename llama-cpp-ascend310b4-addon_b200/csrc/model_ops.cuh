@@ -95,17 +95,20 @@ __global__ void synth_q4_0_kernel(uint64_t seed, float sigma, int64_t row0, int6
     // quantize_row_q4_0_ref: d = max / -8, q = min(15, (int8)(x*id + 8.5f))
     const float d = __fdiv_rn(mx, -8.0f);
     const float id = d != 0.f ? __frcp_rn(d) : 0.f;
-    uint8_t* blk = out + b * 18;
-    const uint16_t dh = f2h(d);
-    blk[0] = (uint8_t)(dh & 0xff);
-    blk[1] = (uint8_t)(dh >> 8);
+    // the block as nine 16-bit words (blocks are 18 bytes, so 2-byte aligned)
+    uint16_t* blk = reinterpret_cast<uint16_t*>(out + b * 18);
+    blk[0] = f2h(d);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        int q0 = (int)(int8_t)__fadd_rn(__fmul_rn(v[j], id), 8.5f);
-        int q1 = (int)(int8_t)__fadd_rn(__fmul_rn(v[16 + j], id), 8.5f);
-        q0 = min(q0, 15);
-        q1 = min(q1, 15);
-        blk[2 + j] = (uint8_t)(q0 | (q1 << 4));
+    for (int j = 0; j < 16; j += 2) {
+        unsigned pair = 0;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            // x * id + 8.5 lies in [0.5, 16.5]: truncation is the (int8_t) cast of the reference rule
+            const int q0 = min((int)__fadd_rn(__fmul_rn(v[j + e], id), 8.5f), 15);
+            const int q1 = min((int)__fadd_rn(__fmul_rn(v[16 + j + e], id), 8.5f), 15);
+            pair |= (unsigned)(q0 | (q1 << 4)) << (8 * e);
+        }
+        blk[1 + j / 2] = (uint16_t)pair;
     }
 }
 
@@ -155,13 +158,17 @@ __global__ void image_to_q8_0_kernel(const uint8_t* img, int64_t U, uint8_t* out
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= U) return;
     const float d = __int_as_float(reinterpret_cast<const int2*>(img + 32 * U)[b].x);
-    uint8_t* o = out + b * 34;
-    const uint16_t dh = f2h(d);
-    o[0] = (uint8_t)(dh & 0xff);
-    o[1] = (uint8_t)(dh >> 8);
-    for (int i = 0; i < 16; ++i) {
-        o[2 + i] = img[16 * b + i];
-        o[18 + i] = img[16 * U + 16 * b + i];
+    // 17 16-bit words per block (34 bytes, so 2-byte aligned); the planes
+    // hold the q bytes of each half-block as four 32-bit words
+    uint16_t* o = reinterpret_cast<uint16_t*>(out + b * 34);
+    o[0] = f2h(d);
+    const int4 lo = reinterpret_cast<const int4*>(img)[b];
+    const int4 hi = reinterpret_cast<const int4*>(img + 16 * U)[b];
+    const int w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        o[1 + 2 * i] = (uint16_t)((unsigned)w[i] & 0xffffu);
+        o[2 + 2 * i] = (uint16_t)((unsigned)w[i] >> 16);
     }
 }
 

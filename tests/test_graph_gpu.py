@@ -85,6 +85,7 @@ def build_layer(rng):
 
     def act(name, ttype, ne, **kw):
         dt = {G.F32: torch.float32, G.F16: torch.float16, G.I32: torch.int32, G.I64: torch.int64}[ttype]
+        assert name not in T, name
         n = int(np.prod(ne))
         T[name] = torch.zeros(n, dtype=dt, device="cuda")
         return g.tensor(ttype, ne, data=_dev(T[name]), name=name, node=False, **kw)
@@ -96,11 +97,12 @@ def build_layer(rng):
     mask = act("mask", G.F16, [kv, 64])
     kcache = act("k_cache", G.F16, [kvd, kv])
     vcache = act("v_cache", G.F16, [kvd, kv])
-    nt = {k: act(k, G.F32, [d]) for k in norms}
+    nt = {k: act(k + ".weight", G.F32, [d]) for k in norms}
     for k in norms:
-        T[k].copy_(torch.from_numpy(norms[k]))
+        T[k + ".weight"].copy_(torch.from_numpy(norms[k]))
 
     def node(name, ttype, ne, op, src, params=()):
+        assert name not in T, name  # every descriptor keeps its own device memory alive
         dt = {G.F32: torch.float32, G.I32: torch.int32}[ttype]
         T[name] = torch.full((int(np.prod(ne)),), float("nan") if ttype == G.F32 else -1, dtype=dt, device="cuda")
         return g.tensor(ttype, ne, op=op, src=src, params=params, data=_dev(T[name]), name=name)
