@@ -126,6 +126,18 @@ int b200_gemv_f16(const void *w_packed, const float *x, float *y, int64_t n, int
  * beside the weight ring, the weight streams once per group of columns. */
 int b200_mul_mat_f16(const void *w, const float *x, float *y, int64_t n, int64_t k, int m, int64_t ldx, int64_t ldy,
                      b200_stream_t stream);
+/* Prefill MUL_MAT with an F16 weight, any number of columns (tokens):
+ * y[j][r] = sum_i w[r][i] * f16(x[j][i]) for j < m, on the 5th-generation
+ * tensor cores (tcgen05.mma, fp32 accumulator in tensor memory, operands
+ * staged by TMA in the 128-byte swizzle).  The reference sends M >= 16 to
+ * CANN's own matmul on the ND copy (patch:1200-1204); its NZ kernels serve
+ * M <= 8 only.  w: the ggml F16 weight [n rows][k] (k % 8 == 0, 16-byte
+ * aligned); x: f32 [m][ldx]; y: f32 [m][ldy]; workspace: device memory of
+ * b200_mul_mat_f16_tc_workspace_size(m, k) bytes (16-byte aligned) that
+ * receives f16(x) first. */
+size_t b200_mul_mat_f16_tc_workspace_size(int64_t m, int64_t k);
+int b200_mul_mat_f16_tc(const void *w, const float *x, float *y, int64_t n, int64_t k, int64_t m, int64_t ldx,
+                        int64_t ldy, void *workspace, size_t workspace_size, b200_stream_t stream);
 int b200_gemv_q4_0(const void *w_packed, const float *x, float *y, int64_t n, int64_t k, int mode,
                    b200_stream_t stream);
 int b200_gemv_q8_0_q8_0(const void *w_packed, const float *x, float *y, int64_t n, int64_t k,

@@ -90,6 +90,8 @@ def _declare(L):
         "b200_repack_interleave2": (C.c_int, [C.c_int, P, P, P, I64, I64, P]),
         "b200_gemv_f16": (C.c_int, [P, P, P, I64, I64, P]),
         "b200_mul_mat_f16": (C.c_int, [P, P, P, I64, I64, C.c_int, I64, I64, P]),
+        "b200_mul_mat_f16_tc_workspace_size": (C.c_size_t, [I64, I64]),
+        "b200_mul_mat_f16_tc": (C.c_int, [P, P, P, I64, I64, I64, I64, I64, P, C.c_size_t, P]),
         "b200_gemv_q4_0": (C.c_int, [P, P, P, I64, I64, C.c_int, P]),
         "b200_gemv_q8_0_q8_0": (C.c_int, [P, P, P, I64, I64, P]),
         "b200_a8w8_transform": (C.c_int, [P, P, I64, I64, P]),
@@ -267,6 +269,8 @@ def mul_mat(w: PackedWeight, x, y=None, q4_mode: int = Q4_MODE_GGML):
         m = x.shape[0]
         if y is None:
             y = torch.empty(m, w.n, dtype=torch.float32, device=x.device)
+        if m > 8:  # prefill: the tensor-core GEMM (the packed F16 layout is the ggml row layout)
+            return mul_mat_f16_tc(w.data, x, w.n, w.k, y)
         rc = lib().b200_mul_mat_f16(_ptr(w.data), _ptr(x), _ptr(y), w.n, w.k, m, x.stride(0), y.stride(0),
                                     _stream(x.device))
         _check(rc, "mul_mat")
@@ -286,6 +290,31 @@ def mul_mat(w: PackedWeight, x, y=None, q4_mode: int = Q4_MODE_GGML):
     else:
         raise B200Unsupported(EUNSUPPORTED, f"mul_mat weight type {w.wtype}")
     _check(rc, "mul_mat")
+    return y
+
+
+_tc_ws: dict = {}
+
+
+def mul_mat_f16_tc(w_f16, x, n: int, k: int, y=None):
+    """Prefill MUL_MAT of an F16 weight ([n, k] ggml rows on the device) with
+    x f32 [m, k] (row stride >= k) on the tcgen05 tensor cores -> y f32 [m, n].
+    The f16 copy of x goes to a workspace cached per device and size."""
+    torch = _torch()
+    m = x.shape[0]
+    if x.dtype != torch.float32 or x.stride(1) != 1 or x.shape[1] != k:
+        raise B200Error(EINVAL, "mul_mat_f16_tc: x must be f32 [m, k] with a contiguous row")
+    if y is None:
+        y = torch.empty(m, n, dtype=torch.float32, device=x.device)
+    size = int(lib().b200_mul_mat_f16_tc_workspace_size(m, k))
+    key = (str(x.device), size)
+    ws = _tc_ws.get(key)
+    if ws is None:
+        ws = torch.empty(size, dtype=torch.uint8, device=x.device)
+        _tc_ws[key] = ws
+    rc = lib().b200_mul_mat_f16_tc(_ptr(w_f16), _ptr(x), _ptr(y), n, k, m, x.stride(0), y.stride(0), _ptr(ws), size,
+                                   _stream(x.device))
+    _check(rc, "mul_mat_f16_tc")
     return y
 
 

@@ -230,6 +230,8 @@ struct b200_backend {
     cudaStream_t stream = nullptr;
     void* fa_ws = nullptr;
     size_t fa_ws_bytes = 0;
+    void* tc_ws = nullptr;
+    size_t tc_ws_bytes = 0;
     int failed = -1;
 };
 
@@ -274,7 +276,21 @@ int fa_workspace(b200_backend* be, size_t need, void** out) {
     return B200_OK;
 }
 
-const b200_stream_t S(b200_backend* be) { return (b200_stream_t)be->stream; }
+// Workspace of the prefill GEMM (the f16 copy of the activation), grown on demand.
+int tc_workspace(b200_backend* be, size_t need, void** out) {
+    if (need > be->tc_ws_bytes) {
+        CR(ck(cudaStreamSynchronize(be->stream), "synchronize"));
+        if (be->tc_ws) cudaFree(be->tc_ws);
+        be->tc_ws = nullptr;
+        be->tc_ws_bytes = 0;
+        CR(ck(cudaMalloc(&be->tc_ws, need), "GEMM workspace"));
+        be->tc_ws_bytes = need;
+    }
+    *out = be->tc_ws;
+    return B200_OK;
+}
+
+b200_stream_t S(b200_backend* be) { return (b200_stream_t)be->stream; }
 
 int run_mul_mat(b200_backend* be, b200_tensor* op) {
     const b200_tensor* w = op->src[0];
@@ -283,14 +299,16 @@ int run_mul_mat(b200_backend* be, b200_tensor* op) {
     if (w->extra == nullptr) return B200_ESTATE;  // the weight was never uploaded through a b200 weight buffer
     const float* xp = static_cast<const float*>(x->data);
     float* y = static_cast<float*>(op->data);
-    if (w->type == B200_TYPE_F16 && m > 1) {
-        // the small-M tensor-core kernel (ggml-layout weight), up to 8 columns per launch
-        for (int64_t j = 0; j < m; j += 8) {
-            const int mm = (int)std::min<int64_t>(8, m - j);
-            CR(b200_mul_mat_f16(w->data, xp + j * k, y + j * n, n, k, mm, k, n, S(be)));
-        }
-        return B200_OK;
+    const int64_t ldx = (int64_t)(x->nb[1] / 4);
+    if (w->type == B200_TYPE_F16 && m > 8) {
+        // prefill: the tcgen05 GEMM on the ggml-layout weight
+        const size_t need = b200_mul_mat_f16_tc_workspace_size(m, k);
+        void* ws = nullptr;
+        CR(tc_workspace(be, need, &ws));
+        return b200_mul_mat_f16_tc(w->data, xp, y, n, k, m, ldx, n, ws, need, S(be));
     }
+    if (w->type == B200_TYPE_F16 && m > 1)  // the reference's small-M (M <= 8) branch
+        return b200_mul_mat_f16(w->data, xp, y, n, k, (int)m, ldx, n, S(be));
     for (int64_t j = 0; j < m; ++j) {
         const float* xj = xp + j * (int64_t)(x->nb[1] / 4);
         float* yj = y + j * n;
@@ -602,6 +620,7 @@ void b200_backend_free(b200_backend* be) {
     cudaSetDevice(be->device);
     if (be->stream) cudaStreamSynchronize(be->stream);
     if (be->fa_ws) cudaFree(be->fa_ws);
+    if (be->tc_ws) cudaFree(be->tc_ws);
     if (be->stream) cudaStreamDestroy(be->stream);
     delete be;
 }

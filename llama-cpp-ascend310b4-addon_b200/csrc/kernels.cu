@@ -19,6 +19,7 @@
 #include "fa.cuh"
 #include "fa_mma.cuh"
 #include "gemm_small.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "internal.h"
 #include "model_ops.cuh"
@@ -310,6 +311,7 @@ int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st, bool pdl) {
 // attention kernel can be resident at once, per head dim; set once per device.
 int g_fa_active[kMaxDevices][2][5];
 bool g_small_m_attr[kMaxDevices];
+bool g_tc_attr[kMaxDevices][3];
 bool g_fa_ready[kMaxDevices][2];
 
 template <int D>
@@ -675,6 +677,76 @@ int b200_repack_interleave2(int type, const void* src_even, const void* src_odd,
 
 int b200_gemv_f16(const void* w, const float* x, float* y, int64_t n, int64_t k, b200_stream_t stream) {
     return gemv_common(FMT_F16, w, x, y, n, k, nullptr, (cudaStream_t)stream);
+}
+
+size_t b200_mul_mat_f16_tc_workspace_size(int64_t m, int64_t k) {
+    if (m <= 0 || k <= 0) return 0;
+    return align256((size_t)m * (size_t)k * 2);
+}
+
+int b200_mul_mat_f16_tc(const void* w, const float* x, float* y, int64_t n, int64_t k, int64_t m, int64_t ldx,
+                        int64_t ldy, void* workspace, size_t workspace_size, b200_stream_t stream) {
+    if (!w || !x || !y || !workspace || n <= 0 || k <= 0 || m <= 0 || ldx < k || ldy < n) return B200_EINVAL;
+    if (k % 8 || !aligned16(w) || !aligned16(workspace)) return B200_EINVAL;
+    if (workspace_size < b200_mul_mat_f16_tc_workspace_size(m, k)) return B200_EINVAL;
+    if (n > INT32_MAX || m > INT32_MAX || k > INT32_MAX) return B200_EUNSUPPORTED;  // TMA coordinates are int32
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return B200_EINVAL;
+    const cudaStream_t st = (cudaStream_t)stream;
+    const int bn = m <= 64 ? 64 : m <= 128 ? 128 : 256;
+    const int slot = bn == 64 ? 0 : bn == 128 ? 1 : 2;
+    {
+        std::lock_guard<std::mutex> lk(g_attr_mu);
+        if (!g_tc_attr[dev][slot]) {
+            const void* fn = bn == 64    ? (const void*)gemm_f16_tc_kernel<64>
+                             : bn == 128 ? (const void*)gemm_f16_tc_kernel<128>
+                                         : (const void*)gemm_f16_tc_kernel<256>;
+            CR_(cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)tc_smem_bytes(bn))));
+            g_tc_attr[dev][slot] = true;
+        }
+    }
+    // X16 = f16(x), K-contiguous rows
+    uint16_t* x16 = static_cast<uint16_t*>(workspace);
+    const int64_t units = m * (k / 8);
+    f32_to_f16_rows_kernel<<<(unsigned)((units + 255) / 256), 256, 0, st>>>(x, ldx, x16, m, k);
+    CR_(cuda_status(cudaGetLastError()));
+    TcArgs a;
+    std::memset(&a, 0, sizeof(a));
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return B200_ECUDA;
+    const cuuint32_t estr[2] = {1, 1};
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)n};
+        const cuuint64_t strides[1] = {(cuuint64_t)(2 * k)};
+        const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM};
+        if (enc(&a.tmw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(w), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return B200_EUNSUPPORTED;
+    }
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+        const cuuint64_t strides[1] = {(cuuint64_t)(2 * k)};
+        const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)bn};
+        if (enc(&a.tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return B200_EUNSUPPORTED;
+    }
+    a.y = y;
+    a.n = n;
+    a.m = m;
+    a.k = k;
+    a.ldy = ldy;
+    const dim3 grid((unsigned)((n + kTcBM - 1) / kTcBM), (unsigned)((m + bn - 1) / bn), 1);
+    const size_t smem = tc_smem_bytes(bn);
+    switch (bn) {
+        case 64: gemm_f16_tc_kernel<64><<<grid, kTcThreads, smem, st>>>(a); break;
+        case 128: gemm_f16_tc_kernel<128><<<grid, kTcThreads, smem, st>>>(a); break;
+        default: gemm_f16_tc_kernel<256><<<grid, kTcThreads, smem, st>>>(a); break;
+    }
+    return cuda_status(cudaGetLastError());
 }
 
 int b200_mul_mat_f16(const void* w, const float* x, float* y, int64_t n, int64_t k, int m, int64_t ldx, int64_t ldy,
