@@ -151,7 +151,9 @@ def test_alloc_size_dual_layout_and_nbytes():
     L = G.lib()
     g = G.Graph()
     for wtype, n, k in ((G.Q4_0, 1536, 8960), (G.Q8_0, 151936, 1536), (G.F16, 8960, 1536)):
-        w = g.tensor(wtype, [k, n], data=FAKE)
+        w = g.tensor(wtype, [k, n], data=FAKE, name="blk.0.ffn_down.weight")
+        # the same tensor under a cache's name is never packed (a 2-D f16 KV cache shares the buffer)
+        assert L.b200_is_matmul_weight(g.tensor(wtype, [k, n], data=FAKE, name="cache_k_l0"), 1) == 0
         nb = G.nbytes(w)
         assert nb == n * G.row_bytes(wtype, k)
         assert L.b200_is_matmul_weight(w, 1) == 1 and L.b200_is_matmul_weight(w, 0) == 0
