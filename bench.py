@@ -55,6 +55,15 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def measured_tensor_peak():
+    """Dense bf16/f16 tensor peak (burst: the prefill GEMM is timed alone)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def ncu_traffic():
     """Per-launch DRAM bytes of the gate/up GEMV from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", "gemv_q4_0_gateup_traffic.json")
@@ -413,10 +422,14 @@ def run_case(args):
             BC.run_launches(n, args.launches)
         return
     peak, kind = measured_peaks()
+    tpeak, tkind = measured_tensor_peak()
     for n in names:
         clocks = ClockSampler(0)
         clocks.start()
-        line = BC.case_line(n, peak, kind, with_cpu=not args.no_cpu)
+        if n in BC.PREFILL:
+            line = BC.prefill_line(n, tpeak, tkind)
+        else:
+            line = BC.case_line(n, peak, kind, with_cpu=not args.no_cpu)
         line["clocks"] = clocks.stop()
         print(json.dumps(line), flush=True)
 

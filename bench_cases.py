@@ -57,7 +57,12 @@ ATTN = {
     "fa_d256": (16, 4, 256, 4096, "workspace"),
     "fa_l70_static": (64, 8, 128, 4160, "static"),
 }
-CASES = list(GEMV) + list(ATTN)
+# prefill MUL_MAT of an F16 weight on the tcgen05 tensor cores: (n rows, k, m tokens)
+PREFILL = {
+    "prefill_f16_512": (8192, 8192, 512),     # a Llama-70B-width projection over 512 prompt tokens
+    "prefill_f16_128": (8960, 1536, 128),     # config 1's weight, 128 tokens
+}
+CASES = list(GEMV) + list(ATTN) + list(PREFILL)
 KERNEL = {"f16": "gemv_kernel<FMT_F16>", "q4_0": "gemv_kernel<FMT_Q4>", "q8_0": "gemv_kernel<FMT_Q8>",
           "a8w8": "gemv_kernel<FMT_A8>"}
 
@@ -151,8 +156,50 @@ def attn_case(name, copies):
                                        workspace=ws)), nbytes
 
 
+def prefill_case(name, copies):
+    torch = _torch()
+    B = _B()
+    n, k, m = PREFILL[name]
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.02).half() for _ in range(copies)]
+    x = torch.randn(m, k, device="cuda", generator=g)
+    y = torch.empty(m, n, device="cuda")
+    B.mul_mat_f16_tc(ws[0], x, n, k, y)  # sizes the cached workspace outside any capture
+    return (lambda i: B.mul_mat_f16_tc(ws[i % copies], x, n, k, y)), n * k * 2 + m * k * 4 + m * n * 4
+
+
 def make(name, copies=1):
+    if name in PREFILL:
+        return prefill_case(name, copies)
     return gemv_case(name, copies) if name in GEMV else attn_case(name, copies)
+
+
+def prefill_line(name, peak_tflops, peak_kind):
+    """Tensor-core roofline of the prefill GEMM: 2 n k m flops per launch
+    over the CUDA-event time of rotated launches (weights > L2)."""
+    torch = _torch()
+    B = _B()
+    n, k, m = PREFILL[name]
+    copies = max(1, min(16, math.ceil(2.5 * L2_BYTES / (n * k * 2))))
+    fn, nbytes = prefill_case(name, copies)
+    us = time_rotated(fn, copies)
+    del fn
+    torch.cuda.empty_cache()
+    st = B.device_status(reset=True)
+    if st:
+        raise SystemExit(f"device status {st:#x} after case {name}")
+    tflops = 2.0 * n * k * m / (us * 1e-6) / 1e12
+    return {
+        "metric": f"{name}: achieved dense f16 TFLOP/s", "case": name, "value": tflops, "unit": "TFLOP/s",
+        "higher_is_better": True, "n_gpus": 1, "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x)",
+        "config": {"workload": name, "n": n, "k": k, "m": m, "weight": "f16",
+                   "l2": "rotated weight copies larger than L2"},
+        "us_rotated": us,
+        "roofline": {"bound": "tensor", "kernel": "gemm_f16_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)",
+                     "flops_per_launch": 2 * n * k * m, "achieved": tflops, "peak": peak_tflops, "unit": "TFLOP/s",
+                     "peak_source": peak_kind, "frac": tflops / peak_tflops,
+                     "hbm_bytes_per_launch": nbytes},
+    }
 
 
 def case_bytes(name):

@@ -309,7 +309,7 @@ int b200i_gemv(int fmt, GemvArgs a, bool debug, cudaStream_t st, bool pdl) {
 
 // How many clusters of each size (16, 8, 4, 2 CTAs) of the tensor-core
 // attention kernel can be resident at once, per head dim; set once per device.
-int g_fa_active[kMaxDevices][2][5];
+int g_fa_active[kMaxDevices][2][kFmMaxCluster + 1];  // [dev][head dim 64 / 128][cluster size]
 bool g_small_m_attr[kMaxDevices];
 bool g_tc_attr[kMaxDevices][3];
 bool g_fa_ready[kMaxDevices][2];
@@ -327,9 +327,8 @@ int fa_cluster_probe(int dev) {
     const bool nonportable =
         cudaFuncSetAttribute(fa_mma_kernel<D, 2>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
         cudaFuncSetAttribute(fa_mma_kernel<D, 3>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
-    for (int li = 0; li < 5; ++li) {
-        const int cs = 16 >> li;  // 16, 8, 4, 2, 1
-        g_fa_active[dev][slot][li] = 0;
+    for (int cs = 1; cs <= kFmMaxCluster; ++cs) {
+        g_fa_active[dev][slot][cs] = 0;
         if (cs > 8 && !nonportable) continue;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(cs, 1, 1);
@@ -343,24 +342,35 @@ int fa_cluster_probe(int dev) {
         cfg.attrs = &at;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, fa_mma_kernel<D, 3>, &cfg) == cudaSuccess) g_fa_active[dev][slot][li] = n;
+        if (cudaOccupancyMaxActiveClusters(&n, fa_mma_kernel<D, 3>, &cfg) == cudaSuccess) g_fa_active[dev][slot][cs] = n;
     }
     cudaGetLastError();
-    if (g_fa_active[dev][slot][4] <= 0) g_fa_active[dev][slot][4] = 1;
+    if (g_fa_active[dev][slot][1] <= 0) g_fa_active[dev][slot][1] = 1;
     g_fa_ready[dev][slot] = true;
     return B200_OK;
 }
 
 // Cluster size for `needed` clusters over `nchunks` chunks: the largest size
-// whose clusters all fit on the device at once, else the one that keeps the
-// most CTAs resident.
+// (any of 1..16, not only powers of two: a GPC that cannot host a cluster of
+// 16 may host one of 12) whose clusters all fit on the device at once, else
+// the one that keeps the most CTAs resident.  B200_FA_CLUSTER forces a size
+// (tuning sweeps).
+int fa_cluster_override() {
+    static const int v = [] {
+        const char* s = getenv("B200_FA_CLUSTER");
+        const int c = s ? atoi(s) : 0;
+        return c >= 1 && c <= kFmMaxCluster ? c : 0;
+    }();
+    return v;
+}
+
 template <int D>
 int fa_pick_cluster(int dev, int needed, int nchunks) {
     const int slot = D == 64 ? 0 : 1;
+    if (const int f = fa_cluster_override()) return std::max(1, std::min(f, nchunks));
     int best = 1, best_ctas = 0;
-    for (int li = 0; li < 5; ++li) {
-        const int cs = 16 >> li;
-        const int act = g_fa_active[dev][slot][li];
+    for (int cs = kFmMaxCluster; cs >= 1; --cs) {
+        const int act = g_fa_active[dev][slot][cs];
         if (act <= 0) continue;
         const int use = std::min(cs, nchunks);
         if (act >= needed) return std::max(1, use);
