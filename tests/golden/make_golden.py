@@ -23,9 +23,9 @@ from __future__ import annotations
 import argparse
 import hashlib
 import os
-import shutil
 import subprocess
 import sys
+import tempfile
 
 import numpy as np
 
@@ -96,10 +96,11 @@ def sha256(path: str) -> str:
 
 def make_w4a16_fixture(reference: str) -> None:
     src = os.path.join(reference, "experiments", "w4a16-gemv", "source", "gen_data.py")
-    work = os.path.join(HERE, "..", "..", "_work", "w4a16_gen")
-    if os.path.isdir(work):
-        shutil.rmtree(work)
-    os.makedirs(work)
+    with tempfile.TemporaryDirectory(prefix="w4a16_gen_") as work:
+        _make_w4a16_fixture_in(src, work)
+
+
+def _make_w4a16_fixture_in(src: str, work: str) -> None:
     subprocess.run([sys.executable, src], cwd=work, check=True)
     golden = np.fromfile(os.path.join(work, "output", "golden.bin"), dtype=np.float16)
     np.savez_compressed(

@@ -262,3 +262,43 @@ def test_graph_trace_sync_and_unsupported_node(monkeypatch, capfd):
         G.lib().b200_config_reload()
         G.lib().b200_backend_free(be)
         wb.free()
+
+
+@pytest.mark.parametrize("wtype,m", [(G.F16, 1), (G.F16, 4), (G.F16, 33), (G.Q4_0, 1), (G.Q4_0, 3), (G.Q8_0, 2)])
+def test_graph_mul_mat_columns(wtype, m):
+    """MUL_MAT nodes with several src1 columns: F16 M <= 8 on the small-M
+    kernel, M > 8 on the tcgen05 prefill GEMM, Q4_0 / Q8_0 column by column;
+    weights through the buffer's set_tensor (packed copy) as in the model."""
+    n, k = 384, 1024
+    r = np.random.default_rng(40 + m + wtype)
+    if wtype == G.F16:
+        wh = (r.standard_normal((n, k)) * 0.02).astype(np.float16)
+        ref_fn = lambda xj: O.mul_mat_f16(wh, xj)  # noqa: E731
+    elif wtype == G.Q4_0:
+        wh = O.synth_q4_0(77, 0.02, 0, n, k)
+        ref_fn = lambda xj: O.mul_mat_q4_0(wh, xj)  # noqa: E731
+    else:
+        wh = O.quantize_q8_0((r.standard_normal((n, k)) * 0.02).astype(np.float32))
+        ref_fn = lambda xj: O.mul_mat_q8_0(wh, xj)  # noqa: E731
+    g = G.Graph()
+    w = g.tensor(wtype, [k, n], name="blk.0.attn_q.weight")
+    wb = Buf((G.lib().b200_alloc_size(C.byref(w), 1) + 255) // 256 * 256, True)
+    wb.place(w, True)
+    wb.set(w, wh)
+    x = r.standard_normal((m, k)).astype(np.float32)
+    tx = torch.from_numpy(x).cuda()
+    ty = torch.full((m, n), float("nan"), device="cuda")
+    xt = g.tensor(G.F32, [k, m], data=_dev(tx), node=False, name="x")
+    g.tensor(G.F32, [n, m], op=G.OP_MUL_MAT, src=(w, xt), data=_dev(ty), name="y")
+    be = C.c_void_p()
+    assert G.lib().b200_backend_create(0, C.byref(be)) == 0
+    try:
+        arr, cnt = g.node_array()
+        assert G.lib().b200_graph_compute(be, arr, cnt) == 0
+        assert G.lib().b200_backend_synchronize(be) == 0
+        y = ty.cpu().numpy()
+        for j in range(m):
+            assert_close(y[j], ref_fn(x[j]), TOL, f"type {wtype} column {j} of {m}")
+    finally:
+        G.lib().b200_backend_free(be)
+        wb.free()

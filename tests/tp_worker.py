@@ -63,10 +63,11 @@ def main():
         mine["kv"].append((m.export_kv(l, 0, n_prefill), m.export_kv(l, 1, n_prefill)))
 
     toks = [3, 1999] if args.shape == "small" else [128000, 9906]
+    parts = [p for p in M.DUMP_PARTS if not p.startswith("dots_")]
     for i, t in enumerate(toks):
-        x, q, a = m.debug_step(t, n_prefill + i)
-        off, logits = m.logits()
-        mine["steps"].append((t, n_prefill + i, x, q, a, off, logits))
+        D = m.dump_step(t, n_prefill + i, parts)
+        off, _ = m.logits()
+        mine["steps"].append((t, n_prefill + i, D, off))
 
     m.capture()
     t = 42
@@ -101,8 +102,15 @@ def main():
     dist.destroy_process_group()
 
 
+# dump entries every rank holds whole (the residual stream and the
+# activations quantised from it) and entries split by heads / ff columns /
+# vocabulary rows (concatenated in rank order on the last axis)
+REPLICATED = ("x", "x_mid", "xq_qkv", "xq_gu", "xq_head")
+SHARDED = ("q", "k_row", "v_row", "att", "h", "xq_o", "xq_down", "logits")
+
+
 def check(cfg, n_prefill, parts, M):
-    from model_ref import per_layer_errors
+    from model_ref import stage_check
 
     L = cfg.n_layer
     d = cfg.d_model
@@ -130,18 +138,20 @@ def check(cfg, n_prefill, parts, M):
         v[:n_prefill] = np.concatenate([p["kv"][l][1] for p in parts], axis=1)
         kc.append(k)
         vc.append(v)
-    out = {"stages": [], "x_replicated": True, "logit_offsets": []}
+    out = {"stages": [], "exact": [], "x_replicated": True, "logit_offsets": []}
     for s in range(len(parts[0]["steps"])):
-        t, pos = parts[0]["steps"][s][:2]
-        x = parts[0]["steps"][s][2]
-        for p in parts[1:]:
-            out["x_replicated"] &= bool(np.array_equal(p["steps"][s][2], x))
-        q = np.concatenate([p["steps"][s][3] for p in parts], axis=1)
-        a = np.concatenate([p["steps"][s][4] for p in parts], axis=1)
-        out["logit_offsets"].append([int(p["steps"][s][5]) for p in parts])
-        logits = np.concatenate([p["steps"][s][6] for p in parts])
-        e = per_layer_errors(cfg, W, kc, vc, x, q, a, logits, t, pos)
-        out["stages"].append({k: [float(v[0]), float(v[1])] for k, v in e.items()})
+        t, pos, D0, _ = parts[0]["steps"][s]
+        D = {}
+        for key in REPLICATED:
+            D[key] = D0[key]
+            for p in parts[1:]:
+                out["x_replicated"] &= bool(np.array_equal(p["steps"][s][2][key], D0[key]))
+        for key in SHARDED:
+            D[key] = np.concatenate([p["steps"][s][2][key] for p in parts], axis=-1)
+        out["logit_offsets"].append([int(p["steps"][s][3]) for p in parts])
+        exact, fp = stage_check(cfg, W, kc, vc, D, t, pos)
+        out["exact"].append(exact)
+        out["stages"].append({k: [float(v[0]), float(v[1])] for k, v in fp.items()})
     return out
 
 
