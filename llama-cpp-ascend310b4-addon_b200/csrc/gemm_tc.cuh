@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_f16_tc_kernel(const __grid
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-    const int64_t n0 = (int64_t)blockIdx.x * kTcBM, m0 = (int64_t)blockIdx.y * BN;
+    const int64_t n0 = (int64_t)blockIdx.y * kTcBM, m0 = (int64_t)blockIdx.x * BN;
     const int kb_total = (int)((a.k + kTcBK - 1) / kTcBK);
 
     if (warp == 0) {
