@@ -355,6 +355,11 @@ def run_ours(args):
     m.set_state(128000, N_PREFILL, advance=True)
     gu_us = m.time_gate_up(iters=5)
     prof = m.profile(iters=2)
+    # where a captured step's time goes, measured inside the step (device
+    # clock stamps at each kernel's start and end; the classes add up to it)
+    m.set_state(128000, N_PREFILL, advance=True)
+    m.timeline()
+    tl = m.timeline()
     d, ff_l = cfg.d_model, cfg.d_ff // world
     gu_bytes = 2 * ff_l * (d // 32) * 18 + d * 4 * 2  # Q4_0 weights + x + ffn_norm
     peak, peak_kind = measured_peaks()
@@ -391,6 +396,7 @@ def run_ours(args):
                          "step_bytes": step_bytes,
                          "step_frac": step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak},
             "kernel_us": prof,
+            "step_breakdown_us": {"step": tl["step_us"], "advance": tl["advance_us"], "span": tl["span_us"]},
             "clocks": clk,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4},
             "gpu_launches": launches_per_step * args.steps,

@@ -141,6 +141,22 @@ int b200_model_step_bytes(b200_model *m, int ctx, uint64_t *bytes);
  * Leaves the step state where the last step put it. */
 int b200_model_profile(b200_model *m, int iters, float *us_per_class8);
 
+/* Where one captured step's time goes, measured inside the step: a second
+ * CUDA graph of the step whose kernels record the device clock (globaltimer)
+ * at their first CTA's return from the wait on the previous kernel and at
+ * their last CTA's exit.  Kernel classes as in b200_model_profile:
+ *   out[c]      time by which the step's end moved while class c ran
+ *               (exit of a kernel minus the latest earlier exit), summed
+ *               over the step; out[1..7] add up to out[16];
+ *   out[8 + c]  mean span of one kernel of class c (exit minus the end of
+ *               its wait), in microseconds;
+ *   out[16]     the step, from the first QKV GEMV's start to the lm_head's
+ *               end.
+ * Runs one real decode step (the state advances as after b200_model_launch);
+ * call between steps.  The embedding and bookkeeping kernels are not
+ * stamped. */
+int b200_model_timeline(b200_model *m, float *out17);
+
 /* The gate/up GEMV alone: one CUDA graph of the n_layer gate/up launches of
  * the step (each layer's own weights, chained as in the step), replayed
  * `iters` times between CUDA events on the model's stream; *us_per_launch is

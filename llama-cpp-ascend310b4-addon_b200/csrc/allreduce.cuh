@@ -66,8 +66,10 @@ __device__ __forceinline__ bool wait_flag_geq(const unsigned long long* flag, un
 }
 
 __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const ArArgs a) {
+    if (threadIdx.x == 0) stamp_point(a.stamp, a.stamp_stride, 0);
     griddep_wait();  // this rank's partial is complete
     griddep_launch_dependents();
+    if (threadIdx.x == 0) stamp_point(a.stamp, a.stamp_stride, 1);
     const unsigned long long seq =
         a.st != nullptr ? a.st->step * (unsigned long long)a.per_step + (unsigned long long)a.idx + 1ull : a.seq;
     if (blockIdx.x == 0 && threadIdx.x < a.world) {
@@ -76,7 +78,10 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const ArArgs a
     }
     bool ok = true;
     for (int r = 0; r < a.world; ++r) ok = ok && wait_flag_geq(&a.flags[r], seq);
-    if (!ok) return;
+    if (!ok) {
+        if (threadIdx.x == 0) stamp_point(a.stamp, a.stamp_stride, 2);
+        return;
+    }
     const int n4 = a.n >> 2;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
         float4 acc = ld_sys_f4(a.part[0] + 4 * i);
@@ -89,6 +94,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const ArArgs a
         }
         reinterpret_cast<float4*>(a.x)[i] = acc;
     }
+    if (threadIdx.x == 0) stamp_point(a.stamp, a.stamp_stride, 2);  // thread 0's exit (no barrier: ok may differ per thread)
 }
 
 }  // namespace b200

@@ -200,6 +200,11 @@ struct GemvArgs {
     int64_t ar_stride;             // floats between two ranks' slots
     int ar_world, ar_grid, ar_idx, ar_per_step;
     const StepState* ar_st;
+    // Timeline stamps (globaltimer ns), when set: [0] earliest CTA entry,
+    // [n] earliest return from griddepcontrol.wait, [2n] latest CTA exit,
+    // n = stamp_stride (atomicMin / atomicMax by one thread per CTA).
+    unsigned long long* stamp;
+    int stamp_stride;
 };
 
 constexpr int kFaThreads = 128;
@@ -228,6 +233,8 @@ struct FaArgs {
     // TMA descriptors of K and V ([head_dim, Hkv, n_kv], 64 x 1 x 64 boxes,
     // 128-byte swizzle), filled by the launcher of the tensor-core kernel.
     CUtensorMap tmk, tmv;
+    unsigned long long* stamp;  // timeline stamps as GemvArgs::stamp
+    int stamp_stride;
 };
 
 // Small-M F16 matmul (gemm_small.cuh).
@@ -289,6 +296,8 @@ struct ArArgs {
     const float* part[kMaxRanks];                  // rank r's partial [n] (peer mapped)
     unsigned long long* flags;                      // this rank's flags [kMaxRanks]: flags[r] = last seq rank r announced
     unsigned long long* peer_flag[kMaxRanks];       // &flags of rank r [this rank]
+    unsigned long long* stamp;                      // timeline stamps as GemvArgs::stamp
+    int stamp_stride;
 };
 
 }  // namespace b200

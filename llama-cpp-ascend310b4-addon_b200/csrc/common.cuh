@@ -112,6 +112,18 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 __device__ __forceinline__ void record_status(unsigned int bit) { atomicOr(&g_status, bit); }
 
+// Kernel timeline (b200_model_timeline): one thread per CTA folds the
+// globaltimer into slot s[which * stride] -- which 0: entry (min), 1: return
+// from griddepcontrol.wait (min), 2: exit (max).  No-ops when s is null.
+__device__ __forceinline__ void stamp_point(unsigned long long* s, int stride, int which) {
+    if (s == nullptr) return;
+    const unsigned long long t = globaltimer();
+    if (which < 2)
+        atomicMin(s + (int64_t)which * stride, t);
+    else
+        atomicMax(s + (int64_t)2 * stride, t);
+}
+
 // Programmatic dependent launch.  A kernel launched with programmatic stream
 // serialisation may start while the previous kernel in the stream is still
 // finishing; griddep_wait() returns once that kernel has completed and its

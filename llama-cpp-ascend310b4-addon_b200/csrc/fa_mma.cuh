@@ -116,6 +116,7 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int grp = warp >> 2, gw = warp & 3, gtid = tid & 127;  // warp group, warp and thread in it
+    if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 0);
     const int g = lane >> 2, t = lane & 3;
     const int split = blockIdx.x, hk = blockIdx.y, gc = blockIdx.z;
     const int h0 = hk * a.G + gc * kFaMaxG;
@@ -151,6 +152,7 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
     if (ncg <= 0) {
         griddep_wait();
         griddep_launch_dependents();
+        if (gtid == 0) stamp_point(a.stamp, a.stamp_stride, 1);
     }
     if (ncg > 0) {
         const uint32_t gbase = sbase + (uint32_t)(grp * kFmStages * 2 * TILE);
@@ -180,6 +182,7 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
         }
         griddep_wait();
         griddep_launch_dependents();
+        if (gtid == 0) stamp_point(a.stamp, a.stamp_stride, 1);
 
         // Q fragments (the B operand: k = dims, n = heads; heads past the
         // group are zero), loaded while the first K/V copies are in flight
@@ -457,6 +460,10 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
             q8_units<1>(v, word, dh, qs);
             if (valid) q8_image_store(a.xq_img, a.xq_U, (int64_t)h0 * D / 4 + i4, word[0], dh[0], qs[0]);
         }
+    }
+    if (a.stamp != nullptr) {  // uniform over the grid
+        __syncthreads();
+        if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 2);
     }
 }
 

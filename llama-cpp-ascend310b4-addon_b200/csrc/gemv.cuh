@@ -664,6 +664,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& P = a.p;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 0);
     const int S = a.stages;
     const int64_t xbytes = gemv_x_bytes(FMT, P);
     uint8_t* xr = smem;
@@ -777,6 +778,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     // activation, residual and outputs are touched only after this wait.
     griddep_wait();
     griddep_launch_dependents();
+    if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 1);
 
     // ---- prologue: the activation, once per CTA, into shared memory ----
     // Q8_0 activations: every thread's first loads of x (and of the norm
@@ -958,6 +960,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
                 a.ar_st->step * (unsigned long long)a.ar_per_step + (unsigned long long)a.ar_idx + 1ull;
             st_release_sys_u64(a.ar_flag_dst[tid] + blockIdx.x, seq);
         }
+    }
+    if (a.stamp != nullptr) {  // uniform over the grid
+        __syncthreads();
+        if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 2);
     }
 }
 

@@ -143,6 +143,13 @@ struct b200_model {
     uint8_t* comm_region = nullptr;
     void* peer_region[kMaxRanks] = {};
     size_t part_stride = 0, flags_off = 0;
+    // b200_model_timeline: a second captured step whose kernels fold
+    // globaltimer stamps into tl_stamps ([3][tl_n]), classes in tl_cls
+    unsigned long long* tl_stamps = nullptr;
+    int tl_n = 0;
+    std::vector<int> tl_cls;
+    cudaGraph_t tl_graph = nullptr;
+    cudaGraphExec_t tl_exec = nullptr;
 };
 
 namespace {
@@ -235,7 +242,24 @@ float* part_buf(b200_model* m, int which) { return reinterpret_cast<float*>(m->c
 
 // x = sum over ranks of partial buffer `which` (0: O projection, 1: down),
 // collective `idx` of the step.
-int allreduce_sum(b200_model* m, int which, int idx, cudaStream_t s, bool pdl) {
+// Timeline stamps of one step (b200_model_timeline): kernel i of the step
+// folds its entry / post-wait / exit times into base[i], base[n + i],
+// base[2n + i]; cls[i] is its kernel class (PROFILE classes of b200_model.h).
+struct Stamps {
+    unsigned long long* base = nullptr;
+    int n = 0, next = 0;
+    std::vector<int> cls;
+    template <class A>
+    void assign(A& a, int c) {
+        if (next >= n) return;  // more kernels than slots: the rest go unstamped
+        a.stamp = base + next;
+        a.stamp_stride = n;
+        cls.push_back(c);
+        ++next;
+    }
+};
+
+int allreduce_sum(b200_model* m, int which, int idx, cudaStream_t s, bool pdl, Stamps* stamps = nullptr) {
     if (!m->peer_ar) {
         NK(ncclAllReduce(part_buf(m, which), m->x, m->c.d_model, ncclFloat32, ncclSum, m->comm, s));
         return B200_OK;
@@ -255,6 +279,7 @@ int allreduce_sum(b200_model* m, int which, int idx, cudaStream_t s, bool pdl) {
         a.peer_flag[r] = reinterpret_cast<unsigned long long*>(base + m->flags_off) + m->rank;
     }
     a.flags = reinterpret_cast<unsigned long long*>(m->comm_region + m->flags_off);
+    if (stamps) stamps->assign(a, 7);
     return b200i_tp_allreduce(a, s, pdl);
 }
 
@@ -436,7 +461,7 @@ GemvArgs head_args(const b200_model* m) {
     return a;
 }
 
-int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = nullptr) {
+int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = nullptr, Stamps* stamps = nullptr) {
     const b200_llama_config& c = m->c;
     const int D = c.head_dim;
     auto B = [&](int cls) { return prof ? prof->begin(s, cls) : B200_OK; };
@@ -474,6 +499,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
             if (dump)
                 dbg = hook(a, dump->xq_qkv ? dump->xq_qkv + (size_t)l * (d / 32) * 34 : nullptr,
                            dump->dots_qkv ? dump->dots_qkv + (size_t)l * m->qkv_rows * (d / 32) : nullptr);
+            if (stamps) stamps->assign(a, 1);
             CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
         }
         CR(E());
@@ -484,7 +510,11 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
             if (dump->v_row) CK(dcopy(dump->v_row + (size_t)l * kvd, m->L[l].vc + off, kvd * 2));
         }
         CR(B(2));
-        CR(b200i_fa(fa_args(m, l), D, s, pdl));
+        {
+            FaArgs f = fa_args(m, l);
+            if (stamps) stamps->assign(f, 2);
+            CR(b200i_fa(f, D, s, pdl));
+        }
         CR(E());
         if (dump && dump->att) CK(dcopy(dump->att + (size_t)l * qd, m->att, qbytes));
         CR(B(3));
@@ -496,12 +526,13 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
                 if (xq && a.xq_in) CR(image_out(a.xq_in, xq, qd));
                 dbg = hook(a, xq, dump->dots_o ? dump->dots_o + (size_t)l * d * (qd / 32) : nullptr);
             }
+            if (stamps) stamps->assign(a, 3);
             CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
         }
         CR(E());
         if (m->world > 1 && !m->ar_now) {
             CR(B(7));
-            CR(allreduce_sum(m, 0, 2 * l, s, pdl));
+            CR(allreduce_sum(m, 0, 2 * l, s, pdl, stamps));
             CR(E());
         }
         if (dump && dump->x_mid) CK(dcopy(dump->x_mid + (size_t)l * d, m->x, d * sizeof(float)));
@@ -512,6 +543,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
             if (dump)
                 dbg = hook(a, dump->xq_gu ? dump->xq_gu + (size_t)l * (d / 32) * 34 : nullptr,
                            dump->dots_gu ? dump->dots_gu + (size_t)l * 2 * m->ff * (d / 32) : nullptr);
+            if (stamps) stamps->assign(a, 4);
             CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
         }
         CR(E());
@@ -525,12 +557,13 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
                 if (xq && a.xq_in) CR(image_out(a.xq_in, xq, m->ff));
                 dbg = hook(a, xq, dump->dots_down ? dump->dots_down + (size_t)l * d * (m->ff / 32) : nullptr);
             }
+            if (stamps) stamps->assign(a, 5);
             CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
         }
         CR(E());
         if (m->world > 1 && !m->ar_now) {
             CR(B(7));
-            CR(allreduce_sum(m, 1, 2 * l + 1, s, pdl));
+            CR(allreduce_sum(m, 1, 2 * l + 1, s, pdl, stamps));
             CR(E());
         }
         if (dump && dump->x) CK(dcopy(dump->x + (size_t)(l + 1) * d, m->x, d * sizeof(float)));
@@ -540,6 +573,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         GemvArgs a = head_args(m);
         bool dbg = false;
         if (dump) dbg = hook(a, dump->xq_head, dump->dots_head);
+        if (stamps) stamps->assign(a, 6);
         CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
     }
     CR(E());
@@ -722,6 +756,9 @@ void b200_model_destroy(b200_model* m) {
     // Graphs that hold NCCL work are released before the communicator.
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
+    if (m->tl_exec) cudaGraphExecDestroy(m->tl_exec);
+    if (m->tl_graph) cudaGraphDestroy(m->tl_graph);
+    if (m->tl_stamps) cudaFree(m->tl_stamps);
     if (m->comm && m->comm_region && m->x) {
         // no peer may still read this rank's region when it is unmapped and freed
         ncclAllReduce(m->x, m->x, 1, ncclFloat32, ncclSum, m->comm, m->stream);
@@ -1002,6 +1039,66 @@ int b200_model_profile(b200_model* m, int iters, float* us) {
         }
     }
     for (int i = 0; i < 8; ++i) us[i] = cnt[i] ? (float)(acc[i] / cnt[i]) : 0.f;
+    return B200_OK;
+}
+
+int b200_model_timeline(b200_model* m, float* out17) {
+    if (!m || !out17) return B200_EINVAL;
+    CK(cudaSetDevice(m->device));
+    CR(b200i_prepare_device());
+    CK(cudaStreamSynchronize(m->stream));
+    if (!m->tl_exec) {
+        // every stamped kernel of a step: 5 per layer, 2 all-reduces per layer, the lm_head
+        m->tl_n = 7 * m->c.n_layer + 1;
+        if (cudaMalloc(reinterpret_cast<void**>(&m->tl_stamps), (size_t)3 * m->tl_n * sizeof(unsigned long long)) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            m->tl_stamps = nullptr;
+            return B200_ENOMEM;
+        }
+        Stamps st;
+        st.base = m->tl_stamps;
+        st.n = m->tl_n;
+        CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        const int rc = enqueue_step(m, m->stream, nullptr, nullptr, &st);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+        if (rc != B200_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        CK(e);
+        m->tl_graph = g;
+        CK(cudaGraphInstantiate(&m->tl_exec, g, 0));
+        m->tl_cls = st.cls;
+    }
+    const int n = m->tl_n, used = (int)m->tl_cls.size();
+    CK(cudaMemsetAsync(m->tl_stamps, 0xFF, (size_t)2 * n * sizeof(unsigned long long), m->stream));
+    CK(cudaMemsetAsync(m->tl_stamps + 2 * n, 0, (size_t)n * sizeof(unsigned long long), m->stream));
+    CK(cudaGraphLaunch(m->tl_exec, m->stream));
+    std::vector<unsigned long long> h((size_t)3 * n);
+    CK(cudaMemcpyAsync(h.data(), m->tl_stamps, h.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                       m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    double inc[8] = {0}, own[8] = {0};
+    int cnt[8] = {0};
+    unsigned long long prev = 0, first = 0;
+    for (int i = 0; i < used; ++i) {
+        const unsigned long long e = h[i], w = h[n + i], x = h[2 * n + i];
+        if (x == 0 || w == ~0ull) continue;  // a kernel that stamped nothing
+        if (prev == 0) prev = first = w;     // the step starts when the first stamped kernel may run
+        const int c = m->tl_cls[i];
+        inc[c] += (double)(x > prev ? x - prev : 0) * 1e-3;
+        own[c] += (double)(x > w ? x - w : 0) * 1e-3;
+        cnt[c] += 1;
+        prev = x > prev ? x : prev;
+        (void)e;
+    }
+    for (int c = 0; c < 8; ++c) {
+        out17[c] = (float)inc[c];
+        out17[8 + c] = cnt[c] ? (float)(own[c] / cnt[c]) : 0.f;
+    }
+    out17[16] = (float)((double)(prev - first) * 1e-3);
     return B200_OK;
 }
 

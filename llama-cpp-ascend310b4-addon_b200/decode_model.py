@@ -81,6 +81,7 @@ def _lib():
             "b200_model_time_gate_up": (C.c_int, [P, C.c_int, C.POINTER(C.c_float)]),
             "b200_model_debug_step": (C.c_int, [P, C.c_int, C.c_int, P, P, P]),
             "b200_model_debug_step_ex": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(_StepDump)]),
+            "b200_model_timeline": (C.c_int, [P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -224,6 +225,16 @@ class DecodeModel:
             setattr(sd, name, out[name].ctypes.data_as(C.c_void_p).value)
         B._check(_lib().b200_model_debug_step_ex(self.h, token, pos, C.byref(sd)), "debug_step_ex")
         return out
+
+    def timeline(self) -> dict:
+        """In-step time per kernel class of one captured step
+        (b200_model_timeline): {"step_us", "advance_us": {class: us},
+        "span_us": {class: mean us per kernel}}."""
+        out = (C.c_float * 17)()
+        B._check(_lib().b200_model_timeline(self.h, C.cast(out, C.c_void_p)), "timeline")
+        return {"step_us": float(out[16]),
+                "advance_us": {k: float(out[i]) for i, k in enumerate(PROFILE_CLASSES) if i > 0},
+                "span_us": {k: float(out[8 + i]) for i, k in enumerate(PROFILE_CLASSES) if i > 0}}
 
     def time_gate_up(self, iters: int = 5) -> float:
         """us per gate/up GEMV launch, from a graph of the step's n_layer
