@@ -5,16 +5,19 @@
 //   Y[j][r] = sum_i W[r][i] * X16[j][i]     r < n (weight rows), j < m (tokens)
 //
 // One CTA computes a 128 x BN tile: 128 weight rows (the MMA's M side) by BN
-// tokens (its N side, 64 / 128 / 256), fp32 in BN tensor-memory columns of
-// the 128 lanes.  K runs in stages of 64 halves (one 128-byte swizzle row):
-// thread 0 issues the two TMA boxes of a stage (W 64 x 128, X 64 x BN, both
-// K-major with the 128-byte swizzle), thread 32 issues the stage's four
-// K = 16 MMAs and commits them to the stage's "empty" barrier, which hands
-// the slot back to thread 0; the last commit signals the epilogue, where the
-// four warps read their 32 lanes of the accumulator with tcgen05.ld and
-// store the f32 results (a warp writes 32 consecutive weight rows of one
-// token: 128-byte stores).  Every wait is bounded; a CTA that gives up lets
-// its copies land, drains the MMAs it issued and frees its tensor memory.
+// tokens (its N side, 64 / 128 / 256), in two BN-column tensor-memory
+// accumulators of the 128 lanes.  K runs in stages of 64 halves (one
+// 128-byte swizzle row): thread 0 issues the two TMA boxes of a stage (W 64
+// x 128, X 64 x BN, both K-major with the 128-byte swizzle) into a 4-stage
+// mbarrier ring; thread 32 issues the stage's four K = 16 MMAs and commits
+// them to the stage's "empty" barrier, which hands the slot back to thread
+// 0.  Every 8 stages (a segment) the MMAs switch accumulator and the
+// finished one is committed to the eight epilogue warps, which add it into
+// fp32 registers with tcgen05.ld (two warps per 32-lane quarter, half the
+// columns each) and hand it back; at the end each thread stores its row's
+// sums (a warp writes 32 consecutive weight rows of one token: 128-byte
+// stores).  Every wait is bounded; a CTA that gives up lets its copies
+// land, drains the MMAs it issued and frees its tensor memory.
 // X16 is the activation converted to f16 first (ggml-cpu converts src1 to
 // the F16 weight's vec_dot_type the same way).
 #pragma once
@@ -28,7 +31,6 @@ namespace b200 {
 constexpr int kTcBM = 128;       // weight rows per CTA (MMA M)
 constexpr int kTcBK = 64;        // halves of K per stage: one 128-byte swizzle row
 constexpr int kTcStages = 4;
-constexpr int kTcThreads = 128;  // 4 warps: producer lane, MMA lane, then all four in the epilogue
 
 struct TcArgs {
     CUtensorMap tmw;  // W [n][k] f16, boxes 64 x 128, 128-byte swizzle
@@ -88,22 +90,27 @@ __device__ __forceinline__ void tc_ld_x16(uint32_t (&r)[16], uint32_t taddr) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Accumulators per tile: k-block kb adds into accumulator kb % NACC (each a
-// BN-column slice of tensor memory), and the epilogue sums them in fp32.
-// The tensor core's own accumulation is not IEEE-exact over thousands of
-// products, so shorter chains keep outputs near zero within 1e-3 of an
-// fp32 reference at K = 8192; all 512 columns of tensor memory are used.
-B200_HD constexpr int tc_nacc(int bn) { return bn >= 256 ? 2 : 4; }
+// K runs in segments of kTcSegKb k-blocks (512 halves).  A segment's MMAs
+// accumulate in one of two tensor-memory accumulators (segments alternate),
+// and the epilogue warps drain each finished segment into fp32 registers
+// while the next one is computed.  The tensor core's own accumulation is not
+// IEEE-exact over thousands of products; with chains of 32 MMAs and the
+// segments summed in fp32, outputs stay within 1e-3 of an fp32 reference
+// (elementwise, with the 1e-3 max floor) at K = 8192 -- the same promotion
+// of partial sums to CUDA-core accumulators that FP8 GEMMs use.
+constexpr int kTcSegKb = 8;
+constexpr int kTcEpiWarps = 8;                        // two warps per 32-lane quarter of tensor memory
+constexpr int kTcThreads2 = 64 + 32 * kTcEpiWarps;    // producer warp, MMA warp, epilogue warps
 
 template <int BN>
-__global__ void __launch_bounds__(kTcThreads, 1) gemm_f16_tc_kernel(const __grid_constant__ TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads2, 1) gemm_f16_tc_kernel(const __grid_constant__ TcArgs a) {
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
     constexpr uint32_t A_BYTES = kTcBM * 128u;
     constexpr uint32_t STAGE = tc_stage_bytes(BN);
-    constexpr int NACC = tc_nacc(BN);
-    constexpr uint32_t TMEM_COLS = NACC * BN;  // a power of two >= 32, <= 512
+    constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators; a power of two <= 512
+    constexpr int HALF = BN / 2;            // columns per epilogue thread
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2], done;
     __shared__ uint32_t tmem_base;
     __shared__ int issued, consumed, aborted;
 
@@ -111,17 +118,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_f16_tc_kernel(const __grid
     const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const int64_t n0 = (int64_t)blockIdx.y * kTcBM, m0 = (int64_t)blockIdx.x * BN;
     const int kb_total = (int)((a.k + kTcBK - 1) / kTcBK);
+    const int nseg = (kb_total + kTcSegKb - 1) / kTcSegKb;
 
-    if (warp == 0) {
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                      "r"(TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (tid == 32) {
+    if (tid == 0) {
         for (int s = 0; s < kTcStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+        }
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(&accf[q], 1);
+            mbar_init(&acce[q], kTcEpiWarps);  // one arrival per epilogue warp
         }
         mbar_init(&done, 1);
         issued = consumed = aborted = 0;
@@ -131,6 +143,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_f16_tc_kernel(const __grid
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base;
+
+    float acc[HALF];
+#pragma unroll
+    for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
 
     if (tid == 0) {
         // producer: a stage's slot is reused once the MMAs that read it committed
@@ -148,27 +164,64 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_f16_tc_kernel(const __grid
         }
         issued = kb;
     } else if (tid == 32) {
-        // MMA issuer
+        // MMA issuer: segment g into accumulator g % 2, once the epilogue
+        // has drained that accumulator's previous segment
         constexpr uint32_t idesc = tc_idesc_f16<BN>();
         int kb = 0;
-        for (; kb < kb_total; ++kb) {
-            const int s = kb % kTcStages;
-            if (!mbar_wait_bounded(&full[s], (uint32_t)((kb / kTcStages) & 1))) {
+        for (int g = 0; g < nseg && !aborted; ++g) {
+            const int q = g & 1;
+            if (g >= 2 && !mbar_wait_bounded(&acce[q], (uint32_t)(((g >> 1) - 1) & 1))) {
                 aborted = 1;
                 break;
             }
             tc_fence_after();
-            const uint32_t st = sbase + (uint32_t)s * STAGE;
-            const uint64_t da = tc_desc_sw128(st), db = tc_desc_sw128(st + A_BYTES);
-            const uint32_t acc = tmem + (uint32_t)((kb % NACC) * BN);
+            const uint32_t d = tmem + (uint32_t)(q * BN);
+            const int kb_end = min(kb_total, (g + 1) * kTcSegKb);
+            for (; kb < kb_end; ++kb) {
+                const int s = kb % kTcStages;
+                if (!mbar_wait_bounded(&full[s], (uint32_t)((kb / kTcStages) & 1))) {
+                    aborted = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = sbase + (uint32_t)s * STAGE;
+                const uint64_t da = tc_desc_sw128(st), db = tc_desc_sw128(st + A_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < kTcBK / 16; ++kk)
-                tc_mma_f16(acc, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), idesc, (kb >= NACC || kk > 0) ? 1 : 0);
-            tc_commit(&empty[s]);
+                for (int kk = 0; kk < kTcBK / 16; ++kk)
+                    tc_mma_f16(d, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), idesc,
+                               (kb > g * kTcSegKb || kk > 0) ? 1 : 0);
+                tc_commit(&empty[s]);
+            }
+            if (aborted) break;
+            tc_commit(&accf[q]);  // the segment's sum is complete in accumulator q
         }
         consumed = kb;
+    } else if (warp >= 2) {
+        // epilogue warps: drain every segment into fp32 registers
+        const int e = warp - 2;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's tensor-memory lanes
+        const uint32_t col0 = (uint32_t)((e >> 2) * HALF);              // this warp's half of the columns
+        for (int g = 0; g < nseg; ++g) {
+            const int q = g & 1;
+            if (!mbar_wait_bounded(&accf[q], (uint32_t)((g >> 1) & 1))) {
+                aborted = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t taddr = tmem + lane_base + (uint32_t)(q * BN) + col0;
+#pragma unroll
+            for (int c = 0; c < HALF; c += 16) {
+                uint32_t v[16];
+                tc_ld_x16(v, taddr + (uint32_t)c);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[c + j] = __fadd_rn(acc[c + j], __uint_as_float(v[j]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acce[q])) : "memory");
+        }
     }
-    __syncthreads();  // both loops are over
+    __syncthreads();  // every loop is over
     if (tid == 32) {
         if (aborted) {
             // copies issued but never consumed must land before the CTA exits
@@ -177,42 +230,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_f16_tc_kernel(const __grid
         }
         tc_commit(&done);  // every MMA issued above has completed
     }
-    __syncwarp();
     mbar_wait_drain(&done, 0);
     tc_fence_after();
-    if (!aborted) {
-        const int row = warp * 32 + lane;
-        const int64_t r = n0 + row;
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-        const int nacc = kb_total < NACC ? kb_total : NACC;  // accumulators some k-block wrote
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-            if (m0 + c0 >= a.m) break;  // uniform over the CTA: no warp skips a collective load it needs
-            float sum[16];
-            {
-                uint32_t v[16];
-                tc_ld_x16(v, taddr + (uint32_t)c0);
+    if (!aborted && warp >= 2) {
+        const int e = warp - 2;
+        const int64_t r = n0 + (warp & 3) * 32 + lane;
+        const int64_t t0 = m0 + (e >> 2) * HALF;
+        if (r < a.n) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) sum[j] = __uint_as_float(v[j]);
-            }
-            for (int q = 1; q < nacc; ++q) {  // accumulators in order 0, 1, ...: the same sum on every run
-                uint32_t v[16];
-                tc_ld_x16(v, taddr + (uint32_t)(q * BN + c0));
-#pragma unroll
-                for (int j = 0; j < 16; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(v[j]));
-            }
-            if (r < a.n) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int64_t t = m0 + c0 + j;
-                    if (t < a.m) a.y[t * a.ldy + r] = sum[j];
-                }
+            for (int j = 0; j < HALF; ++j) {
+                const int64_t t = t0 + j;
+                if (t < a.m) a.y[t * a.ldy + r] = acc[j];
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
     }

@@ -705,11 +705,8 @@ int b200_mul_mat_f16_tc(const void* w, const float* x, float* y, int64_t n, int6
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return B200_EINVAL;
     const cudaStream_t st = (cudaStream_t)stream;
-    // tile width: 256 tokens keeps the weight tile's reuse highest, but only
-    // two 256-column accumulators fit in tensor memory; for K >= 4096 the
-    // tile is 128 wide with four accumulators (shorter accumulation chains:
-    // outputs near zero stay within 1e-3 of an fp32 reference at K = 8192)
-    const int bn = m <= 64 ? 64 : (m <= 128 || k >= 4096) ? 128 : 256;
+    // tile width: the fewest token tiles (each re-reads the weight tile)
+    const int bn = m <= 64 ? 64 : m <= 128 ? 128 : 256;
     const int slot = bn == 64 ? 0 : bn == 128 ? 1 : 2;
     {
         std::lock_guard<std::mutex> lk(g_attr_mu);
@@ -760,9 +757,9 @@ int b200_mul_mat_f16_tc(const void* w, const float* x, float* y, int64_t n, int6
     const dim3 grid((unsigned)((m + bn - 1) / bn), (unsigned)((n + kTcBM - 1) / kTcBM), 1);
     const size_t smem = tc_smem_bytes(bn);
     switch (bn) {
-        case 64: gemm_f16_tc_kernel<64><<<grid, kTcThreads, smem, st>>>(a); break;
-        case 128: gemm_f16_tc_kernel<128><<<grid, kTcThreads, smem, st>>>(a); break;
-        default: gemm_f16_tc_kernel<256><<<grid, kTcThreads, smem, st>>>(a); break;
+        case 64: gemm_f16_tc_kernel<64><<<grid, kTcThreads2, smem, st>>>(a); break;
+        case 128: gemm_f16_tc_kernel<128><<<grid, kTcThreads2, smem, st>>>(a); break;
+        default: gemm_f16_tc_kernel<256><<<grid, kTcThreads2, smem, st>>>(a); break;
     }
     return cuda_status(cudaGetLastError());
 }

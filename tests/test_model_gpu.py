@@ -252,3 +252,28 @@ def test_synthetic_model_regenerates_bit_for_bit_on_host():
         np.testing.assert_array_equal(m.export_kv(l, 0, 40).view(np.uint16), kc[l][:40].view(np.uint16))
         np.testing.assert_array_equal(m.export_kv(l, 1, 40).view(np.uint16), vc[l][:40].view(np.uint16))
     m.close()
+
+
+def test_step_timeline_adds_up():
+    """b200_model_timeline: a captured step with device-clock stamps; the
+    per-class advances add up to the step and every class ran."""
+    import decode_model as M
+
+    cfg = M.LlamaConfig(**SMALL)
+    m = M.DecodeModel(cfg)
+    m.init_synthetic(seed=5)
+    m.fill_kv_synthetic(seed=6, n_pos=20)
+    m.capture()
+    m.set_state(42, 20, advance=True)
+    m.timeline()
+    tl = m.timeline()
+    assert tl["step_us"] > 0
+    adv = tl["advance_us"]
+    assert abs(sum(adv.values()) - tl["step_us"]) <= 1e-3 * tl["step_us"] + 0.01
+    for k in ("qkv", "attn", "o", "gate_up", "down", "lm_head"):
+        assert tl["span_us"][k] > 0, k
+    assert adv["allreduce"] == 0.0  # one GPU: no all-reduce kernels
+    import b200_decode as B
+
+    assert B.device_status(reset=True) == 0
+    m.close()
