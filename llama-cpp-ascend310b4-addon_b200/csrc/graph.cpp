@@ -19,6 +19,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/b200_graph.h"
@@ -335,18 +336,19 @@ int run_fa(b200_backend* be, b200_tensor* op) {
                           op_f32(op, 0), ws, be->fa_ws_bytes, S(be));
 }
 
-// Does any node after index i read nodes[i]?  (other than `except`)
-bool read_later(b200_tensor* const* nodes, int n, int i, const b200_tensor* except) {
-    const b200_tensor* t = nodes[i];
-    for (int j = i + 1; j < n; ++j) {
-        if (nodes[j] == except) continue;
+// How many source slots of the graph's nodes name each tensor.
+using Readers = std::unordered_map<const b200_tensor*, int>;
+
+Readers count_readers(b200_tensor* const* nodes, int n) {
+    Readers r;
+    r.reserve((size_t)n * 2);
+    for (int j = 0; j < n; ++j)
         for (int s = 0; s < B200_MAX_SRC; ++s)
-            if (nodes[j]->src[s] == t) return true;
-    }
-    return false;
+            if (nodes[j]->src[s] != nullptr) ++r[nodes[j]->src[s]];
+    return r;
 }
 
-int run_node(b200_backend* be, b200_tensor* const* nodes, int n, int i, int* skip) {
+int run_node(b200_backend* be, b200_tensor* const* nodes, int n, int i, int* skip, const Readers& readers) {
     b200_tensor* op = nodes[i];
     const b200_tensor* a = op->src[0];
     const b200_tensor* b = op->src[1];
@@ -363,8 +365,9 @@ int run_node(b200_backend* be, b200_tensor* const* nodes, int n, int i, int* ski
             if (i + 1 < n) {
                 b200_tensor* nx = nodes[i + 1];
                 const b200_tensor* wv = nx->src[1];
+                const auto it = readers.find(op);
                 if (nx->op == B200_OP_MUL && nx->src[0] == op && f32_rows(wv) && nelements(wv) == cols &&
-                    f32_rows(nx) && !read_later(nodes, n, i, nx)) {
+                    f32_rows(nx) && wv != op && it != readers.end() && it->second == 1) {
                     *skip = 1;
                     return b200_rms_norm_f32(static_cast<const float*>(a->data), static_cast<const float*>(wv->data),
                                              static_cast<float*>(nx->data), cols, rows, eps, S(be));
@@ -640,6 +643,9 @@ int b200_graph_compute(b200_backend* be, b200_tensor* const* nodes, int n_nodes)
     be->failed = -1;
     CR(ck(cudaSetDevice(be->device), "set device"));
     const Config c = config();
+    for (int i = 0; i < n_nodes; ++i)
+        if (nodes[i] == nullptr) return B200_EINVAL;
+    const Readers readers = count_readers(nodes, n_nodes);
     for (int i = 0; i < n_nodes; ++i) {
         b200_tensor* op = nodes[i];
         if (!b200_supports_op(op)) {
@@ -656,7 +662,7 @@ int b200_graph_compute(b200_backend* be, b200_tensor* const* nodes, int n_nodes)
             nvtxRangePushA(label);
         }
         int skip = 0;
-        int rc = run_node(be, nodes, n_nodes, i, &skip);
+        int rc = run_node(be, nodes, n_nodes, i, &skip, readers);
         if (rc == B200_OK && trace) rc = ck(cudaStreamSynchronize(be->stream), "node synchronize");
         if (c.flags & B200_CFG_NVTX) nvtxRangePop();
         if (rc != B200_OK) {
