@@ -396,7 +396,8 @@ def run_ours(args):
                          "step_bytes": step_bytes,
                          "step_frac": step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak},
             "kernel_us": prof,
-            "step_breakdown_us": {"step": tl["step_us"], "advance": tl["advance_us"], "span": tl["span_us"]},
+            "step_breakdown_us": {"step": tl["step_us"], "advance": tl["advance_us"], "span": tl["span_us"],
+                                  "phases": tl["phases_us"]},
             "clocks": clk,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4},
             "gpu_launches": launches_per_step * args.steps,

@@ -157,6 +157,21 @@ int b200_model_profile(b200_model *m, int iters, float *us_per_class8);
  * stamped. */
 int b200_model_timeline(b200_model *m, float *out17);
 
+/* Phases inside the kernels of the last b200_model_timeline step, per kernel
+ * class c (as above), means over the step's kernels of that class, in
+ * microseconds from the class's return from the wait on the previous kernel
+ * (w = the earliest CTA's return):
+ *   out[8c + 0]  w minus the earliest CTA's entry (how early the kernel was
+ *                resident under programmatic launch);
+ *   out[8c + 1..3]  the LATEST CTA at: input ready (GEMV: activation in shared
+ *                memory; attention: q loaded; all-reduce: every rank
+ *                announced), first streamed chunk landed, main loop done;
+ *   out[8c + 4]  the latest CTA's exit (the span of out17[8 + c]);
+ *   out[8c + 5..7]  the EARLIEST CTA at the three marks.
+ * A mark a class does not have reads 0.  B200_EINVAL before the first
+ * b200_model_timeline call. */
+int b200_model_timeline_phases(b200_model *m, float *out64);
+
 /* The gate/up GEMV alone: one CUDA graph of the n_layer gate/up launches of
  * the step (each layer's own weights, chained as in the step), replayed
  * `iters` times between CUDA events on the model's stream; *us_per_launch is

@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const ArArgs a
     }
     bool ok = true;
     for (int r = 0; r < a.world; ++r) ok = ok && wait_flag_geq(&a.flags[r], seq);
+    if (threadIdx.x == 0) stamp_point(a.stamp, a.stamp_stride, 3);  // every rank's partial is announced
     if (!ok) {
         if (threadIdx.x == 0) stamp_point(a.stamp, a.stamp_stride, 2);
         return;

@@ -202,9 +202,14 @@ struct GemvArgs {
     const StepState* ar_st;
     // Timeline stamps (globaltimer ns), when set: [0] earliest CTA entry,
     // [n] earliest return from griddepcontrol.wait, [2n] latest CTA exit,
-    // n = stamp_stride (atomicMin / atomicMax by one thread per CTA).
+    // [3n..5n] latest and [6n..8n] earliest CTA at the phase marks (input
+    // ready, first chunk landed, main loop done), n = stamp_stride
+    // (atomicMin / atomicMax by one thread per CTA).
     unsigned long long* stamp;
     int stamp_stride;
+    // The weight stream is read with the evict_first L2 policy when set
+    // (weights are read once per step).
+    int l2_ef;
 };
 
 constexpr int kFaThreads = 128;
@@ -235,6 +240,9 @@ struct FaArgs {
     CUtensorMap tmk, tmv;
     unsigned long long* stamp;  // timeline stamps as GemvArgs::stamp
     int stamp_stride;
+    // Tensor-core kernel: K and V are read with the evict_first L2 policy
+    // when set (as GemvArgs::l2_ef).
+    int l2_ef;
 };
 
 // Small-M F16 matmul (gemm_small.cuh).

@@ -110,18 +110,43 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// L2 eviction policy for a copy: evict_first for data read once per step,
+// evict_normal otherwise.
+__device__ __forceinline__ uint64_t l2_policy(bool evict_first) {
+    uint64_t p;
+    if (evict_first)
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    else
+        asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// bulk_g2s with an L2 cache policy.
+__device__ __forceinline__ void bulk_g2s_pol(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 __device__ __forceinline__ void record_status(unsigned int bit) { atomicOr(&g_status, bit); }
 
 // Kernel timeline (b200_model_timeline): one thread per CTA folds the
 // globaltimer into slot s[which * stride] -- which 0: entry (min), 1: return
-// from griddepcontrol.wait (min), 2: exit (max).  No-ops when s is null.
+// from griddepcontrol.wait (min), 2: exit (max); 3, 4, 5: phase marks inside
+// the kernel (input ready, first streamed data landed, main loop done), each
+// folded as a max into s[which * stride] and as a min into
+// s[(which + 3) * stride].  No-ops when s is null.
 __device__ __forceinline__ void stamp_point(unsigned long long* s, int stride, int which) {
     if (s == nullptr) return;
     const unsigned long long t = globaltimer();
-    if (which < 2)
+    if (which < 2) {
         atomicMin(s + (int64_t)which * stride, t);
-    else
-        atomicMax(s + (int64_t)2 * stride, t);
+    } else {
+        atomicMax(s + (int64_t)which * stride, t);
+        if (which > 2) atomicMin(s + (int64_t)(which + 3) * stride, t);
+    }
 }
 
 // Programmatic dependent launch.  A kernel launched with programmatic stream

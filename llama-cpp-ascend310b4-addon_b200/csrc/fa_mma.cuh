@@ -65,13 +65,15 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t r[4], uint32_t addr) {
 }
 
 // 3-D tiled TMA load of one box into this CTA's shared memory; completion
-// is counted on `bar`.  x (the head_dim coordinate) is a multiple of 64
-// halves, so its byte offset is 16-byte aligned.
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
+// is counted on `bar`; `pol` is the L2 policy (l2_policy).  x (the head_dim
+// coordinate) is a multiple of 64 halves, so its byte offset is 16-byte
+// aligned.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z, uint64_t* bar,
+                                            uint64_t pol) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];" ::"r"(dst),
-        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4}], [%5], %6;" ::"r"(dst),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
 
@@ -149,6 +151,7 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
 
     // this group's chunks: c_begin + grp + kFmGroups * i, i < ncg
     const int ncg = active ? (c_end - c_begin - grp + kFmGroups - 1) / kFmGroups : 0;
+    const uint64_t pol = l2_policy(a.l2_ef != 0);
     if (ncg <= 0) {
         griddep_wait();
         griddep_launch_dependents();
@@ -166,8 +169,8 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
             mbar_arrive_expect_tx(&bars[st], 2 * TILE);
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
-                tma_load_3d(kdst + b * BOXB, &a.tmk, 64 * b, hk, p0, &bars[st]);
-                tma_load_3d(kdst + TILE + b * BOXB, &a.tmv, 64 * b, hk, p0, &bars[st]);
+                tma_load_3d(kdst + b * BOXB, &a.tmk, 64 * b, hk, p0, &bars[st], pol);
+                tma_load_3d(kdst + TILE + b * BOXB, &a.tmv, 64 * b, hk, p0, &bars[st], pol);
             }
         };
         const int c_new = (ctx - 1) / kFaChunk;  // the chunk holding the newest row
@@ -199,12 +202,14 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
             }
         }
         group_sync(grp);  // barrier init visible to the group
+        if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 3);
 
         int ci = 0;
         for (; ci < ncg; ++ci) {
             const int c = cfirst + kFmGroups * ci;
             const int stage = ci % kFmStages;
             if (!mbar_wait_bounded(&bars[stage], (uint32_t)((ci / kFmStages) & 1))) fabort[grp] = 1;
+            if (ci == 0 && tid == 0) stamp_point(a.stamp, a.stamp_stride, 4);
             // V rows at or past the context hold no cache data: zero them
             const int valid = ctx - c * kFaChunk;
             if (valid < kFaChunk) {
@@ -326,6 +331,7 @@ __global__ void __launch_bounds__(fm_threads(G)) fa_mma_kernel(const __grid_cons
     float* co = wo + NW * kFaMaxG * WS;                       // [kFaMaxG][D]  this CTA's partial
     __shared__ float cm[kFaMaxG], cl[kFaMaxG], ew[NW][kFaMaxG];
     __syncthreads();  // the rings are no longer read
+    if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 5);
     if (g == 0) {
         wm[warp][2 * t] = m_run[0];
         wm[warp][2 * t + 1] = m_run[1];

@@ -449,10 +449,12 @@ __device__ __forceinline__ float4 norm_unit(float4 v, float4 w, float nscale) {
 // clamped to the last half-block, stores only for real ones).  The sum of
 // squares runs over each thread's values in order.  `after_issue` runs once
 // the first loads are in flight (the caller issues its remaining weight
-// copies there).  Ends with __syncthreads.
+// copies there).  `wpre`: this thread's norm weights of round 0, loaded by
+// the caller before its wait on the previous kernel (norm_w is constant).
+// Ends with __syncthreads.
 template <bool AR, class AfterIssue>
 __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan& P, uint8_t* xr, float* red, int tid,
-                                              int lane, int warp, AfterIssue after_issue) {
+                                              int lane, int warp, const float4 (&wpre)[4], AfterIssue after_issue) {
     const bool norm = a.pro == PRO_RMSNORM;
     const int nh = 2 * P.U;  // half-blocks of x
     const int rounds = (nh + kGemvThreads - 1) / kGemvThreads;
@@ -494,7 +496,7 @@ __device__ __forceinline__ void activation_q8(const GemvArgs& a, const GemvPlan&
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             xv[j] = ldx(4 * h + j);
-            if (norm) wv[j] = w4[4 * h + j];
+            if (norm) wv[j] = r == 0 ? wpre[j] : w4[4 * h + j];
         }
     };
     load(0);
@@ -722,6 +724,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     // below keeps the same order, so no division is needed on the hot path.
     int64_t irow = 0;
     int ic = P.rpc > 1 ? 0 : (int)(q_begin % P.nchunk);
+    const uint64_t pol = l2_policy(a.l2_ef != 0);
     auto issue = [&](int s) {
         uint8_t* dst = ring + (int64_t)s * P.stage_bytes;
         uint64_t* bar = &bars[s];
@@ -730,7 +733,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             const int64_t nr = min((int64_t)P.rpc, P.n - r0);
             const uint32_t bytes = (uint32_t)(nr * P.rs);
             mbar_arrive_expect_tx(bar, bytes);
-            bulk_g2s(dst, a.w + r0 * P.rs, bytes, bar);
+            bulk_g2s_pol(dst, a.w + r0 * P.rs, bytes, bar, pol);
             irow += P.rpc;
         } else {
             const int64_t row = row_begin + irow;
@@ -740,22 +743,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             const uint32_t b0 = (uint32_t)(16 * nu);
             if constexpr (FMT == FMT_F16) {
                 mbar_arrive_expect_tx(bar, b0);
-                bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
+                bulk_g2s_pol(dst, base + 16 * (int64_t)u0, b0, bar, pol);
             } else if constexpr (FMT == FMT_Q8) {
                 const uint32_t b1 = (uint32_t)pad16(2 * nu);
                 mbar_arrive_expect_tx(bar, 2 * b0 + b1);
-                bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
-                bulk_g2s(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 16 * (int64_t)u0, b0, bar);
-                bulk_g2s(dst + 32 * P.kc, base + 32 * (int64_t)P.U + 2 * (int64_t)u0, b1, bar);
+                bulk_g2s_pol(dst, base + 16 * (int64_t)u0, b0, bar, pol);
+                bulk_g2s_pol(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 16 * (int64_t)u0, b0, bar, pol);
+                bulk_g2s_pol(dst + 32 * P.kc, base + 32 * (int64_t)P.U + 2 * (int64_t)u0, b1, bar, pol);
             } else if constexpr (FMT == FMT_A8) {
                 mbar_arrive_expect_tx(bar, 2 * b0);
-                bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
-                bulk_g2s(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 16 * (int64_t)u0, b0, bar);
+                bulk_g2s_pol(dst, base + 16 * (int64_t)u0, b0, bar, pol);
+                bulk_g2s_pol(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 16 * (int64_t)u0, b0, bar, pol);
             } else {
                 const uint32_t b1 = (uint32_t)pad16(2 * nu);
                 mbar_arrive_expect_tx(bar, b0 + b1);
-                bulk_g2s(dst, base + 16 * (int64_t)u0, b0, bar);
-                bulk_g2s(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 2 * (int64_t)u0, b1, bar);
+                bulk_g2s_pol(dst, base + 16 * (int64_t)u0, b0, bar, pol);
+                bulk_g2s_pol(dst + 16 * P.kc, base + 16 * (int64_t)P.U + 2 * (int64_t)u0, b1, bar, pol);
             }
             if (++ic == P.nchunk) {
                 ic = 0;
@@ -764,6 +767,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         }
     };
 
+    // Lane 0: the rest of the ring's first S stages (stage 0 goes before the
+    // wait on the previous kernel).
+    auto issue_rest = [&]() {
+        for (int s = 1; s < S && s < nq; ++s) issue(s);
+    };
+    // The norm weights are constant: round 0 of them is loaded before the
+    // first weight copies and the wait on the previous kernel, so that after
+    // the wait the prologue waits only for x (an L2 hit), not for an HBM
+    // read queued behind every SM's copies.
+    float4 wpre[4] = {};
+    if constexpr (FMT == FMT_Q4 || FMT == FMT_Q8) {
+        if (a.pro == PRO_RMSNORM && a.xq_in == nullptr) {
+            const int h = min(tid, 2 * P.U - 1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) wpre[j] = reinterpret_cast<const float4*>(a.norm_w)[4 * h + j];
+        }
+    }
     if (lane == 0) {
         for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
         mbar_fence_init();
@@ -798,8 +818,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
 #pragma unroll
                 for (int i = 0; i < RC; ++i)
                     if (base + tid + i * kGemvThreads < n16) t[i] = src[base + tid + i * kGemvThreads];
-                if (base == 0 && lane == 0)
-                    for (int s = 1; s < S && s < nq; ++s) issue(s);
+                if (base == 0 && lane == 0) issue_rest();
 #pragma unroll
                 for (int i = 0; i < RC; ++i)
                     if (base + tid + i * kGemvThreads < n16) dst[base + tid + i * kGemvThreads] = t[i];
@@ -807,19 +826,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             if (tid == 0 && (P.U & 1))  // 40 U is a multiple of 8 only: the last 8 bytes
                 reinterpret_cast<int2*>(xr)[5 * (int64_t)P.U - 1] = reinterpret_cast<const int2*>(a.xq_in)[5 * (int64_t)P.U - 1];
         } else {
-            activation_q8<AR>(a, P, xr, red, tid, lane, warp, [&] {
-                if (lane == 0)
-                    for (int s = 1; s < S && s < nq; ++s) issue(s);
+            activation_q8<AR>(a, P, xr, red, tid, lane, warp, wpre, [&] {
+                if (lane == 0) issue_rest();
             });
         }
     } else if constexpr (FMT == FMT_A8) {
         activation_a8(a, P, xr, red, tid, lane, warp, [&] {
-            if (lane == 0)
-                for (int s = 1; s < S && s < nq; ++s) issue(s);
+            if (lane == 0) issue_rest();
         });
     } else {
-        if (lane == 0)
-            for (int s = 1; s < S && s < nq; ++s) issue(s);
+        if (lane == 0) issue_rest();
         float nscale = 1.f;
         if (norm) {
             double ss = 0.0;
@@ -845,6 +861,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         }
     }
     __syncthreads();  // activation ready; also publishes every warp's barrier init
+    if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 3);
 
     // ---- stream this warp's chunks ----
     using Acc = typename GemvTraits<FMT>::Acc;
@@ -879,6 +896,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             }
             break;  // the status word records the timeout; still meet the CTA barrier below
         }
+        if (q == 0 && tid == 0) stamp_point(a.stamp, a.stamp_stride, 4);
         const uint8_t* st = ring + (int64_t)s * P.stage_bytes;
         if (P.rpc > 1) {
             const int64_t r0 = row_begin + crow;
@@ -931,6 +949,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     }
     if (P.rpc == 1) {
         __syncthreads();  // all row partials of the CTA are in shared memory
+        if (tid == 0) stamp_point(a.stamp, a.stamp_stride, 5);
         const int64_t nrows = cr1 - cr0;
         if constexpr (FMT == FMT_A8) {
             for (int64_t r = tid; r < nrows; r += kGemvThreads)

@@ -125,6 +125,9 @@ struct b200_model {
     // the o projection's (img_att); those GEMVs copy the image instead of
     // quantising in every CTA.
     bool xq_fused = true;
+    // Weight and KV streams of the step are read with the evict_first L2
+    // policy (on unless B200_L2_EF=0).
+    int l2_ef = 1;
     uint8_t* img_h = nullptr;
     uint8_t* img_att = nullptr;
     unsigned int* img_tickets = nullptr;
@@ -146,6 +149,7 @@ struct b200_model {
     // b200_model_timeline: a second captured step whose kernels fold
     // globaltimer stamps into tl_stamps ([3][tl_n]), classes in tl_cls
     unsigned long long* tl_stamps = nullptr;
+    std::vector<unsigned long long> tl_host;  // the last timeline step's stamps, [9][tl_n]
     int tl_n = 0;
     std::vector<int> tl_cls;
     cudaGraph_t tl_graph = nullptr;
@@ -244,7 +248,8 @@ float* part_buf(b200_model* m, int which) { return reinterpret_cast<float*>(m->c
 // collective `idx` of the step.
 // Timeline stamps of one step (b200_model_timeline): kernel i of the step
 // folds its entry / post-wait / exit times into base[i], base[n + i],
-// base[2n + i]; cls[i] is its kernel class (PROFILE classes of b200_model.h).
+// base[2n + i] and its phase marks into base[(3..8)n + i]; cls[i] is its
+// kernel class (PROFILE classes of b200_model.h).
 struct Stamps {
     unsigned long long* base = nullptr;
     int n = 0, next = 0;
@@ -491,10 +496,12 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         return b200i_image_to_q8_0(img, k / 32, xq, s);
     };
     if (dump && dump->x) CK(dcopy(dump->x, m->x, d * sizeof(float)));
+    auto l2 = [&](GemvArgs& a) { a.l2_ef = m->l2_ef; };
     for (int l = 0; l < c.n_layer; ++l) {
         CR(B(1));
         {
             GemvArgs a = qkv_args(m, l);
+            l2(a);
             bool dbg = false;
             if (dump)
                 dbg = hook(a, dump->xq_qkv ? dump->xq_qkv + (size_t)l * (d / 32) * 34 : nullptr,
@@ -512,6 +519,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         CR(B(2));
         {
             FaArgs f = fa_args(m, l);
+            f.l2_ef = m->l2_ef;
             if (stamps) stamps->assign(f, 2);
             CR(b200i_fa(f, D, s, pdl));
         }
@@ -520,6 +528,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         CR(B(3));
         {
             GemvArgs a = proj_args(m, l, 0);
+            l2(a);
             bool dbg = false;
             if (dump) {
                 uint8_t* xq = dump->xq_o ? dump->xq_o + (size_t)l * (qd / 32) * 34 : nullptr;
@@ -539,6 +548,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         CR(B(4));
         {
             GemvArgs a = gate_up_args(m, l);
+            l2(a);
             bool dbg = false;
             if (dump)
                 dbg = hook(a, dump->xq_gu ? dump->xq_gu + (size_t)l * (d / 32) * 34 : nullptr,
@@ -551,6 +561,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
         CR(B(5));
         {
             GemvArgs a = proj_args(m, l, 1);
+            l2(a);
             bool dbg = false;
             if (dump) {
                 uint8_t* xq = dump->xq_down ? dump->xq_down + (size_t)l * (m->ff / 32) * 34 : nullptr;
@@ -571,6 +582,7 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
     CR(B(6));
     {
         GemvArgs a = head_args(m);
+        l2(a);
         bool dbg = false;
         if (dump) dbg = hook(a, dump->xq_head, dump->dots_head);
         if (stamps) stamps->assign(a, 6);
@@ -663,6 +675,8 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
     m->device = device;
     if (const char* e = getenv("B200_PDL")) m->pdl = atoi(e) != 0;
     if (const char* e = getenv("B200_XQ_FUSED")) m->xq_fused = atoi(e) != 0;
+    if (const char* e = getenv("B200_L2_EF")) m->l2_ef = atoi(e) != 0;
+
     m->rank = tp_rank;
     m->world = tp_world;
     const b200_llama_config& c = m->c;
@@ -1050,7 +1064,7 @@ int b200_model_timeline(b200_model* m, float* out17) {
     if (!m->tl_exec) {
         // every stamped kernel of a step: 5 per layer, 2 all-reduces per layer, the lm_head
         m->tl_n = 7 * m->c.n_layer + 1;
-        if (cudaMalloc(reinterpret_cast<void**>(&m->tl_stamps), (size_t)3 * m->tl_n * sizeof(unsigned long long)) !=
+        if (cudaMalloc(reinterpret_cast<void**>(&m->tl_stamps), (size_t)9 * m->tl_n * sizeof(unsigned long long)) !=
             cudaSuccess) {
             cudaGetLastError();
             m->tl_stamps = nullptr;
@@ -1073,10 +1087,13 @@ int b200_model_timeline(b200_model* m, float* out17) {
         m->tl_cls = st.cls;
     }
     const int n = m->tl_n, used = (int)m->tl_cls.size();
+    // min slots (entry, post-wait, earliest phase marks) start at ~0, max slots at 0
     CK(cudaMemsetAsync(m->tl_stamps, 0xFF, (size_t)2 * n * sizeof(unsigned long long), m->stream));
-    CK(cudaMemsetAsync(m->tl_stamps + 2 * n, 0, (size_t)n * sizeof(unsigned long long), m->stream));
+    CK(cudaMemsetAsync(m->tl_stamps + 2 * n, 0, (size_t)4 * n * sizeof(unsigned long long), m->stream));
+    CK(cudaMemsetAsync(m->tl_stamps + 6 * n, 0xFF, (size_t)3 * n * sizeof(unsigned long long), m->stream));
     CK(cudaGraphLaunch(m->tl_exec, m->stream));
-    std::vector<unsigned long long> h((size_t)3 * n);
+    std::vector<unsigned long long>& h = m->tl_host;
+    h.assign((size_t)9 * n, 0);
     CK(cudaMemcpyAsync(h.data(), m->tl_stamps, h.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
                        m->stream));
     CK(cudaStreamSynchronize(m->stream));
@@ -1099,6 +1116,35 @@ int b200_model_timeline(b200_model* m, float* out17) {
         out17[8 + c] = cnt[c] ? (float)(own[c] / cnt[c]) : 0.f;
     }
     out17[16] = (float)((double)(prev - first) * 1e-3);
+    return B200_OK;
+}
+
+int b200_model_timeline_phases(b200_model* m, float* out64) {
+    if (!m || !out64) return B200_EINVAL;
+    const int n = m->tl_n, used = (int)m->tl_cls.size();
+    if (m->tl_host.size() != (size_t)9 * n || n == 0) return B200_EINVAL;  // no timeline step yet
+    const std::vector<unsigned long long>& h = m->tl_host;
+    double sum[8][8] = {};
+    int cnt[8][8] = {};
+    for (int i = 0; i < used; ++i) {
+        const unsigned long long e = h[i], w = h[n + i], x = h[2 * n + i];
+        if (x == 0 || w == ~0ull || e == ~0ull) continue;
+        const int c = m->tl_cls[i];
+        auto add = [&](int j, unsigned long long t, unsigned long long from, bool valid) {
+            if (!valid) return;
+            sum[c][j] += (double)((long long)t - (long long)from) * 1e-3;
+            cnt[c][j] += 1;
+        };
+        add(0, w, e, true);
+        for (int k = 0; k < 3; ++k) {
+            const unsigned long long hi = h[(size_t)(3 + k) * n + i], lo = h[(size_t)(6 + k) * n + i];
+            add(1 + k, hi, w, hi != 0);
+            add(5 + k, lo, w, lo != ~0ull);
+        }
+        add(4, x, w, true);
+    }
+    for (int c = 0; c < 8; ++c)
+        for (int j = 0; j < 8; ++j) out64[c * 8 + j] = cnt[c][j] ? (float)(sum[c][j] / cnt[c][j]) : 0.f;
     return B200_OK;
 }
 

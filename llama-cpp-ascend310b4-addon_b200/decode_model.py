@@ -82,6 +82,7 @@ def _lib():
             "b200_model_debug_step": (C.c_int, [P, C.c_int, C.c_int, P, P, P]),
             "b200_model_debug_step_ex": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(_StepDump)]),
             "b200_model_timeline": (C.c_int, [P, P]),
+            "b200_model_timeline_phases": (C.c_int, [P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -229,12 +230,19 @@ class DecodeModel:
     def timeline(self) -> dict:
         """In-step time per kernel class of one captured step
         (b200_model_timeline): {"step_us", "advance_us": {class: us},
-        "span_us": {class: mean us per kernel}}."""
+        "span_us": {class: mean us per kernel}, "phases_us": {class: {mark:
+        us after the class's wait}}} (b200_model_timeline_phases)."""
         out = (C.c_float * 17)()
         B._check(_lib().b200_model_timeline(self.h, C.cast(out, C.c_void_p)), "timeline")
+        ph = (C.c_float * 64)()
+        B._check(_lib().b200_model_timeline_phases(self.h, C.cast(ph, C.c_void_p)), "timeline_phases")
+        marks = ("resident_before_wait", "input_ready", "first_chunk", "loop_done", "exit",
+                 "input_ready_first_cta", "first_chunk_first_cta", "loop_done_first_cta")
         return {"step_us": float(out[16]),
                 "advance_us": {k: float(out[i]) for i, k in enumerate(PROFILE_CLASSES) if i > 0},
-                "span_us": {k: float(out[8 + i]) for i, k in enumerate(PROFILE_CLASSES) if i > 0}}
+                "span_us": {k: float(out[8 + i]) for i, k in enumerate(PROFILE_CLASSES) if i > 0},
+                "phases_us": {k: {mk: round(float(ph[8 * i + j]), 2) for j, mk in enumerate(marks)}
+                              for i, k in enumerate(PROFILE_CLASSES) if i > 0}}
 
     def time_gate_up(self, iters: int = 5) -> float:
         """us per gate/up GEMV launch, from a graph of the step's n_layer

@@ -272,6 +272,14 @@ def test_step_timeline_adds_up():
     assert abs(sum(adv.values()) - tl["step_us"]) <= 1e-3 * tl["step_us"] + 0.01
     for k in ("qkv", "attn", "o", "gate_up", "down", "lm_head"):
         assert tl["span_us"][k] > 0, k
+        ph = tl["phases_us"][k]
+        # marks in order inside the kernel, all within its span (the
+        # earliest CTA no later than the latest one)
+        assert 0.0 < ph["input_ready"] <= ph["exit"] + 1e-3, (k, ph)
+        assert ph["first_chunk"] <= ph["exit"] + 1e-3 and ph["loop_done"] <= ph["exit"] + 1e-3, (k, ph)
+        assert ph["input_ready_first_cta"] <= ph["input_ready"] + 1e-3, (k, ph)
+        assert ph["loop_done_first_cta"] <= ph["loop_done"] + 1e-3, (k, ph)
+        assert abs(ph["exit"] - tl["span_us"][k]) <= 0.01 + 1e-3 * tl["span_us"][k], (k, ph)
     assert adv["allreduce"] == 0.0  # one GPU: no all-reduce kernels
     import b200_decode as B
 
