@@ -85,13 +85,22 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const ArArgs a
     }
     const int n4 = a.n >> 2;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
-        float4 acc = ld_sys_f4(a.part[0] + 4 * i);
-        for (int r = 1; r < a.world; ++r) {
-            const float4 v = ld_sys_f4(a.part[r] + 4 * i);
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+        // every rank's load in flight before the first add (a warp issues in
+        // order: an add between two loads would make them one NVLink round
+        // trip each), then the sum in rank order
+        float4 v[kMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+            if (r < a.world) v[r] = ld_sys_f4(a.part[r] + 4 * i);
+        float4 acc = v[0];
+#pragma unroll
+        for (int r = 1; r < kMaxRanks; ++r) {
+            if (r < a.world) {
+                acc.x = __fadd_rn(acc.x, v[r].x);
+                acc.y = __fadd_rn(acc.y, v[r].y);
+                acc.z = __fadd_rn(acc.z, v[r].z);
+                acc.w = __fadd_rn(acc.w, v[r].w);
+            }
         }
         reinterpret_cast<float4*>(a.x)[i] = acc;
     }

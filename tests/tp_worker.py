@@ -28,8 +28,10 @@ SHAPES = {
     "small": dict(n_layer=2, d_model=512, n_head=8, n_head_kv=2, head_dim=64, d_ff=1024, vocab=2048, kv_size=96),
     "llama70b": dict(n_layer=2, d_model=8192, n_head=64, n_head_kv=8, head_dim=128, d_ff=28672, vocab=128256,
                      kv_size=4224),
+    # eight KV heads: shards evenly over 2, 4 and 8 ranks
+    "small8": dict(n_layer=2, d_model=1024, n_head=16, n_head_kv=8, head_dim=64, d_ff=2048, vocab=4096, kv_size=96),
 }
-N_PREFILL = {"small": 40, "llama70b": 4096}
+N_PREFILL = {"small": 40, "llama70b": 4096, "small8": 40}
 
 
 def main():
@@ -62,7 +64,7 @@ def main():
     for l in range(L):
         mine["kv"].append((m.export_kv(l, 0, n_prefill), m.export_kv(l, 1, n_prefill)))
 
-    toks = [3, 1999] if args.shape == "small" else [128000, 9906]
+    toks = [3, 1999] if cfg.vocab < 128256 else [128000, 9906]
     parts = [p for p in M.DUMP_PARTS if not p.startswith("dots_")]
     for i, t in enumerate(toks):
         D = m.dump_step(t, n_prefill + i, parts)
@@ -95,7 +97,12 @@ def main():
         report = {"world": world, "shape": args.shape, "status": status,
                   "greedy": [g["greedy"] for g in gathered],
                   "graph_vs_dump_equal": [g["graph_vs_dump_equal"] for g in gathered]}
-        report.update(check(cfg, n_prefill, gathered, M))
+        try:
+            report.update(check(cfg, n_prefill, gathered, M))
+        except Exception:  # reported to the test, which fails with it
+            import traceback
+
+            report["error"] = traceback.format_exc()
         with open(args.out, "w") as f:
             json.dump(report, f)
     dist.barrier()
