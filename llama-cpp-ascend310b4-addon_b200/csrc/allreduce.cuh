@@ -35,15 +35,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
     return v;
 }
 
-// Relaxed system-scope 16-byte load (a peer's buffer: no stale L1 copy).
-__device__ __forceinline__ float4 ld_sys_f4(const float* p) {
-    float4 v;
-    asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(p)
-                 : "memory");
-    return v;
-}
+// 16-byte load of a peer's (or this rank's) partial, bypassing L1 (no stale
+// copy from an earlier collective); ordered after the acquire of the flags.
+// A plain cached-at-L2 load rather than a volatile one, so that the loads of
+// all ranks are in flight together.
+__device__ __forceinline__ float4 ld_sys_f4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 // Spins until *flag >= want (flags only grow).  Gives up after
 // g_wait_timeout_ns, records B200_DEVSTATUS_TIMEOUT and returns false; gives
