@@ -184,18 +184,31 @@ __device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__flo
 // before an F16 dot and q to F16 before the attention dot.
 __device__ __forceinline__ float round_f16(float f) { return __half2float(__float2half_rn(f)); }
 
-// Round half away from zero (C roundf semantics), written out: t = trunc(x)
-// and x - t is exact in fp32 for |x| < 2^23, so the tie test is exact.
+// Round half away from zero (C roundf semantics) for |x| < 2^31, in three
+// instructions: add h = 0.5 - 2^-25 (the largest float below one half) with
+// x's sign, round to nearest even, truncate.  For x >= 0 (the sign is
+// symmetric): an exact half k + 0.5 gives k + 1 - 2^-25, which rounds to
+// k + 1 (for k = 0 it is the midpoint of 1 - 2^-24 and 1 and the tie goes
+// to the even 1; above, floats are at least 2^-23 apart and k + 1 is
+// nearest); x at most one spacing below k + 0.5 gives a sum below k + 1
+// that rounds to a float below k + 1 (same binade as the sum's rounding
+// neighbours, and at k = 0 exactly 1 - 2^-24 at most); from 2^23 on, x is an
+// integer and adding less than half its spacing rounds back to x.
+// tests/test_oracle_golden.py checks the identity on every float in
+// [0.25, 256) and on samples below.
 __device__ __forceinline__ int round_half_away(float x) {
-    const float t = truncf(x);
-    const float f = __fsub_rn(x, t);
-    int r = (int)t;
-    if (f >= 0.5f) r += 1;
-    if (f <= -0.5f) r -= 1;
-    return r;
+    return __float2int_rz(__fadd_rn(x, copysignf(0.49999997f, x)));
 }
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// Low bytes of q0..q3 (each in [-127, 127]) packed into one word, q0 lowest.
+__device__ __forceinline__ int pack_q4(int q0, int q1, int q2, int q3) {
+    return (int)__byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
+}
+
+// Sum of the four signed bytes of a packed word.
+__device__ __forceinline__ int sum_q4(int w) { return __dp4a(w, 0x01010101, 0); }
 
 // R float4 units per lane, each an eighth of a 32-block: the 8 units of a
 // block sit in 8 consecutive lanes (lane & 7 = the unit's index in the
@@ -228,9 +241,8 @@ __device__ __forceinline__ void q8_units(const float4 (&v)[R], int (&word)[R], u
         const int q1 = round_half_away(__fmul_rn(v[i].y, id[i]));
         const int q2 = round_half_away(__fmul_rn(v[i].z, id[i]));
         const int q3 = round_half_away(__fmul_rn(v[i].w, id[i]));
-        qs[i] = q0 + q1 + q2 + q3;
-        word[i] = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) | ((unsigned)(q2 & 0xff) << 16) |
-                        ((unsigned)(q3 & 0xff) << 24));
+        word[i] = pack_q4(q0, q1, q2, q3);
+        qs[i] = sum_q4(word[i]);
     }
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1)
@@ -271,9 +283,8 @@ __device__ __forceinline__ void q8_halves(const float4 (&v)[R][4], int4 (&w)[R],
             const int q1 = round_half_away(__fmul_rn(v[i][j].y, id[i]));
             const int q2 = round_half_away(__fmul_rn(v[i][j].z, id[i]));
             const int q3 = round_half_away(__fmul_rn(v[i][j].w, id[i]));
-            s += (q0 + q1) + (q2 + q3);
-            wd[j] = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) | ((unsigned)(q2 & 0xff) << 16) |
-                          ((unsigned)(q3 & 0xff) << 24));
+            wd[j] = pack_q4(q0, q1, q2, q3);
+            s = __dp4a(wd[j], 0x01010101, s);
         }
         w[i] = make_int4(wd[0], wd[1], wd[2], wd[3]);
         qs[i] = s;

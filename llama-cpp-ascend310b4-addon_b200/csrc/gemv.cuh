@@ -61,9 +61,8 @@ __device__ __forceinline__ void quantize_block32(Load load, int q[8], float& d_o
         const int q1 = round_half_away(__fmul_rn(v.y, id));
         const int q2 = round_half_away(__fmul_rn(v.z, id));
         const int q3 = round_half_away(__fmul_rn(v.w, id));
-        s += q0 + q1 + q2 + q3;
-        q[e] = (int)((unsigned)(q0 & 0xff) | ((unsigned)(q1 & 0xff) << 8) | ((unsigned)(q2 & 0xff) << 16) |
-                     ((unsigned)(q3 & 0xff) << 24));
+        q[e] = pack_q4(q0, q1, q2, q3);
+        s = __dp4a(q[e], 0x01010101, s);
     }
     d_h = f2h(d);
     d_out = h2f(d_h);

@@ -200,3 +200,26 @@ def test_synthetic_normal_generator_moments():
     w = O.synth_q4_0(3, 0.02, 0, 64, 256)
     deq = O.dequantize_q4_0(w)
     assert 0.015 < deq.std() < 0.025
+
+
+def test_round_half_away_identity():
+    """The device quantisers round x / d half away from zero as
+    trunc(fl32(x + copysign(0.5 - 2^-25, x))) (common.cuh round_half_away);
+    the identity holds for every float in [0.25, 256) -- every |x / d| a
+    Q8_0 block can produce above a quarter -- and for samples below and of
+    both signs."""
+    h = np.float32(0.49999997)
+    assert h == np.nextafter(np.float32(0.5), np.float32(0.0))
+    lo, hi = np.float32(0.25).view(np.uint32), np.float32(256.0).view(np.uint32)
+    step = 1 << 23
+    for b in range(int(lo), int(hi), step):
+        x = np.arange(b, min(b + step, int(hi)), dtype=np.uint32).view(np.float32)
+        got = np.trunc(x + h)  # float32 add, round to nearest even
+        ref = np.floor(x.astype(np.float64) + 0.5)
+        assert np.array_equal(got.astype(np.float64), ref), b
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.uniform(-0.25, 0.25, 1 << 20), rng.uniform(-128, 128, 1 << 20)]).astype(np.float32)
+    x = np.concatenate([x, np.float32([0.0, -0.0, 0.5, -0.5, 0.49999997, -0.49999997, 127.5, -127.5])])
+    got = np.trunc(x + np.copysign(h, x)).astype(np.float64)
+    ref = np.sign(x.astype(np.float64)) * np.floor(np.abs(x.astype(np.float64)) + 0.5)
+    assert np.array_equal(got, ref)
