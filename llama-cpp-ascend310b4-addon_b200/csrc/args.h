@@ -182,7 +182,15 @@ struct GemvArgs {
     // {d as f32, sum of q}[U].
     const uint8_t* xq_in;         // set: the prologue copies this image instead of quantising x
     uint8_t* xq_img;              // EPI_SWIGLU (rpc == 1): also quantise the output into this image
-    unsigned int* xq_tickets;     // one counter per 32-block of the output, zero between launches
+                                  // (the 32-blocks each CTA owns whole; see xq_fix_*)
+    // With xq_in: the image's blocks that span two CTAs of its SwiGLU
+    // producer (a grid of xq_fix_grid CTAs over xq_fix_items outputs) are
+    // quantised in this prologue from the producer's f32 output xq_fix_h;
+    // CTA 0 writes them to xq_fix_out (the image) as well.
+    const float* xq_fix_h;
+    uint8_t* xq_fix_out;
+    int64_t xq_fix_items;
+    int xq_fix_grid;
     // Fused tensor-parallel all-reduce of a row-split projection's partial
     // (collective number seq = step x ar_per_step + ar_idx + 1).
     //   EPI_PUSH (producer): row n's partial (+ res[n] when res is set) goes

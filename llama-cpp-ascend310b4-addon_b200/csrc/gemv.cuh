@@ -112,12 +112,15 @@ __device__ __forceinline__ void epi_row(const GemvArgs& a, int64_t n, float v, u
     }
 }
 
+// ggml swiglu of a (gate, up) pair: silu(g) * u with silu(g) = g / (1 + exp(-g)).
+__device__ __forceinline__ float swiglu(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 // Rows n (even) and n + 1.
 __device__ __forceinline__ void epi_pair(const GemvArgs& a, int64_t n, float v0, float v1) {
     if (a.epi == EPI_SWIGLU) {
-        // ggml swiglu: silu(g) * u with silu(g) = g / (1 + exp(-g))
-        const float sg = __fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0)));
-        a.y[n / 2] = __fmul_rn(sg, v1);
+        a.y[n / 2] = swiglu(v0, v1);
     } else if (a.epi == EPI_QKV) {
         const int pos = *a.pos;
         if (n < a.nq + a.nkv) {
@@ -608,52 +611,75 @@ __device__ __forceinline__ void activation_a8(const GemvArgs& a, const GemvPlan&
 
 // UPL: units per lane of this plan's full chunks (P.full_upl), or 0 when the
 // plan has none; fixed at compile time so those chunks run fully unrolled.
-// SwiGLU outputs [j0, j1) of this CTA (already stored to a.y) into the
-// Q8_0 image a.xq_img that the down projection reads.  A 32-block may span
-// two CTAs: each CTA adds the number of the block's outputs it owns to the
-// block's ticket, and the CTA that completes the count quantises the block
-// (reading the other CTA's outputs from L2) and resets the ticket.  Blocks
-// this CTA owns whole are quantised without a ticket.  The output count is
-// a multiple of 32.  `scratch` holds at least 2 + (j1 - j0) / 32 + 2 ints.
-__device__ __forceinline__ void swiglu_quantise(const GemvArgs& a, int64_t j0, int64_t j1, int tid, float* scratch) {
-    if (j1 <= j0) return;
+// SwiGLU outputs [j0, j1) of this CTA, held in shared memory at hs[j - jb]
+// (jb = j0 rounded down to a block, so blocks start 16-byte aligned), into
+// the Q8_0 image a.xq_img that the down projection reads: the 32-blocks this
+// CTA owns whole.  A block that spans two CTAs is left to the
+// down projection's prologue, which quantises it from h (GemvArgs::xq_fix_*)
+// -- no cross-CTA fence or counter on this kernel's tail.
+__device__ __forceinline__ void swiglu_quantise(const GemvArgs& a, int64_t j0, int64_t j1, int tid, const float* hs) {
     const int64_t nout = a.n / 2;
-    int* list = reinterpret_cast<int*>(scratch);  // [0] = count, then block indices
-    const bool whole = (j0 & 31) == 0 && (j1 & 31) == 0;  // no block shared with another CTA
-    if (!whole) __threadfence();  // this CTA's outputs are visible before any ticket moves
-    __syncthreads();   // ... and the row partials (which `scratch` overlaps) are read
-    if (tid == 0) list[0] = 0;
-    __syncthreads();
-    const int64_t bf = j0 / 32, bl = (j1 - 1) / 32;
-    for (int64_t b = bf + tid; b <= bl; b += kGemvThreads) {
-        const int64_t lo = max(j0, 32 * b), hi = min(j1, 32 * b + 32);
-        const unsigned own = (unsigned)(hi - lo);
-        bool mine = own == 32u;
-        if (!mine) {
-            const unsigned old = atomicAdd(&a.xq_tickets[b], own);
-            mine = old + own == 32u;
-            if (mine) a.xq_tickets[b] = 0u;
-        }
-        if (mine) list[1 + atomicAdd(&list[0], 1)] = (int)b;
-    }
-    __syncthreads();
-    const int nb = list[0];
-    if (!whole) __threadfence();  // the other CTAs' outputs of the completed blocks
+    const int64_t b0 = (j0 + 31) / 32, b1 = j1 / 32;  // whole blocks [b0, b1)
+    const int nh = b1 > b0 ? (int)(2 * (b1 - b0)) : 0;  // half-blocks
     const int lane = tid & 31;
     // 2 lanes per block, 16 values each; whole warps run q8_halves
-    for (int g0 = (tid >> 5) * 16; g0 < nb; g0 += kGemvThreads / 2) {
-        const int gi = g0 + (lane >> 1);
-        const bool valid = gi < nb;
-        const int64_t half = 2 * (int64_t)list[1 + (valid ? gi : 0)] + (lane & 1);
-        const float4* src = reinterpret_cast<const float4*>(a.y) + 4 * half;
+    for (int g0 = (tid >> 5) * 32; g0 < nh; g0 += kGemvThreads) {
+        const int hi = g0 + lane;
+        const bool valid = hi < nh;
+        const float4* src = reinterpret_cast<const float4*>(hs + (32 * b0 - (j0 & ~31LL)) + 16 * (int64_t)(valid ? hi : 0));
         float4 v[1][4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[0][k] = __ldcg(src + k);
+        for (int k = 0; k < 4; ++k) v[0][k] = src[k];
         int4 w[1];
         uint16_t dh[1];
         int qs[1];
         q8_halves<1>(v, w, dh, qs);
-        if (valid) q8_image_store_half(a.xq_img, nout / 32, half, w[0], dh[0], qs[0]);
+        if (valid) q8_image_store_half(a.xq_img, nout / 32, 2 * b0 + hi, w[0], dh[0], qs[0]);
+    }
+}
+
+// The blocks of an image that span two CTAs of its producer (the SwiGLU
+// epilogue above leaves them), quantised here from the producer's f32
+// output a.xq_fix_h into this CTA's shared-memory image: the producer's CTA
+// c (1 <= c < xq_fix_grid) starts at output c * xq_fix_items / xq_fix_grid;
+// a start inside a block marks that block, two half-blocks (lanes) each.
+// Thread t takes half-block t (2 (grid - 1) <= 2 * 255 < kGemvThreads, so
+// one round); fix_load issues its loads (with the image copy's), fix_store
+// quantises whole warps and replaces the block in the copied image; CTA 0
+// also writes it to the global image (a.xq_fix_out), so the image in HBM is
+// complete after this kernel.
+struct ImageFix {
+    float4 v[1][4];
+    int64_t half;
+    bool valid, run;  // run: this warp takes part (q8_halves needs whole warps)
+};
+
+__device__ __forceinline__ ImageFix fix_load(const GemvArgs& a, int tid) {
+    ImageFix f;
+    const int nfix = 2 * (a.xq_fix_grid - 1);
+    f.run = (tid & ~31) < nfix;
+    const int hi = tid < nfix ? tid : 0;
+    const int c = 1 + hi / 2;
+    const int64_t jc = (int64_t)c * a.xq_fix_items / a.xq_fix_grid;
+    f.valid = tid < nfix && (jc & 31) != 0;
+    f.half = 2 * (jc / 32) + (hi & 1);
+    if (f.run) {
+        const float4* src = reinterpret_cast<const float4*>(a.xq_fix_h) + 4 * f.half;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) f.v[0][k] = src[k];
+    }
+    return f;
+}
+
+__device__ __forceinline__ void fix_store(const GemvArgs& a, const GemvPlan& P, uint8_t* xr, const ImageFix& f) {
+    if (!f.run) return;  // uniform over the warp
+    int4 w[1];
+    uint16_t dh[1];
+    int qs[1];
+    q8_halves<1>(f.v, w, dh, qs);
+    if (f.valid) {
+        q8_image_store_half(xr, P.U, f.half, w[0], dh[0], qs[0]);
+        if (blockIdx.x == 0 && a.xq_fix_out != nullptr) q8_image_store_half(a.xq_fix_out, P.U, f.half, w[0], dh[0], qs[0]);
     }
 }
 
@@ -811,6 +837,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             const int64_t n16 = 40 * (int64_t)P.U / 16;
             const int4* src = reinterpret_cast<const int4*>(a.xq_in);
             int4* dst = reinterpret_cast<int4*>(xr);
+            const bool fix = a.xq_fix_h != nullptr;
+            ImageFix fx;
+            if (fix) fx = fix_load(a, tid);
             constexpr int RC = 8;
             int4 t[RC];
             for (int64_t base = 0; base < n16; base += RC * kGemvThreads) {
@@ -824,6 +853,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             }
             if (tid == 0 && (P.U & 1))  // 40 U is a multiple of 8 only: the last 8 bytes
                 reinterpret_cast<int2*>(xr)[5 * (int64_t)P.U - 1] = reinterpret_cast<const int2*>(a.xq_in)[5 * (int64_t)P.U - 1];
+            if (fix) {
+                __syncthreads();  // the copied image, before its boundary blocks are replaced
+                fix_store(a, P, xr, fx);
+            }
         } else {
             activation_q8<AR>(a, P, xr, red, tid, lane, warp, wpre, [&] {
                 if (lane == 0) issue_rest();
@@ -953,10 +986,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         if constexpr (FMT == FMT_A8) {
             for (int64_t r = tid; r < nrows; r += kGemvThreads)
                 a.y[cr0 + r] = a8w8_dequant(pacc0[r] + pacc1[r], a8_xs, a8_ws[cr0 + r]);
+        } else if (a.epi == EPI_SWIGLU && a.xq_img != nullptr) {
+            // the outputs also go to shared memory (the rings: every copy has
+            // landed and been read) for the image of the down projection
+            float* hs = reinterpret_cast<float*>(rings);
+            const int64_t jb = (cr0 / 2) & ~31LL;
+            for (int64_t r = 2 * (int64_t)tid; r < nrows; r += 2 * kGemvThreads) {
+                const float v = swiglu(part0[r] + part1[r], part0[r + 1] + part1[r + 1]);
+                a.y[(cr0 + r) / 2] = v;
+                hs[(cr0 + r) / 2 - jb] = v;
+            }
+            __syncthreads();
+            swiglu_quantise(a, cr0 / 2, cr1 / 2, tid, hs);
         } else if (pair) {
             for (int64_t r = 2 * (int64_t)tid; r < nrows; r += 2 * kGemvThreads)
                 epi_pair(a, cr0 + r, part0[r] + part1[r], part0[r + 1] + part1[r + 1]);
-            if (a.epi == EPI_SWIGLU && a.xq_img != nullptr) swiglu_quantise(a, cr0 / 2, cr1 / 2, tid, red);
         } else {
             for (int64_t r = tid; r < nrows; r += kGemvThreads) epi_row<AR>(a, cr0 + r, part0[r] + part1[r], best);
         }

@@ -130,7 +130,7 @@ struct b200_model {
     int l2_ef = 1;
     uint8_t* img_h = nullptr;
     uint8_t* img_att = nullptr;
-    unsigned int* img_tickets = nullptr;
+    int gu_grid = 0;  // CTAs of the gate/up GEMV (the down projection's image fix-up)
     // Tensor parallel: the O / down partials go to an IPC-shared region
     // (two partial buffers, then the per-rank flags) summed by the
     // peer-memory all-reduce; B200_TP_ALLREDUCE=nccl selects ncclAllReduce.
@@ -409,7 +409,13 @@ GemvArgs proj_args(b200_model* m, int l, int which) {
     a.k = which == 0 ? (int64_t)m->hq * c.head_dim : m->ff;
     a.x = which == 0 ? m->att : m->h;
     if (which == 0 && fused_o(m)) a.xq_in = m->img_att;
-    if (which == 1 && fused_down(m)) a.xq_in = m->img_h;
+    if (which == 1 && fused_down(m)) {
+        a.xq_in = m->img_h;
+        a.xq_fix_h = m->h;
+        a.xq_fix_out = m->img_h;
+        a.xq_fix_items = m->ff;
+        a.xq_fix_grid = m->gu_grid;
+    }
     a.pro = PRO_PLAIN;
     a.res = m->x;
     if (m->world == 1) {
@@ -439,10 +445,7 @@ GemvArgs gate_up_args(const b200_model* m, int l) {
     a.pro = PRO_RMSNORM;
     a.epi = EPI_SWIGLU;
     a.y = m->h;
-    if (fused_down(m)) {
-        a.xq_img = m->img_h;
-        a.xq_tickets = m->img_tickets;
-    }
+    if (fused_down(m)) a.xq_img = m->img_h;
     if (m->ar_now) set_ar_consumer(m, a, 2 * l, 0, m->ar_grid_o);
     return a;
 }
@@ -563,13 +566,16 @@ int enqueue_step(b200_model* m, cudaStream_t s, Prof* prof, const Dump* dump = n
             GemvArgs a = proj_args(m, l, 1);
             l2(a);
             bool dbg = false;
+            uint8_t* xq = nullptr;
             if (dump) {
-                uint8_t* xq = dump->xq_down ? dump->xq_down + (size_t)l * (m->ff / 32) * 34 : nullptr;
-                if (xq && a.xq_in) CR(image_out(a.xq_in, xq, m->ff));
+                xq = dump->xq_down ? dump->xq_down + (size_t)l * (m->ff / 32) * 34 : nullptr;
                 dbg = hook(a, xq, dump->dots_down ? dump->dots_down + (size_t)l * d * (m->ff / 32) : nullptr);
             }
             if (stamps) stamps->assign(a, 5);
             CR(b200i_gemv(FMT_Q4, a, dbg, s, pdl));
+            // the image is complete once this GEMV has quantised the blocks
+            // its producer's CTAs share (written back by its CTA 0)
+            if (xq && a.xq_in) CR(image_out(a.xq_in, xq, m->ff));
         }
         CR(E());
         if (m->world > 1 && !m->ar_now) {
@@ -748,11 +754,10 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
         (rc = dalloc(m, &m->fa_ws, m->fa_ws_bytes)) || (rc = dalloc_t(m, &m->staging, m->staging_bytes)))
         return fail(rc);
     if ((rc = dalloc_t(m, &m->img_h, (size_t)(40 * (m->ff / 32)))) ||
-        (rc = dalloc_t(m, &m->img_att, (size_t)(40 * ((int64_t)m->hq * D / 32)))) ||
-        (rc = dalloc_t(m, &m->img_tickets, (size_t)(m->ff / 32) * sizeof(unsigned int))))
+        (rc = dalloc_t(m, &m->img_att, (size_t)(40 * ((int64_t)m->hq * D / 32)))))
         return fail(rc);
-    if (cudaMemset(m->img_tickets, 0, (size_t)(m->ff / 32) * sizeof(unsigned int)) != cudaSuccess)
-        return fail(B200_ECUDA);
+    m->gu_grid = b200i_gemv_grid(FMT_Q4, 2 * (int64_t)m->ff, c.d_model, EPI_SWIGLU);
+    if (m->gu_grid <= 0 || 2 * (m->gu_grid - 1) > kGemvThreads) return fail(B200_EUNSUPPORTED);  // one fix-up round
     if (cudaMemset(m->fa_ws, 0, m->fa_ws_bytes) != cudaSuccess) return fail(B200_ECUDA);
     if (cudaMallocHost(reinterpret_cast<void**>(&m->h_st), sizeof(StepState)) != cudaSuccess) return fail(B200_ENOMEM);
     if (cudaMallocHost(reinterpret_cast<void**>(&m->h_next), sizeof(int)) != cudaSuccess) return fail(B200_ENOMEM);
