@@ -72,8 +72,11 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(const ArArgs a
         __threadfence_system();
         st_release_sys_u64(a.peer_flag[threadIdx.x], seq);
     }
+    // thread r of each CTA waits for rank r's announcement (the ranks in
+    // parallel, one poller per flag and CTA), then the CTA meets
     bool ok = true;
-    for (int r = 0; r < a.world; ++r) ok = ok && wait_flag_geq(&a.flags[r], seq);
+    if (threadIdx.x < a.world) ok = wait_flag_geq(&a.flags[threadIdx.x], seq);
+    ok = __syncthreads_and(ok) != 0;
     if (threadIdx.x == 0) stamp_point(a.stamp, a.stamp_stride, 3);  // every rank's partial is announced
     if (!ok) {
         if (threadIdx.x == 0) stamp_point(a.stamp, a.stamp_stride, 2);
