@@ -218,7 +218,25 @@ struct GemvArgs {
     // The weight stream is read with the evict_first L2 policy when set
     // (weights are read once per step).
     int l2_ef;
+    // Uneven rows (rpc == 1): the last late_ctas CTAs of the grid get
+    // late_pct % of an even share, the others the rest.  For a GEMV that
+    // follows a kernel holding late_ctas SMs: under programmatic launch the
+    // low-numbered CTAs become resident on the free SMs first and start
+    // streaming as soon as the wait ends, the last ones only once the
+    // previous kernel's CTAs have left their SMs (gemv_cta_start).
+    int late_ctas;
+    int late_pct;
 };
+
+// First item of CTA c of `grid` over `items` (see GemvArgs::late_ctas);
+// an even split when late is 0 or not below grid.
+B200_HD inline int64_t gemv_cta_start(int64_t c, int64_t grid, int64_t items, int64_t late, int64_t pct) {
+    if (late <= 0 || late >= grid || pct <= 0 || pct >= 100) return c * items / grid;
+    const int64_t early = grid - late;
+    const int64_t total = 100 * early + pct * late;
+    const int64_t w = c <= early ? 100 * c : 100 * early + pct * (c - early);
+    return w * items / total;
+}
 
 constexpr int kFaThreads = 128;
 constexpr int kFaChunk = 64;    // positions per inner step

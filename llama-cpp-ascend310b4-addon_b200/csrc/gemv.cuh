@@ -720,8 +720,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     } else {
         const int64_t item_rows = pair ? 2 : 1;
         const int64_t items = (P.n + item_rows - 1) / item_rows;
-        cr0 = (int64_t)blockIdx.x * items / gridDim.x * item_rows;
-        cr1 = min((int64_t)(blockIdx.x + 1) * items / gridDim.x * item_rows, P.n);
+        cr0 = gemv_cta_start(blockIdx.x, gridDim.x, items, a.late_ctas, a.late_pct) * item_rows;
+        cr1 = min(gemv_cta_start(blockIdx.x + 1, gridDim.x, items, a.late_ctas, a.late_pct) * item_rows, P.n);
         const int64_t R = cr1 - cr0;
         int64_t q_end;
         if (R >= kGemvWarps) {

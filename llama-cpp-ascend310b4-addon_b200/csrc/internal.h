@@ -12,6 +12,8 @@
 // stream; the kernels wait for that kernel before touching its outputs.
 int b200i_gemv(int fmt, b200::GemvArgs a, bool debug, cudaStream_t st, bool pdl = false);
 int b200i_fa(const b200::FaArgs& a, int head_dim, cudaStream_t st, bool pdl = false);
+// CTAs of the tensor-core attention launch for a (one per SM); 0 for head dim 256.
+int b200i_fa_ctas(const b200::FaArgs& a, int head_dim);
 // Tensor-parallel all-reduce of a.n floats over peer memory (allreduce.cuh).
 int b200i_tp_allreduce(const b200::ArArgs& a, cudaStream_t st, bool pdl);
 int b200i_sm_count();

@@ -152,7 +152,14 @@ int launch_gemv_u(GemvArgs a, const GemvPlan& p, cudaStream_t st, bool pdl) {
     const int64_t grid64 = p.rpc > 1 ? std::min<int64_t>(sm_count(dev), (items + kGemvWarps - 1) / kGemvWarps)
                                      : std::min<int64_t>(sm_count(dev), items);
     const int grid = (int)std::max<int64_t>(1, grid64);
-    const int64_t rows_per_cta = ((items + grid - 1) / grid) * item_rows;
+    int64_t rows_per_cta = ((items + grid - 1) / grid) * item_rows;
+    if (p.rpc == 1 && a.late_ctas > 0) {  // uneven shares: the largest
+        rows_per_cta = 0;
+        for (int c = 0; c < grid; ++c)
+            rows_per_cta = std::max(rows_per_cta, (gemv_cta_start(c + 1, grid, items, a.late_ctas, a.late_pct) -
+                                                   gemv_cta_start(c, grid, items, a.late_ctas, a.late_pct)) *
+                                                      item_rows);
+    }
     int S = kGemvStagesMax;
     const int cap = stage_cap();
     if (cap > 0) S = std::min(S, cap);
@@ -470,6 +477,19 @@ int b200i_fa(const FaArgs& in, int D, cudaStream_t st, bool pdl) {
         }
         default: return B200_EUNSUPPORTED;
     }
+}
+
+// CTAs (one per SM) of the tensor-core attention launch for these arguments
+// (head dim 64 / 128; the same choice as launch_fa_mma); 0 for head dim 256,
+// whose kernel shares SMs.
+int b200i_fa_ctas(const FaArgs& a, int D) {
+    if (D != 64 && D != 128) return 0;
+    if (set_fa_attrs() != B200_OK) return 0;
+    const int dev = current_device();
+    const int nchunks = (a.n_kv + kFaChunk - 1) / kFaChunk;
+    const int S = D == 64 ? fa_pick_cluster<64>(dev, a.Hkv * a.gchunks, nchunks)
+                          : fa_pick_cluster<128>(dev, a.Hkv * a.gchunks, nchunks);
+    return S * a.Hkv * a.gchunks;
 }
 
 int b200i_tp_allreduce(const ArArgs& a, cudaStream_t st, bool pdl) {

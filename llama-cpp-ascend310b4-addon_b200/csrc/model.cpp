@@ -131,6 +131,11 @@ struct b200_model {
     uint8_t* img_h = nullptr;
     uint8_t* img_att = nullptr;
     int gu_grid = 0;  // CTAs of the gate/up GEMV (the down projection's image fix-up)
+    // The O GEMV follows attention, whose fa_ctas CTAs hold as many SMs: its
+    // last fa_ctas CTAs start late and get o_late_pct % of an even row share
+    // (GemvArgs::late_ctas; B200_O_SKEW, 100 = even).
+    int fa_ctas = 0;
+    int o_late_pct = 65;
     // Tensor parallel: the O / down partials go to an IPC-shared region
     // (two partial buffers, then the per-rank flags) summed by the
     // peer-memory all-reduce; B200_TP_ALLREDUCE=nccl selects ncclAllReduce.
@@ -409,6 +414,10 @@ GemvArgs proj_args(b200_model* m, int l, int which) {
     a.k = which == 0 ? (int64_t)m->hq * c.head_dim : m->ff;
     a.x = which == 0 ? m->att : m->h;
     if (which == 0 && fused_o(m)) a.xq_in = m->img_att;
+    if (which == 0) {
+        a.late_ctas = m->fa_ctas;
+        a.late_pct = m->o_late_pct;
+    }
     if (which == 1 && fused_down(m)) {
         a.xq_in = m->img_h;
         a.xq_fix_h = m->h;
@@ -756,6 +765,8 @@ int b200_model_create(const b200_llama_config* cfg, int device, int tp_rank, int
     if ((rc = dalloc_t(m, &m->img_h, (size_t)(40 * (m->ff / 32)))) ||
         (rc = dalloc_t(m, &m->img_att, (size_t)(40 * ((int64_t)m->hq * D / 32)))))
         return fail(rc);
+    m->fa_ctas = b200i_fa_ctas(fa_args(m, 0), D);
+    if (const char* e = getenv("B200_O_SKEW")) m->o_late_pct = std::max(1, std::min(100, atoi(e)));
     m->gu_grid = b200i_gemv_grid(FMT_Q4, 2 * (int64_t)m->ff, c.d_model, EPI_SWIGLU);
     if (m->gu_grid <= 0 || 2 * (m->gu_grid - 1) > kGemvThreads) return fail(B200_EUNSUPPORTED);  // one fix-up round
     if (cudaMemset(m->fa_ws, 0, m->fa_ws_bytes) != cudaSuccess) return fail(B200_ECUDA);
