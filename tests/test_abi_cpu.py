@@ -147,3 +147,58 @@ def test_a8w8_weight_policy_malformed_list(bad):
 
     with pytest.raises(B.B200Error):
         B.a8w8_selects_weight("blk.5.ffn_up.weight", 1, (1536, 8960, 1, 1), bad)
+
+
+def test_gemv_uneven_cta_shares(tmp_path):
+    """gemv_cta_start (csrc/args.h), the row split of a GEMV whose last CTAs
+    start late: compiled on the host and checked to cover [0, items) in
+    order with every CTA's share, the late CTAs' share near pct % of the
+    others', and the even split whenever the skew is off."""
+    import shutil
+    import subprocess
+
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.skip("no g++")
+    src = tmp_path / "split.cpp"
+    src.write_text(r'''
+#include <cstdio>
+#include "args.h"
+using b200::gemv_cta_start;
+int main() {
+    const long cases[][4] = {{148, 8192, 64, 65}, {148, 8192, 64, 100}, {148, 28672, 16, 50}, {148, 4096, 0, 65},
+                             {132, 5120, 131, 65}, {148, 200, 64, 30}};
+    for (auto& c : cases) {
+        const long grid = c[0], items = c[1], late = c[2], pct = c[3];
+        long prev = gemv_cta_start(0, grid, items, late, pct);
+        if (prev != 0) return 1;
+        long early_max = 0, late_min = items;
+        for (long i = 0; i < grid; ++i) {
+            const long a = gemv_cta_start(i, grid, items, late, pct), b = gemv_cta_start(i + 1, grid, items, late, pct);
+            if (b < a) return 2;
+            if (late == 0 || pct >= 100) {
+                if (a != i * items / grid) return 3;
+            }
+            if (i < grid - late) early_max = b - a > early_max ? b - a : early_max;
+            else late_min = b - a < late_min ? b - a : late_min;
+        }
+        if (gemv_cta_start(grid, grid, items, late, pct) != items) return 4;
+        printf("%ld %ld %ld %ld %ld %ld\n", grid, items, late, pct, early_max, late_min);
+    }
+    return 0;
+}
+''')
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = tmp_path / "split"
+    inc = [f"-I{os.path.join(root, 'llama-cpp-ascend310b4-addon_b200', 'csrc')}", "-I/usr/local/cuda/include"]
+    r = subprocess.run([gxx, "-std=c++17", "-O1", *inc, str(src), "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, (r.returncode, r.stdout)
+    for ln in r.stdout.split("\n"):
+        if not ln:
+            continue
+        grid, items, late, pct, early_max, late_min = map(int, ln.split())
+        if 0 < late < grid and pct < 100 and items >= 4 * grid:
+            # the late CTAs' share is pct % of the early ones' (to a row)
+            assert abs(late_min - early_max * pct / 100) <= 2, ln
